@@ -1,0 +1,63 @@
+"""The compiler's entry points: ``compile_module`` (reference ``ptxgen/compiler.py:82-93``) and
+``to_ptx`` (reference ``compile.py:24-55``), with the same arguments and error behaviour.
+
+A kernel first meets the template matchers (``templates``): a matmul-shaped nest over bf16/f16
+operands becomes the TMA + tcgen05 kernel. Everything else, and everything with a flag that asks
+for the plain lowering, goes through the generic lowering (``lower``).
+"""
+
+from __future__ import annotations
+
+from collections.abc import Mapping, Sequence
+from typing import Any
+
+from .ir import Graph, KernelOp
+from .lower import Buffer, Lowering
+
+__all__ = ["Buffer", "compile_module", "to_ptx", "kernel_for_meta"]
+
+
+def compile_module(op: KernelOp, buffers: Mapping[str, Buffer], arg_order: Sequence[str],
+                   block_threads: int, *, no_unroll: bool = False, no_fusion: bool = False,
+                   no_cse: bool = False, smem_bytes: int = 0, templates: bool = True) -> str:
+    """The sm_100a PTX module for ``op``, launched with ``block_threads`` threads per block and
+    ``smem_bytes`` of dynamic shared memory (meta.json's figure; templates size their pipelines
+    to it)."""
+    if templates:
+        from . import templates as tpl
+
+        ptx = tpl.try_templates(op, buffers, arg_order, block_threads, smem_bytes)
+        if ptx is not None:
+            return ptx
+    k = Lowering(op, buffers, arg_order, block_threads, no_unroll=no_unroll,
+                 no_fusion=no_fusion, no_cse=no_cse).run()
+    return k.render()
+
+
+def kernel_for_meta(graph: Graph, meta: dict[str, Any]) -> tuple[KernelOp, dict[str, Any]]:
+    """The KernelOp whose name a meta.json kernel names, and that launch entry."""
+    launches = {k["entry"]: k for k in meta["kernels"]}
+    ops = graph.kernel_ops()
+    op = next((o for o in ops if o.name in launches), None)
+    if op is None:
+        raise ValueError(f"no KernelOp named like a meta.json kernel ({', '.join(launches)})")
+    return op, launches[op.name]
+
+
+def to_ptx(graph: Graph, meta: dict[str, Any], no_unroll: bool = False, no_fusion: bool = False,
+           no_cse: bool = False) -> str:
+    """The PTX module for the kernel meta.json names (same contract as the reference)."""
+    op, launch = kernel_for_meta(graph, meta)
+    if list(launch["block"][1:]) != [1, 1] or list(launch["grid"][1:]) != [1, 1]:
+        raise NotImplementedError("only 1-D launches")
+    if any(a.get("scalar") for a in launch["args"]):
+        raise NotImplementedError("by-value scalar arguments")
+    buffers = {
+        a["name"]: Buffer(tuple(a["shape"]), a["dtype"],
+                          bool(a.get("output")) or a["name"] in op.outputs)
+        for a in launch["args"]
+    }
+    return compile_module(op, buffers, launch["arg_order"], launch["block"][0],
+                          no_unroll=no_unroll, no_fusion=no_fusion, no_cse=no_cse,
+                          smem_bytes=int(launch.get("smem_bytes", 0)),
+                          templates=not (no_unroll or no_fusion or no_cse))

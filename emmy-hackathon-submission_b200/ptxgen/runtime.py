@@ -1,0 +1,296 @@
+"""Running emitted PTX on a GPU through the C-ABI launcher (``include/ptxgen_b200.h``).
+
+``Module`` loads a PTX module, ``Module.kernel`` finds an entry, and ``Kernel.launch`` starts it
+on device pointers. ``Problem`` is one meta.json kernel end to end: compile the IR, allocate the
+buffers (PyTorch is used for device memory only), fill its inputs, zero ``zero_outputs``, launch
+with meta.json's geometry, and read the status word.
+
+The emitted module states the launch it was compiled for in ``// @ptxgen`` header lines
+(``launch grid=G block=B``, ``dynamic_smem=N``, ``tensormap ...``); a launch that disagrees is
+refused here, because the kernel's index arithmetic relies on it (a tail guard proven
+unnecessary for G blocks is not there for more).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import json
+import re
+import threading
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import Any
+
+import numpy as np
+
+from .build import LIB
+
+_NOTE = re.compile(r"^// @ptxgen (\w+) (.*)$", re.M)
+_DTYPE_CODE = {"u8": 0, "f16": 1, "bf16": 2, "f32": 3}
+
+
+class LaunchError(RuntimeError):
+    """A launcher call failed; the message carries the driver's error and any JIT log."""
+
+
+class KernelStatusError(LaunchError):
+    """A kernel reported a failure through its status word (a bounded wait gave up)."""
+
+
+_lib: ctypes.CDLL | None = None
+_lock = threading.Lock()
+_initialised: set[int] = set()
+
+
+def library() -> ctypes.CDLL:
+    """The loaded launcher library (it must have been built: ``ptxgen.build``)."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not LIB.exists():
+                raise LaunchError(f"launcher library {LIB} is not built (run ptxgen.build)")
+            lib = ctypes.CDLL(str(LIB))
+            u64, i32, u32, vp, cp = (ctypes.c_uint64, ctypes.c_int, ctypes.c_uint32,
+                                     ctypes.c_void_p, ctypes.c_char_p)
+            pu64, pu32, psz = (ctypes.POINTER(u64), ctypes.POINTER(u32),
+                               ctypes.POINTER(ctypes.c_size_t))
+            sig = {
+                "pg_init": [i32],
+                "pg_last_error": [],
+                "pg_module_load": [cp, ctypes.POINTER(vp)],
+                "pg_module_unload": [vp],
+                "pg_kernel_get": [vp, cp, ctypes.POINTER(vp)],
+                "pg_kernel_launch": [vp, u32, u32, u32, u64, pu64, i32],
+                "pg_tensormap_fill": [vp, cp, i32, i32, u64, pu64, pu64, pu32, i32],
+                "pg_status_take": [vp, pu32],
+                "pg_memset_async": [u64, ctypes.c_size_t, u64],
+                "pg_memcpy_htod_async": [u64, vp, ctypes.c_size_t, u64],
+                "pg_memcpy_dtoh_async": [vp, u64, ctypes.c_size_t, u64],
+                "pg_stream_synchronize": [u64],
+                "pg_run_host": [vp, u32, u32, u32, u64, i32, pu64, ctypes.POINTER(vp), psz,
+                                pu32],
+            }
+            for name, args in sig.items():
+                fn = getattr(lib, name)
+                fn.argtypes = args
+                fn.restype = ctypes.c_char_p if name == "pg_last_error" else ctypes.c_int
+            _lib = lib
+        return _lib
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = library().pg_last_error().decode(errors="replace")
+        cls = KernelStatusError if rc == -4 else LaunchError
+        raise cls(f"{what} failed ({rc}): {msg}")
+
+
+def init(device: int = 0) -> None:
+    """Make ``device``'s primary context current for the launcher (idempotent per device)."""
+    lib = library()
+    _check(lib.pg_init(device), f"pg_init({device})")
+    _initialised.add(device)
+
+
+def header_notes(ptx: str) -> dict[str, list[str]]:
+    notes: dict[str, list[str]] = {}
+    for key, rest in _NOTE.findall(ptx):
+        notes.setdefault(key, []).append(rest.strip())
+    return notes
+
+
+def _kv(text: str) -> dict[str, str]:
+    return dict(part.split("=", 1) for part in text.split() if "=" in part)
+
+
+@dataclass
+class TensorMapNote:
+    """A ``// @ptxgen tensormap`` line: which .global symbol holds a map over which buffer."""
+
+    symbol: str
+    buffer: str
+    dtype: str
+    dims: tuple[int, ...]
+    strides: tuple[int, ...]
+    box: tuple[int, ...]
+    swizzle: int
+
+    @classmethod
+    def parse(cls, text: str) -> TensorMapNote:
+        kv = _kv(text)
+        ints = lambda s: tuple(int(x) for x in s.split(",") if x)  # noqa: E731
+        return cls(kv["symbol"], kv["buffer"], kv["dtype"], ints(kv["dims"]),
+                   ints(kv.get("strides", "")), ints(kv["box"]), int(kv.get("swizzle", "0")))
+
+
+class Module:
+    def __init__(self, ptx: str, device: int = 0):
+        if device not in _initialised:
+            init(device)
+        self.ptx = ptx
+        self.notes = header_notes(ptx)
+        handle = ctypes.c_void_p()
+        _check(library().pg_module_load(ptx.encode(), ctypes.byref(handle)), "pg_module_load")
+        self.handle = handle
+        self.tensormaps = [TensorMapNote.parse(t) for t in self.notes.get("tensormap", [])]
+        launch = _kv(self.notes["launch"][0]) if "launch" in self.notes else {}
+        self.grid = int(launch["grid"]) if "grid" in launch else None
+        self.block = int(launch["block"]) if "block" in launch else None
+        dyn = self.notes.get("dynamic_smem")
+        self.dynamic_smem = int(dyn[0]) if dyn else 0
+
+    def kernel(self, entry: str) -> Kernel:
+        handle = ctypes.c_void_p()
+        _check(library().pg_kernel_get(self.handle, entry.encode(), ctypes.byref(handle)),
+               f"pg_kernel_get({entry})")
+        return Kernel(self, handle, entry)
+
+    def fill_tensormaps(self, pointers: dict[str, int]) -> None:
+        """Write every tensor map the module names, over the buffers at ``pointers``."""
+        lib = library()
+        for t in self.tensormaps:
+            rank = len(t.dims)
+            dims = (ctypes.c_uint64 * rank)(*t.dims)
+            strides = (ctypes.c_uint64 * max(1, rank - 1))(*(t.strides or (0,)))
+            box = (ctypes.c_uint32 * rank)(*t.box)
+            _check(lib.pg_tensormap_fill(self.handle, t.symbol.encode(), _DTYPE_CODE[t.dtype],
+                                         rank, pointers[t.buffer], dims, strides, box,
+                                         t.swizzle), f"pg_tensormap_fill({t.symbol})")
+
+    def status(self) -> int:
+        out = ctypes.c_uint32()
+        _check(library().pg_status_take(self.handle, ctypes.byref(out)), "pg_status_take")
+        return out.value
+
+    def __del__(self) -> None:
+        h = getattr(self, "handle", None)
+        if h is not None and _lib is not None:
+            try:
+                _lib.pg_module_unload(h)
+            except Exception:  # noqa: BLE001 - interpreter shutdown
+                pass
+
+
+@dataclass
+class Kernel:
+    module: Module
+    handle: ctypes.c_void_p
+    entry: str
+
+    def launch(self, grid: int, block: int, smem: int, pointers: list[int],
+               stream: int = 0) -> None:
+        m = self.module
+        if m.grid is not None and (grid, block) != (m.grid, m.block):
+            raise LaunchError(f"{self.entry}: compiled for grid {m.grid} x block {m.block}, "
+                              f"asked to launch {grid} x {block}")
+        smem = max(smem, m.dynamic_smem)
+        ptrs = (ctypes.c_uint64 * len(pointers))(*pointers)
+        _check(library().pg_kernel_launch(self.handle, grid, block, smem, stream, ptrs,
+                                          len(pointers)), f"pg_kernel_launch({self.entry})")
+
+    def run_host(self, grid: int, block: int, smem: int, stream: int, dev: list[int],
+                 host: list[int | None], nbytes: list[int], flags: list[int]) -> None:
+        """The one-call host-buffer path (``pg_run_host``)."""
+        n = len(dev)
+        _check(library().pg_run_host(
+            self.handle, grid, block, max(smem, self.module.dynamic_smem), stream, n,
+            (ctypes.c_uint64 * n)(*dev), (ctypes.c_void_p * n)(*host),
+            (ctypes.c_size_t * n)(*nbytes), (ctypes.c_uint32 * n)(*flags)),
+            f"pg_run_host({self.entry})")
+
+
+# --- problems: one meta.json kernel, end to end ----------------------------------------------
+
+_TORCH_DTYPE = {"f32": "float32", "f64": "float64", "f16": "float16", "bf16": "bfloat16",
+                "i32": "int32", "i64": "int64", "u8": "uint8", "i16": "int16", "bool": "bool",
+                "u32": "int32", "u64": "int64", "u16": "int16"}
+
+
+def torch_dtype(dtype: str) -> Any:
+    import torch
+
+    return getattr(torch, _TORCH_DTYPE[dtype])
+
+
+@dataclass
+class Problem:
+    """A compiled meta.json kernel: its IR, launch entry and module."""
+
+    graph_json: dict[str, Any]
+    meta: dict[str, Any]
+    ptx: str = ""
+    flags: dict[str, bool] = field(default_factory=dict)
+    device: int = 0
+    _module: Module | None = None
+    _kernel: Kernel | None = None
+
+    @classmethod
+    def from_dir(cls, path: str | Path, **flags: bool) -> Problem:
+        path = Path(path)
+        ir = next(path.glob("*.ir.json"))
+        return cls(json.loads(ir.read_text()), json.loads((path / "meta.json").read_text()),
+                   flags=flags)
+
+    @property
+    def launch_entry(self) -> dict[str, Any]:
+        from .compiler import kernel_for_meta
+        from .ir import Graph
+
+        return kernel_for_meta(Graph.from_dict(self.graph_json), self.meta)[1]
+
+    def compile(self) -> str:
+        from .compiler import to_ptx
+        from .ir import Graph
+
+        if not self.ptx:
+            self.ptx = to_ptx(Graph.from_dict(self.graph_json), self.meta,
+                              self.flags.get("no_unroll", False),
+                              self.flags.get("no_fusion", False),
+                              self.flags.get("no_cse", False))
+        return self.ptx
+
+    def load(self) -> Kernel:
+        if self._kernel is None:
+            self._module = Module(self.compile(), self.device)
+            self._kernel = self._module.kernel(self.launch_entry["entry"])
+        return self._kernel
+
+    @property
+    def module(self) -> Module:
+        self.load()
+        assert self._module is not None
+        return self._module
+
+    def allocate(self, extra_guard: int = 0) -> dict[str, Any]:
+        """Device tensors for every argument (uninitialised)."""
+        import torch
+
+        out = {}
+        for a in self.launch_entry["args"]:
+            n = int(np.prod(a["shape"]))
+            out[a["name"]] = torch.empty(n + extra_guard, dtype=torch_dtype(a["dtype"]),
+                                         device=f"cuda:{self.device}")
+        return out
+
+    def launch(self, tensors: dict[str, Any], stream: int | None = None, zero: bool = True,
+               check_status: bool = False) -> None:
+        import torch
+
+        launch = self.launch_entry
+        kernel = self.load()
+        if stream is None:
+            stream = torch.cuda.current_stream(self.device).cuda_stream
+        ptrs = {name: t.data_ptr() for name, t in tensors.items()}
+        self.module.fill_tensormaps(ptrs)
+        if zero:
+            for name in launch.get("zero_outputs", []):
+                t = tensors[name]
+                _check(library().pg_memset_async(t.data_ptr(), t.numel() * t.element_size(),
+                                                 stream), "pg_memset_async")
+        kernel.launch(launch["grid"][0], launch["block"][0], int(launch.get("smem_bytes", 0)),
+                      [ptrs[n] for n in launch["arg_order"]], stream)
+        if check_status:
+            torch.cuda.synchronize(self.device)
+            status = self.module.status()
+            if status:
+                raise KernelStatusError(f"{launch['entry']}: status word 0x{status:08x}")

@@ -1,0 +1,115 @@
+"""Shared test set-up: import paths, the ``gpu`` marker, and helpers that run a meta.json kernel
+through the C-ABI launcher on a GPU and through the NumPy oracle on the CPU."""
+
+from __future__ import annotations
+
+import json
+import sys
+from pathlib import Path
+from typing import Any
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+PKG = ROOT / "emmy-hackathon-submission_b200"
+GOLDEN = Path(__file__).resolve().parent / "golden"
+for p in (str(ROOT), str(PKG)):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+
+def pytest_configure(config: pytest.Config) -> None:
+    config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200, sm_100a)")
+
+
+SHIPPED = sorted(p.name for p in (GOLDEN / "shipped").iterdir() if p.is_dir())
+
+
+def shipped(name: str) -> tuple[dict[str, Any], dict[str, Any]]:
+    d = GOLDEN / "shipped" / name
+    ir = next(d.glob("*.ir.json"))
+    return json.loads(ir.read_text()), json.loads((d / "meta.json").read_text())
+
+
+def reference_inputs(meta: dict[str, Any]) -> dict[str, np.ndarray]:
+    """Seeded inputs the reference's packager would make (``default_rng(index)``, standard
+    normal, constants from ``data``), or the ``dist`` a generated problem names."""
+    from ptxgen.problems import seeded_input
+
+    out = {}
+    for a in meta["kernels"][0]["args"]:
+        if a.get("output") or a.get("intermediate"):
+            continue
+        arg = dict(a)
+        if "seed" in arg and "dist" not in arg:
+            arg["seed"] = meta["graph_inputs"].index(a["name"])
+        out[a["name"]] = seeded_input(arg)
+    return out
+
+
+def gpu_run(graph: dict[str, Any], meta: dict[str, Any], inputs: dict[str, np.ndarray],
+            guard: int = 0, **flags: bool) -> dict[str, np.ndarray]:
+    """Compile, launch on cuda:0 through the C-ABI launcher, and return every output buffer
+    (bf16 as uint16 bits). With ``guard`` > 0 each output gets that many canary elements past
+    its end, and the test fails if the kernel touched them."""
+    import torch
+
+    from ptxgen.runtime import Problem
+
+    prob = Problem(graph, meta, flags=flags)
+    tensors = prob.allocate(extra_guard=guard)
+    launch = prob.launch_entry
+    for a in launch["args"]:
+        t = tensors[a["name"]]
+        if a["name"] in inputs:
+            host = np.ascontiguousarray(inputs[a["name"]]).reshape(-1)
+            src = torch.from_numpy(host.view(np.int16) if host.dtype == np.uint16 else host)
+            t[: host.size].copy_(src.view(t.dtype) if host.dtype == np.uint16 else src)
+        else:
+            t.fill_(float("nan") if t.is_floating_point() else 0x5A)
+        if guard and a["name"] not in inputs:
+            t[-guard:].fill_(-1024)
+    prob.launch(tensors, check_status=True)
+    torch.cuda.synchronize()
+    out = {}
+    for a in launch["args"]:
+        if not a.get("output"):
+            continue
+        t = tensors[a["name"]]
+        n = int(np.prod(a["shape"]))
+        if guard:
+            tail = t[n:].float().cpu().numpy()
+            assert np.all(tail == -1024), f"{a['name']}: kernel wrote past the buffer end"
+        arr = t[:n].cpu()
+        if a["dtype"] == "bf16":
+            out[a["name"]] = arr.view(torch.int16).numpy().view(np.uint16).reshape(a["shape"])
+        else:
+            out[a["name"]] = arr.numpy().reshape(a["shape"])
+    return out
+
+
+def oracle_run(graph: dict[str, Any], meta: dict[str, Any], inputs: dict[str, np.ndarray],
+               no_fusion: bool = False) -> dict[str, np.ndarray]:
+    """The oracle's output buffers (bf16 as uint16 bits, like ``gpu_run``)."""
+    from oracle.fp import f32_to_bf16_bits
+    from oracle.interp import run_kernel
+
+    out = run_kernel(graph, meta, inputs, no_fusion=no_fusion)
+    args = {a["name"]: a for a in meta["kernels"][0]["args"]}
+    return {n: (f32_to_bf16_bits(v) if args[n]["dtype"] == "bf16" else v).reshape(
+        args[n]["shape"]) for n, v in out.items()}
+
+
+@pytest.fixture(scope="session")
+def cuda() -> Any:
+    import torch
+
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from ptxgen.build import build_library
+    from ptxgen.runtime import init
+
+    build_library()
+    init(0)
+    return torch.device("cuda:0")

@@ -1,0 +1,160 @@
+"""Compilation on the CPU: every IR lowers, ptxas accepts the module for sm_100a, the CLI keeps
+the reference's contract, and the emitted code has the shape the B200 design asks for."""
+
+from __future__ import annotations
+
+import json
+import re
+import shutil
+import subprocess
+import sys
+
+import pytest
+from conftest import ROOT, SHIPPED, shipped
+
+from ptxgen import problems
+from ptxgen.compiler import to_ptx
+from ptxgen.ir import Graph
+
+PTXAS = shutil.which("ptxas")
+
+
+def ptxas(ptx: str, tmp_path) -> str:
+    if PTXAS is None:
+        pytest.skip("no ptxas")
+    f = tmp_path / "k.ptx"
+    f.write_text(ptx)
+    r = subprocess.run([PTXAS, "-arch=sm_100a", "-v", str(f), "-o", str(tmp_path / "k.cubin")],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    return r.stderr
+
+
+def compile_spec(spec: problems.ProblemSpec, **flags: bool) -> str:
+    return to_ptx(Graph.from_dict(spec.graph), spec.meta, **flags)
+
+
+FLAG_SETS = [{}, {"no_unroll": True}, {"no_fusion": True}, {"no_cse": True}]
+
+
+@pytest.mark.parametrize("name", SHIPPED)
+@pytest.mark.parametrize("flags", FLAG_SETS, ids=["default", "no_unroll", "no_fusion", "no_cse"])
+def test_shipped_compiles_and_assembles(name: str, flags: dict, tmp_path) -> None:
+    graph, meta = shipped(name)
+    ptx = to_ptx(Graph.from_dict(graph), meta, **flags)
+    assert ".target sm_100a" in ptx
+    assert ".multicast::cluster" not in ptx
+    ptxas(ptx, tmp_path)
+
+
+SMALL = {
+    "c1": lambda: problems.pointwise_add(3000),
+    "c2": lambda: problems.gelu_chain(64, 256),
+    "c3": lambda: problems.row_softmax(8, 1024),
+    "c4": lambda: problems.full_sum(1 << 20, 256, 16),
+    "c5": lambda: problems.matmul(256, 256, 256),
+    "c5b": lambda: problems.matmul(256, 256, 512, split_k=2, raster_group=None),
+}
+
+
+@pytest.mark.parametrize("key", sorted(SMALL))
+def test_configs_assemble(key: str, tmp_path) -> None:
+    ptx = compile_spec(SMALL[key]())
+    info = ptxas(ptx, tmp_path)
+    assert "spill" in info
+
+
+def test_full_size_configs_assemble(tmp_path) -> None:
+    for key in ("c1_vector_add", "c2_gelu_chain", "c3_row_softmax", "c4_full_sum"):
+        ptxas(compile_spec(problems.CONFIGS[key]()), tmp_path)
+
+
+def test_pointwise_is_vectorised() -> None:
+    ptx = compile_spec(problems.pointwise_add(1 << 20))
+    assert ptx.count("ld.global.nc.v4.f32") == 2
+    assert ptx.count("st.global.v4.f32") == 1
+    assert "add.rn.f32" in ptx and "bra" not in ptx  # no tail guard: every block is full
+
+
+def test_tail_guard_only_when_needed() -> None:
+    assert "bra" in compile_spec(problems.pointwise_add(3000))  # 750 cells, blocks of 256
+    assert "bra" not in compile_spec(problems.pointwise_add(4096))
+
+
+def test_gelu_packs_bf16_128_bit() -> None:
+    ptx = compile_spec(problems.gelu_chain(64, 256))
+    assert ptx.count("ld.global.nc.v4.b32") == 1 and ptx.count("st.global.v4.b32") == 1
+    assert ptx.count("ld.global.nc.f32") == 3  # a, b and one s[row] for all eight elements
+    assert "fma.rn.f32" in ptx and "ex2.approx.ftz.f32" in ptx
+
+
+def test_gelu_no_fusion_flag() -> None:
+    ptx = compile_spec(problems.gelu_chain(64, 256), no_fusion=True)
+    assert "fma.rn.f32" not in ptx.replace("fma.rn.f32 %f", "") or \
+        ptx.count("fma.rn.f32") == ptx.count("rcp.approx")  # only tanh's own fma remains
+
+
+def test_softmax_reads_each_row_once() -> None:
+    ptx = compile_spec(problems.row_softmax(8, 4096, 256))
+    assert ptx.count("ld.global.nc.f32") == 4096 // 256  # passes 2 and 3 reuse pass 1's loads
+    assert ptx.count("ex2.approx") == 4096 // 256
+    assert "redux.sync.max.f32" in ptx
+
+
+def test_no_cse_reloads() -> None:
+    ptx = compile_spec(problems.row_softmax(8, 4096, 256), no_cse=True)
+    assert ptx.count("ld.global.nc.f32") == 3 * 4096 // 256
+
+
+def test_no_unroll_makes_runtime_loops() -> None:
+    ptx = compile_spec(problems.row_softmax(8, 4096, 256), no_unroll=True)
+    assert ptx.count("$L_loop_") >= 3 * 2
+
+
+def test_sum_unrolls_grid_stride_loop() -> None:
+    ptx = compile_spec(problems.CONFIGS["c4_full_sum"]())
+    assert ptx.count("ld.global.nc.f32") >= 16
+    assert "red.global.add.f32" in ptx
+    # no immediate offset beyond 2^30 bytes
+    offs = [int(m) for m in re.findall(r"\[%rd\d+\+(\d+)\]", ptx)]
+    assert max(offs) < 2**30
+
+
+def test_cli_contract(tmp_path) -> None:
+    graph, meta = shipped("p02_scale_shift")
+    d = tmp_path / "p02"
+    d.mkdir()
+    (d / "k.ir.json").write_text(json.dumps(graph))
+    (d / "meta.json").write_text(json.dumps(meta))
+    for flags in ([], ["--no_loop_unroll"], ["--no_fusion"], ["--no_cse"]):
+        r = subprocess.run([sys.executable, str(ROOT / "compile.py"), str(d / "k.ir.json"),
+                            *flags], capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr
+        assert r.stdout.startswith("//") and ".visible .entry k_add_pointwise(" in r.stdout
+
+
+def test_cli_fails_loudly(tmp_path) -> None:
+    graph, meta = shipped("p02_scale_shift")
+    meta["kernels"][0]["grid"] = [4, 2, 1]  # a 2-D launch is not supported
+    d = tmp_path / "bad"
+    d.mkdir()
+    (d / "k.ir.json").write_text(json.dumps(graph))
+    (d / "meta.json").write_text(json.dumps(meta))
+    r = subprocess.run([sys.executable, str(ROOT / "compile.py"), str(d / "k.ir.json")],
+                       capture_output=True, text=True)
+    assert r.returncode != 0 and "NotImplementedError" in r.stderr
+    meta["kernels"][0]["grid"] = [4, 1, 1]
+    meta["kernels"][0]["entry"] = "no_such_kernel"
+    (d / "meta.json").write_text(json.dumps(meta))
+    r = subprocess.run([sys.executable, str(ROOT / "compile.py"), str(d / "k.ir.json")],
+                       capture_output=True, text=True)
+    assert r.returncode != 0 and "ValueError" in r.stderr
+
+
+def test_unsupported_node_raises() -> None:
+    graph, meta = shipped("p02_scale_shift")
+    body = graph["nodes"]["add"]["op_fields"]["body"][0]
+    graph["nodes"]["add"]["op_fields"]["body"][0] = body.replace("swizzle='NONE'",
+                                                                 "swizzle='XOR'")
+    with pytest.raises(NotImplementedError):
+        to_ptx(Graph.from_dict(graph), meta)

@@ -1,0 +1,115 @@
+"""GPU parity: every kernel, launched through the C-ABI launcher on a B200, against the NumPy
+oracle on the same seeded inputs.
+
+Bars (stated per case): bit-exact wherever the kernel's arithmetic is IEEE round-to-nearest with
+the lowering's own fma contractions and a fixed order (pointwise, single-block reductions, the
+SIMT matmul); within a few f32 ulp where fast-math approximations enter (``ex2``/``rcp.approx``,
+about 2 ulp each, propagated); within one bf16 ulp for bf16 outputs of fast-math chains; and
+within rel 1e-5 of the f64 sum, or rel 1e-2 for bf16 GEMMs, where atomics add in an order the
+hardware picks.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+from conftest import SHIPPED, gpu_run, oracle_run, reference_inputs, shipped
+
+from ptxgen import problems
+
+pytestmark = pytest.mark.gpu
+
+
+def ulp_diff_f32(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """Distance in f32 ulps (via the ordered integer line of the bit patterns)."""
+    def ordered(x: np.ndarray) -> np.ndarray:
+        i = np.ascontiguousarray(x, np.float32).view(np.int32).astype(np.int64)
+        return np.where(i < 0, -(i & 0x7FFFFFFF), i)
+    return np.abs(ordered(a) - ordered(b))
+
+
+def check(kind: str, got: np.ndarray, want: np.ndarray, dtype: str, bound: float = 0) -> None:
+    if kind == "exact":
+        if dtype == "bf16":
+            assert np.array_equal(got, want), f"{np.sum(got != want)} of {got.size} differ"
+        else:
+            bad = ~((got == want) | (np.isnan(got) & np.isnan(want)))
+            assert not bad.any(), f"{bad.sum()} of {got.size} differ, e.g. {got[bad][:4]} vs " \
+                                  f"{want[bad][:4]}"
+    elif kind == "ulp":
+        if dtype == "bf16":
+            d = np.abs(got.astype(np.int32) - want.astype(np.int32))
+        else:
+            d = ulp_diff_f32(got, want)
+        assert d.max() <= bound, f"max {d.max()} ulp (bound {bound}) at {np.argmax(d)}"
+    else:
+        g, w = got.astype(np.float64), want.astype(np.float64)
+        np.testing.assert_allclose(g, w, rtol=bound, atol=bound * max(1.0, np.abs(w).max()))
+
+
+SHIPPED_BAR = {"p02_scale_shift": ("exact", 0), "r02_big_sum": ("exact", 0),
+               "m01_matmul_512": ("exact", 0), "a01_attention": ("ulp", 64),
+               "a03_noscale": ("ulp", 64)}
+
+
+@pytest.mark.parametrize("name", SHIPPED)
+@pytest.mark.parametrize("flags", [{}, {"no_unroll": True}, {"no_fusion": True},
+                                   {"no_cse": True}],
+                         ids=["default", "no_unroll", "no_fusion", "no_cse"])
+def test_shipped_parity(cuda, name: str, flags: dict) -> None:
+    graph, meta = shipped(name)
+    ins = reference_inputs(meta)
+    got = gpu_run(graph, meta, ins, guard=64, **flags)
+    want = oracle_run(graph, meta, ins, no_fusion=flags.get("no_fusion", False))
+    kind, bound = SHIPPED_BAR[name]
+    for out in got:
+        check(kind, got[out], want[out], "f32", bound)
+
+
+CASES = {
+    # key: (spec maker, comparison, bound, output dtype)
+    "c1_odd": (lambda: problems.pointwise_add(3000), "exact", 0, "f32"),
+    "c1_one_block": (lambda: problems.pointwise_add(1000, unroll=4), "exact", 0, "f32"),
+    "c1_unroll1_odd": (lambda: problems.pointwise_add(1001), "exact", 0, "f32"),
+    "c1_2e20": (lambda: problems.pointwise_add(1 << 20), "exact", 0, "f32"),
+    "c2_small": (lambda: problems.gelu_chain(64, 256), "ulp", 1, "bf16"),
+    "c2_odd_cols": (lambda: problems.gelu_chain(33, 24, unroll=8), "ulp", 1, "bf16"),
+    "c2_unroll1": (lambda: problems.gelu_chain(17, 15), "ulp", 1, "bf16"),
+    "c3_small": (lambda: problems.row_softmax(64, 1024), "ulp", 32, "f32"),
+    "c3_block512": (lambda: problems.row_softmax(16, 4096, 512), "ulp", 32, "f32"),
+    "c3_block32": (lambda: problems.row_softmax(8, 256, 32), "ulp", 32, "f32"),
+    "c4_small": (lambda: problems.full_sum(1 << 20, 256, 16), "rel", 1e-6, "f32"),
+    "c4_ragged": (lambda: problems.full_sum((1 << 20) + 12345, 128, 37), "rel", 1e-6, "f32"),
+    "c5_generic": (lambda: problems.matmul(256, 256, 256), "exact", 0, "f32"),
+    "c5_generic_rect": (lambda: problems.matmul(256, 512, 128, bn=128), "exact", 0, "f32"),
+    "c5b_generic": (lambda: problems.matmul(256, 256, 512, split_k=2, raster_group=None),
+                    "rel", 1e-5, "f32"),
+}
+
+
+@pytest.mark.parametrize("key", sorted(CASES))
+def test_config_parity(cuda, key: str) -> None:
+    make, kind, bound, dtype = CASES[key]
+    spec = make()
+    ins = reference_inputs(spec.meta)
+    got = gpu_run(spec.graph, spec.meta, ins, guard=64)
+    want = oracle_run(spec.graph, spec.meta, ins)
+    for out in got:
+        check(kind, got[out], want[out], dtype, bound)
+
+
+def test_sum_against_f64(cuda) -> None:
+    """Config 4's reduction at 2^26 elements against an f64 NumPy sum (rel 1e-5)."""
+    spec = problems.full_sum(1 << 26)
+    ins = reference_inputs(spec.meta)
+    got = gpu_run(spec.graph, spec.meta, ins)["sum_1"][0]
+    want = ins["x"].astype(np.float64).sum()
+    assert abs(got / want - 1) < 1e-5, (got, want)
+
+
+def test_vector_add_full_size(cuda) -> None:
+    """Config 1 at its full size, bit-exact against NumPy's IEEE add."""
+    spec = problems.CONFIGS["c1_vector_add"]()
+    ins = reference_inputs(spec.meta)
+    got = gpu_run(spec.graph, spec.meta, ins)["add"]
+    assert np.array_equal(got, ins["x"] + ins["y"])
