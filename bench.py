@@ -1,0 +1,480 @@
+"""Benchmark of the B200 ptxgen backend: kernel throughput against the HBM / tensor roofline.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+For N > 1 launch one process per GPU with torchrun (``--nproc-per-node N``); ranks share each
+configuration's Tile axis (``ptxgen.shard``), and only the full sum all-reduces its partials.
+
+A step is one launch of the workload's kernel over its whole (per-rank) input, compiled from
+Kernel IR by this repository's compiler and launched through its C-ABI launcher, with the inputs
+already resident in HBM. L2 is flushed (a 256 MiB write) before every timed step, outside the
+kernel's CUDA events. The printed ``value`` is the whole job's algorithmic bytes (or flops) per
+second over the slowest rank's mean kernel time; ``e2e`` is the same metric through the one-call
+host-buffer path (``pg_run_host``: page-locked inputs copied in, launch, result copied out).
+Rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+from typing import Any
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "emmy-hackathon-submission_b200"))
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+
+DEFAULT_WORKLOAD = "c2_gelu_chain"  # the configuration BASELINE.json's metric is quoted on
+EXTRA_WORKLOADS = ("c1_vector_add", "c3_row_softmax", "c4_full_sum")
+FLUSH_BYTES = 256 << 20
+
+
+def parse_args() -> argparse.Namespace:
+    p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--workload", default=DEFAULT_WORKLOAD)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--no-extras", action="store_true", help="skip the other configurations")
+    p.add_argument("--cpu-seconds", type=float, default=12.0,
+                   help="target seconds of CPU work for the CPU baseline sample")
+    return p.parse_args()
+
+
+# --- distributed plumbing ----------------------------------------------------------------------
+
+
+def dist_env() -> tuple[int, int, int]:
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def init_dist(world: int, local_rank: int) -> Any:
+    import torch
+    import torch.distributed as dist
+
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device(f"cuda:{local_rank}"))
+    return dist
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# --- peaks, clocks, profiles -------------------------------------------------------------------
+
+
+def peaks() -> tuple[dict[str, float], str]:
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        d = json.loads(f.read_text())
+        return {"hbm": float(d["hbm_gbs"]), "tensor": float(d["bf16_tflops"]),
+                "tensor_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"]))}, \
+            "measured"
+    return {"hbm": 6650.0, "tensor": 1590.0, "tensor_sustained": 1400.0}, "fallback"
+
+
+def traffic_of(workload: str) -> float | None:
+    f = ROOT / "profiles" / "traffic.json"
+    if not f.exists():
+        return None
+    return json.loads(f.read_text()).get(workload)
+
+
+class ClockSampler:
+    """Samples SM clocks and clock-event reasons through NVML while the timed region runs."""
+
+    REASONS = {0x2: "applications_clocks", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clocks"}
+
+    def __init__(self, index: int):
+        self.samples: list[int] = []
+        self.reasons: set[str] = set()
+        self.max_mhz: int | None = None
+        self._stop = threading.Event()
+        self._thread: threading.Thread | None = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # noqa: BLE001 - no NVML: report no clocks
+            self.nvml = None
+
+    def _run(self) -> None:
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nvml.nvmlDeviceGetClockInfo(self.h,
+                                                                     self.nvml.NVML_CLOCK_SM))
+                bits = self.nvml.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.reasons |= {n for b, n in self.REASONS.items() if bits & b}
+            except Exception:  # noqa: BLE001
+                pass
+            self._stop.wait(0.005)
+
+    def __enter__(self) -> ClockSampler:
+        if self.nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc: object) -> None:
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self) -> dict[str, Any]:
+        med = statistics.median(self.samples) if self.samples else None
+        return {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.samples)}
+
+
+# --- inputs ------------------------------------------------------------------------------------
+
+
+def device_tensors(prob: Any, seed: int) -> dict[str, Any]:
+    """Every argument of the problem on the GPU; inputs drawn on the device from their
+    configured distribution (bf16 rounded to nearest even), outputs left for the kernel."""
+    import torch
+
+    tensors = prob.allocate()
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    for i, a in enumerate(prob.launch_entry["args"]):
+        t = tensors[a["name"]]
+        if a.get("output"):
+            continue
+        if "data" in a:
+            t.copy_(torch.tensor(a["data"], dtype=torch.float32).to(t.dtype))
+            continue
+        dist = a.get("dist", ["normal", 0.0, 1.0])
+        f = torch.empty(t.numel(), dtype=torch.float32, device=t.device)
+        if dist[0] == "uniform":
+            f.uniform_(dist[1], dist[2], generator=gen)
+        else:
+            f.normal_(dist[1], dist[2], generator=gen)
+        t.copy_(f.to(t.dtype))
+        del f
+    return tensors
+
+
+# --- measurement ---------------------------------------------------------------------------------
+
+
+def measure_kernel(plan: Any, steps: int, warmup: int, world: int) -> dict[str, Any]:
+    """Mean kernel time over ``steps`` timed launches (each after an L2 flush), the slowest
+    rank's, with the launch count and NVML clocks of the timed region."""
+    import torch
+
+    from ptxgen.runtime import Problem
+
+    rank = int(os.environ.get("RANK", 0))
+    prob = Problem(plan.spec.graph, plan.spec.meta)
+    prob.load()
+    tensors = device_tensors(prob, seed=1000 + rank)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step() -> None:
+        prob.launch(tensors, stream=stream.cuda_stream)
+        if plan.allreduce and world > 1:
+            import torch.distributed as tdist
+
+            for name in plan.allreduce:
+                tdist.all_reduce(tensors[name])
+
+    for _ in range(warmup):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as tdist
+
+        tdist.barrier()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    stops = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    sampler = ClockSampler(torch.cuda.current_device())
+    with sampler:
+        for i in range(steps):
+            flush.zero_()
+            starts[i].record(stream)
+            step()
+            stops[i].record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as tdist
+
+        tdist.barrier()
+    torch.cuda.synchronize()
+    times = [s.elapsed_time(e) for s, e in zip(starts, stops, strict=True)]
+    mean_ms = statistics.fmean(times)
+    status = prob.module.status()
+    if status:
+        raise RuntimeError(f"kernel status word 0x{status:08x}")
+    out = {"mean_ms": max_over_ranks(mean_ms, world),
+           "median_ms": max_over_ranks(statistics.median(times), world),
+           "min_ms": max_over_ranks(min(times), world), "launches": steps,
+           "clocks": sampler.summary(), "tensors": tensors, "prob": prob}
+    return out
+
+
+def measure_e2e(plan: Any, prob: Any, tensors: dict[str, Any], steps: int, world: int
+                ) -> dict[str, Any]:
+    """The same metric through ``pg_run_host``: page-locked host inputs copied in, the
+    zero_outputs zeroed, the launch, and the outputs copied back, every step."""
+    import torch
+
+    launch = prob.launch_entry
+    host, dev, nbytes, flags = [], [], [], []
+    keep = []
+    h2d = d2h = 0
+    zero = set(launch.get("zero_outputs", []))
+    for name in launch["arg_order"]:
+        a = next(x for x in launch["args"] if x["name"] == name)
+        t = tensors[name]
+        size = t.numel() * t.element_size()
+        pinned = torch.empty(t.numel(), dtype=t.dtype, pin_memory=True)
+        if not a.get("output"):
+            pinned.copy_(t)
+        keep.append(pinned)
+        f = 0
+        if not a.get("output"):
+            f |= 1
+            h2d += size
+        if name in zero:
+            f |= 2
+        if a.get("output"):
+            f |= 4
+            d2h += size
+        host.append(pinned.data_ptr())
+        dev.append(t.data_ptr())
+        nbytes.append(size)
+        flags.append(f)
+    prob.module.fill_tensormaps({n: tensors[n].data_ptr() for n in tensors})
+    kernel = prob.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    args = (launch["grid"][0], launch["block"][0], int(launch.get("smem_bytes", 0)), stream,
+            dev, host, nbytes, flags)
+    kernel.run_host(*args)  # warm the path once
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        kernel.run_host(*args)
+        if plan.allreduce and world > 1:
+            import torch.distributed as tdist
+
+            for name in plan.allreduce:
+                tdist.all_reduce(tensors[name])
+            torch.cuda.synchronize()
+        times.append(time.perf_counter() - t0)
+    mean_s = max_over_ranks(statistics.fmean(times), world)
+    return {"mean_s": mean_s, "h2d": h2d, "d2h": d2h}
+
+
+def cpu_baseline(name: str, plan: Any, seconds: float) -> dict[str, Any]:
+    """The NumPy path of the same configuration on a bounded sample, timed on this host."""
+    from oracle.semantics import FORMULAS
+    from ptxgen import problems, shard
+
+    fn = FORMULAS[name]
+    # a sample of the workload: the same kernel shape on fewer rows / elements
+    samples = {
+        "c1_vector_add": lambda f: problems.pointwise_add(max(1 << 12, int((1 << 24) * f))),
+        "c2_gelu_chain": lambda f: problems.gelu_chain(max(8, int(8192 * f)), 8192),
+        "c3_row_softmax": lambda f: problems.row_softmax(max(8, int(16384 * f)), 4096),
+        "c4_full_sum": lambda f: problems.full_sum(max(1 << 16, int((1 << 30) * f) // 256 * 256)),
+        "c5_matmul": lambda f: problems.matmul(max(128, int(8192 * f) // 128 * 128), 8192, 8192),
+        "c5b_matmul_splitk": lambda f: problems.matmul(128, 1024, 65536, split_k=4,
+                                                        raster_group=None),
+    }
+    frac = 1 / 64
+    spec = samples[name](frac)
+    ins = {a["name"]: problems.seeded_input(a) for a in spec.kernel["args"]
+           if not a.get("output")}
+    work = shard.local_problem(name, 1).work
+    full = problems.CONFIGS[name]().kernel["args"]
+    scale = _elements(spec.kernel["args"]) / _elements(full)
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        fn(ins, spec.meta)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or reps >= 1000:
+            break
+    per_rep = el / reps
+    value = work * scale / per_rep
+    threads = os.cpu_count() if name.startswith("c5") else 1
+    return {"value": value, "per_rep_s": per_rep, "reps": reps, "cores": threads,
+            "sample": f"{spec.meta['id']} at {scale:.4f} of the full size "
+                      f"({_elements(spec.kernel['args'])} elements), {reps} repetitions"}
+
+
+def _elements(args: list[dict[str, Any]]) -> int:
+    return int(sum(np.prod(a["shape"]) for a in args if not a.get("output")))
+
+
+# --- the two arms --------------------------------------------------------------------------------
+
+
+def unit_of(plan: Any) -> tuple[str, str, float]:
+    if plan.units == "flops":
+        return "TFLOP/s", "tensor", 1e12
+    return "GB/s", "hbm", 1e9
+
+
+def run_ours(args: argparse.Namespace) -> None:
+    import torch
+
+    from ptxgen import shard
+    from ptxgen.build import build_library
+    from ptxgen.runtime import init
+
+    rank, world, local_rank = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}: launch with torchrun")
+    torch.cuda.set_device(local_rank)
+    init_dist(world, local_rank)
+    if rank == 0:
+        build_library()
+    if world > 1:
+        import torch.distributed as tdist
+
+        tdist.barrier()
+    init(local_rank)
+    pk, pk_kind = peaks()
+
+    def one(name: str, steps: int, warmup: int, with_e2e: bool) -> dict[str, Any]:
+        plan = shard.local_problem(name, world)
+        unit, bound, scale = unit_of(plan)
+        m = measure_kernel(plan, steps, warmup, world)
+        per_rank = plan.work / (m["mean_ms"] / 1e3) / scale
+        res: dict[str, Any] = {"workload": name, "value": per_rank * world, "unit": unit,
+                               "ms_per_step": m["mean_ms"], "median_ms": m["median_ms"],
+                               "min_ms": m["min_ms"], "clocks": m["clocks"],
+                               "launches": m["launches"]}
+        peak = pk[bound]
+        traffic = traffic_of(name)
+        res["roofline"] = {"bound": bound, "achieved": per_rank, "peak": peak,
+                           "unit": unit, "frac": per_rank / peak,
+                           "traffic": traffic, "peak_source": pk_kind,
+                           "algorithmic_per_launch": plan.work}
+        if with_e2e:
+            e = measure_e2e(plan, m["prob"], m["tensors"], max(3, min(steps, 20)), world)
+            res["e2e"] = {"value": plan.work * world / e["mean_s"] / scale, "unit": unit,
+                          "h2d_bytes_per_step": e["h2d"], "d2h_bytes_per_step": e["d2h"]}
+        del m
+        torch.cuda.empty_cache()
+        return res
+
+    head = one(args.workload, args.steps, args.warmup, with_e2e=True)
+    extras = []
+    if not args.no_extras:
+        for name in EXTRA_WORKLOADS:
+            if name == args.workload:
+                continue
+            try:
+                r = one(name, min(args.steps, 20), min(args.warmup, 3), with_e2e=False)
+                extras.append({k: r[k] for k in ("workload", "value", "unit", "ms_per_step",
+                                                 "roofline")})
+            except Exception as e:  # noqa: BLE001 - report and continue
+                extras.append({"workload": name, "error": f"{type(e).__name__}: {e}"[:300]})
+    if rank != 0:
+        return
+    plan = shard.local_problem(args.workload, world)
+    cpu = cpu_baseline(args.workload, plan, args.cpu_seconds) if world == 1 else None
+    line = {
+        "metric": "Kernel time: HBM GB/s (% of ~8 TB/s), GEMM TFLOPS (% peak) at 1/2/4/8 B200",
+        "value": head["value"], "unit": head["unit"], "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": _dtype(args.workload),
+        "data": "synthetic (seeded, the configuration's distributions, generated on the GPU)",
+        "config": {"workload": args.workload, "per_rank": plan.spec.meta["id"],
+                   "parallelism": f"tile-axis x{world}" if world > 1 else "single GPU",
+                   "l2": "flushed (256 MiB write) before every timed step",
+                   "allreduce": list(plan.allreduce)},
+        "roofline": head["roofline"], "e2e": head["e2e"], "clocks": head["clocks"],
+        "gpu_launches": head["launches"],
+        "cpu_baseline": cpu and {"value": cpu["value"] / unit_of(plan)[2], "unit": head["unit"],
+                                 "cores": cpu["cores"], "kind": "port", "sample": cpu["sample"]},
+        "workloads": extras,
+    }
+    print(json.dumps(line))
+
+
+def _dtype(name: str) -> str:
+    return {"c1_vector_add": "f32", "c2_gelu_chain": "bf16 (f32 compute)",
+            "c3_row_softmax": "f32", "c4_full_sum": "f32", "c5_matmul": "bf16 (f32 accumulate)",
+            "c5b_matmul_splitk": "bf16 (f32 accumulate)"}[name]
+
+
+def run_reference(args: argparse.Namespace) -> None:
+    """The CPU path of the same configuration (the NumPy port of its semantics, the oracle's
+    formulas), timed per step on a bounded sample on this host's cores."""
+    from ptxgen import shard
+
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    plan = shard.local_problem(args.workload, 1)
+    unit, _, scale = unit_of(plan)
+    per_step = max(1.0, args.cpu_seconds / max(1, args.steps + args.warmup))
+    vals = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline(args.workload, plan, per_step)
+        if i >= args.warmup:
+            vals.append(r["value"])
+    value = statistics.fmean(vals) / scale
+    line = {
+        "metric": "Kernel time: HBM GB/s (% of ~8 TB/s), GEMM TFLOPS (% peak) at 1/2/4/8 B200",
+        "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": r["per_rep_s"] * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": _dtype(args.workload),
+        "data": "synthetic (seeded NumPy inputs)", "impl": "reference",
+        "config": {"workload": args.workload, "parallelism": "host CPU"},
+        "cpu_baseline": {"value": value, "unit": unit, "cores": r["cores"], "kind": "port",
+                         "sample": r["sample"]},
+        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    run_ours(args)
+    rank, world, _ = dist_env()
+    if world > 1:
+        import torch.distributed as tdist
+
+        tdist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -144,6 +144,11 @@ def cvt(k: Kernel, x: str, src: str, dst: str) -> str:
         return x
     if src in FLOAT_TYPES and dst in FLOAT_TYPES and "f32" not in (src, dst):
         return cvt(k, cvt(k, x, src, "f32"), "f32", dst)
+    if src == "bf16" and dst == "f32":
+        # exact: the bf16 bits are the upper half of the f32 bits. A register pack runs on the
+        # integer pipe, where cvt.f32.bf16 would take a slot of the XU pipe that ex2/rcp need.
+        zero = k.pure("mov.b16", "b16", "0")
+        return k.pure("mov.b32", "f32", f"{{{zero}, {x}}}")
     if src in FLOAT_TYPES and dst in FLOAT_TYPES:
         rnd = "" if size(dst) > size(src) else ".rn"  # widening is exact
     elif dst in FLOAT_TYPES:

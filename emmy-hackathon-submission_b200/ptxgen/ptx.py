@@ -366,6 +366,9 @@ class _Vectorizer:
     def _segment(self, seg: list[Ins]) -> list[Ins]:
         if len(seg) < 2:
             return seg
+        # bf16 registers that are a plain rounding of an f32 register, for cvt.rn.bf16x2.f32
+        self.bf16_sources = {ins.dst[0]: ins.src[0] for ins in seg
+                             if ins.op == "cvt.rn.bf16.f32" and len(ins.dst) == 1}
         seg = self._loads(seg)
         seg = self._stores(seg)
         return seg
@@ -510,8 +513,13 @@ class _Vectorizer:
             for j in range(len(regs) // 2):
                 w = k.reg("b32")
                 words.append(w)
-                ins = Ins(text=f"\tmov.b32 {w}, {{{regs[2 * j]}, {regs[2 * j + 1]}}};")
-                ins.dst, ins.src = (w,), (regs[2 * j], regs[2 * j + 1])
+                lo, hi = self.bf16_sources.get(regs[2 * j]), self.bf16_sources.get(regs[2 * j + 1])
+                if lo is not None and hi is not None:
+                    # two f32 -> bf16 roundings packed by one instruction (upper half first)
+                    ins = Ins("cvt.rn.bf16x2.f32", (w,), (hi, lo), pure=True)
+                else:
+                    ins = Ins(text=f"\tmov.b32 {w}, {{{regs[2 * j]}, {regs[2 * j + 1]}}};")
+                    ins.dst, ins.src = (w,), (regs[2 * j], regs[2 * j + 1])
                 out.append(ins)
             out.append(Ins(mem=Mem(kind, space, "b32", addr, off, tuple(words), hint)))
             return out

@@ -223,6 +223,7 @@ class Problem:
     device: int = 0
     _module: Module | None = None
     _kernel: Kernel | None = None
+    _launch: dict[str, Any] | None = None
 
     @classmethod
     def from_dir(cls, path: str | Path, **flags: bool) -> Problem:
@@ -233,10 +234,12 @@ class Problem:
 
     @property
     def launch_entry(self) -> dict[str, Any]:
-        from .compiler import kernel_for_meta
-        from .ir import Graph
+        if self._launch is None:
+            from .compiler import kernel_for_meta
+            from .ir import Graph
 
-        return kernel_for_meta(Graph.from_dict(self.graph_json), self.meta)[1]
+            self._launch = kernel_for_meta(Graph.from_dict(self.graph_json), self.meta)[1]
+        return self._launch
 
     def compile(self) -> str:
         from .compiler import to_ptx
@@ -283,10 +286,12 @@ class Problem:
         ptrs = {name: t.data_ptr() for name, t in tensors.items()}
         self.module.fill_tensormaps(ptrs)
         if zero:
+            shapes = {a["name"]: a["shape"] for a in launch["args"]}
             for name in launch.get("zero_outputs", []):
                 t = tensors[name]
-                _check(library().pg_memset_async(t.data_ptr(), t.numel() * t.element_size(),
-                                                 stream), "pg_memset_async")
+                n = int(np.prod(shapes[name])) if shapes[name] else 1
+                _check(library().pg_memset_async(t.data_ptr(), n * t.element_size(), stream),
+                       "pg_memset_async")
         kernel.launch(launch["grid"][0], launch["block"][0], int(launch.get("smem_bytes", 0)),
                       [ptrs[n] for n in launch["arg_order"]], stream)
         if check_status:
