@@ -33,7 +33,8 @@ sys.path.insert(0, str(ROOT))
 import numpy as np  # noqa: E402
 
 DEFAULT_WORKLOAD = "c2_gelu_chain"  # the configuration BASELINE.json's metric is quoted on
-EXTRA_WORKLOADS = ("c1_vector_add", "c3_row_softmax", "c4_full_sum")
+EXTRA_WORKLOADS = ("c1_vector_add", "c3_row_softmax", "c4_full_sum", "c5_matmul",
+                   "c5b_matmul_splitk")
 FLUSH_BYTES = 256 << 20
 
 
@@ -276,7 +277,7 @@ def measure_e2e(plan: Any, prob: Any, tensors: dict[str, Any], steps: int, world
     prob.module.fill_tensormaps({n: tensors[n].data_ptr() for n in tensors})
     kernel = prob.load()
     stream = torch.cuda.current_stream().cuda_stream
-    args = (launch["grid"][0], launch["block"][0], int(launch.get("smem_bytes", 0)), stream,
+    args = (prob.grid(), launch["block"][0], int(launch.get("smem_bytes", 0)), stream,
             dev, host, nbytes, flags)
     kernel.run_host(*args)  # warm the path once
     torch.cuda.synchronize()

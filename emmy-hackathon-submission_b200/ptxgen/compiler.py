@@ -45,8 +45,9 @@ def kernel_for_meta(graph: Graph, meta: dict[str, Any]) -> tuple[KernelOp, dict[
 
 
 def to_ptx(graph: Graph, meta: dict[str, Any], no_unroll: bool = False, no_fusion: bool = False,
-           no_cse: bool = False) -> str:
-    """The PTX module for the kernel meta.json names (same contract as the reference)."""
+           no_cse: bool = False, templates: bool = True) -> str:
+    """The PTX module for the kernel meta.json names (same contract as the reference).
+    ``templates=False`` keeps every kernel on the generic lowering."""
     op, launch = kernel_for_meta(graph, meta)
     if list(launch["block"][1:]) != [1, 1] or list(launch["grid"][1:]) != [1, 1]:
         raise NotImplementedError("only 1-D launches")
@@ -60,4 +61,4 @@ def to_ptx(graph: Graph, meta: dict[str, Any], no_unroll: bool = False, no_fusio
     return compile_module(op, buffers, launch["arg_order"], launch["block"][0],
                           no_unroll=no_unroll, no_fusion=no_fusion, no_cse=no_cse,
                           smem_bytes=int(launch.get("smem_bytes", 0)),
-                          templates=not (no_unroll or no_fusion or no_cse))
+                          templates=templates and not (no_unroll or no_fusion or no_cse))

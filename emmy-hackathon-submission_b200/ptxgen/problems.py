@@ -390,7 +390,9 @@ def matmul(m: int = 8192, n: int = 8192, k: int = 8192, dtype: str = "bf16",
         axes.insert(0, Axis("ak_s", Dim(split_k)))
     raster = ("a0_b", "a1_b") if raster_group else None
     tile = Tile(tuple(axes), tuple(body), block, 0, raster, raster_group, "m")
-    smem = stages * (bm * bk + bk * bn) * esz
+    # the shared tiles plus 2 KiB, which a kernel aligning its tiles to 1 KiB and keeping its
+    # barriers beside them can use
+    smem = stages * (bm * bk + bk * bn) * esz + 2048
     b_dist = ["normal", 0.0, b_std if b_std is not None else 1.0 / math.sqrt(k)]
     args = [_arg("x1", dtype, [k, n], seed=1, dist=b_dist),
             _arg("x0", dtype, [m, k], seed=0, dist=["normal", 0.0, 1.0]),

@@ -136,6 +136,9 @@ class Module:
         launch = _kv(self.notes["launch"][0]) if "launch" in self.notes else {}
         self.grid = int(launch["grid"]) if "grid" in launch else None
         self.block = int(launch["block"]) if "block" in launch else None
+        # a persistent kernel loops over its tiles (tile = ctaid + i * nctaid): any grid works,
+        # and one CTA per SM is the right one
+        self.persistent = launch.get("persistent") == "1"
         dyn = self.notes.get("dynamic_smem")
         self.dynamic_smem = int(dyn[0]) if dyn else 0
 
@@ -180,7 +183,10 @@ class Kernel:
     def launch(self, grid: int, block: int, smem: int, pointers: list[int],
                stream: int = 0) -> None:
         m = self.module
-        if m.grid is not None and (grid, block) != (m.grid, m.block):
+        if m.persistent:
+            if block != m.block:
+                raise LaunchError(f"{self.entry}: compiled for block {m.block}, asked {block}")
+        elif m.grid is not None and (grid, block) != (m.grid, m.block):
             raise LaunchError(f"{self.entry}: compiled for grid {m.grid} x block {m.block}, "
                               f"asked to launch {grid} x {block}")
         smem = max(smem, m.dynamic_smem)
@@ -249,7 +255,8 @@ class Problem:
             self.ptx = to_ptx(Graph.from_dict(self.graph_json), self.meta,
                               self.flags.get("no_unroll", False),
                               self.flags.get("no_fusion", False),
-                              self.flags.get("no_cse", False))
+                              self.flags.get("no_cse", False),
+                              templates=not self.flags.get("no_templates", False))
         return self.ptx
 
     def load(self) -> Kernel:
@@ -263,6 +270,16 @@ class Problem:
         self.load()
         assert self._module is not None
         return self._module
+
+    def grid(self) -> int:
+        """meta.json's grid, or for a persistent kernel one CTA per SM (at most one per tile)."""
+        m = self.module
+        if m.persistent and m.grid is not None:
+            import torch
+
+            sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+            return max(1, min(m.grid, sms))
+        return int(self.launch_entry["grid"][0])
 
     def allocate(self, extra_guard: int = 0) -> dict[str, Any]:
         """Device tensors for every argument (uninitialised)."""
@@ -292,7 +309,7 @@ class Problem:
                 n = int(np.prod(shapes[name])) if shapes[name] else 1
                 _check(library().pg_memset_async(t.data_ptr(), n * t.element_size(), stream),
                        "pg_memset_async")
-        kernel.launch(launch["grid"][0], launch["block"][0], int(launch.get("smem_bytes", 0)),
+        kernel.launch(self.grid(), launch["block"][0], int(launch.get("smem_bytes", 0)),
                       [ptrs[n] for n in launch["arg_order"]], stream)
         if check_status:
             torch.cuda.synchronize(self.device)

@@ -14,4 +14,9 @@ from ..lower import Buffer
 
 def try_templates(op: KernelOp, buffers: Mapping[str, Buffer], arg_order: Sequence[str],
                   block: int, smem_bytes: int) -> str | None:
+    from . import matmul
+
+    plan = matmul.match(op, buffers, arg_order, block, smem_bytes)
+    if plan is not None:
+        return matmul.emit(plan)
     return None

@@ -1,0 +1,687 @@
+"""The tcgen05 GEMM template: a matmul-shaped Kernel IR nest over bf16/f16 operands, replaced by a
+persistent TMA + mbarrier + tcgen05.mma kernel with TMEM accumulators.
+
+Matching (``match``). The nest Emmy writes for ``A @ B`` (reference
+``examples/cse/m01_matmul_512/k_matmul_2967be.ir.txt``): a Tile whose block axes window the M
+and N axes of C (and, for split-K, one more axis that offsets K), Init'ed f32 accumulators, two
+shared buffers fed by cp.async copies of A and B tiles, one K loop whose inner loop loads from
+the two shared buffers, multiplies and Accum-adds into the accumulators, and Writes of the
+accumulators into C (atomic for split-K). The matcher checks these facts and the shapes
+A [M, K], B [K, N], C [M, N] with K the K loop's extent times the splits; anything else keeps
+the generic lowering.
+
+The kernel (``emit``), one CTA per SM, persistent over the output tiles (``tile = ctaid +
+i * nctaid``, so any grid size computes every tile once):
+
+* warp 0, lane 0 -- TMA producer: ``cp.async.bulk.tensor`` loads of a 128 x 64 A tile and a
+  64 x BN B tile (128-byte swizzled; B as BN/64 column chunks) per K step into a ring of
+  ``stages`` shared-memory stages, each guarded by a ``full`` mbarrier (expect_tx bytes) and an
+  ``empty`` one;
+* warp 1 -- allocates TMEM (two BN-column f32 accumulators), and lane 0 issues
+  ``tcgen05.mma.cta_group::1.kind::f16`` (M=128, N=BN, K=16, bf16/f16 in, f32 accumulate) from
+  the stage's shared-memory descriptors, ``tcgen05.commit``s each stage back to its ``empty``
+  barrier and each finished tile to the accumulator's ``tmem_full`` barrier;
+* warps 4-7 -- epilogue: ``tcgen05.ld`` (32 lanes x 32 columns per load) of the finished
+  accumulator, stores into C (``red.global.add.v4.f32`` for split-K), then ``tmem_empty``; with
+  two accumulators the epilogue of one tile overlaps the MMAs of the next.
+
+The tile order is the IR's own block order (its raster groups included), baked into the module as
+a table. Tensor maps live in module ``.global`` symbols that the launcher fills
+(``pg_tensormap_fill``), named in ``// @ptxgen tensormap`` header lines, so the kernel's
+parameters stay the plain device pointers of meta.json's arg_order. Every mbarrier wait is
+bounded by ``%globaltimer``; a wait that runs out sets a bit of the module's ``ptxgen_status``
+word, and the kernel winds down: the producer waits (bounded) for its own TMA loads to land, the
+MMA thread for its MMAs, then TMEM is freed. No load uses cluster multicast.
+"""
+
+from __future__ import annotations
+
+import math
+from collections.abc import Mapping, Sequence
+from dataclasses import dataclass
+
+from ..ir import (Accum, Assign, BinaryExpr, CpAsyncCommit, CpAsyncCopy, Expr, Init, KernelOp,
+                  Literal, Load, Loop, Smem, StridedLoop, Tile, Var, Write, walk)
+from ..lower import Buffer
+from ..ptx import PTX_VERSION, TARGET
+
+BM, BK = 128, 64  # tile rows (the MMA's M) and K per stage (64 bf16 = one 128-byte swizzle row)
+UMMA_K = 16
+MAX_STAGES = 6
+WAIT_NS = 2_000_000_000  # a bounded wait gives up after 2 s of %globaltimer
+EPILOGUE_WARPS = (4, 5, 6, 7)
+BAR_BYTES = 8
+
+
+@dataclass(frozen=True)
+class MatmulPlan:
+    entry: str
+    params: tuple[str, ...]
+    a: str
+    b: str
+    c: str
+    dtype: str  # of A and B: bf16 | f16
+    m: int
+    n: int
+    k: int
+    bn: int
+    splits: int
+    block: int
+    stages: int
+    atomic: bool
+    schedule: tuple[tuple[int, int, int], ...]  # (m tile, n tile, split) per tile index
+
+    @property
+    def kc(self) -> int:
+        return self.k // self.splits
+
+    @property
+    def tiles(self) -> int:
+        return len(self.schedule)
+
+    @property
+    def stage_bytes(self) -> int:
+        return (BM * BK + BK * self.bn) * 2
+
+
+# --- matching ----------------------------------------------------------------------------------
+
+
+def _names_in(e: object) -> set[str]:
+    out: set[str] = set()
+    if isinstance(e, Var):
+        out.add(e.name)
+    elif isinstance(e, BinaryExpr):
+        out |= _names_in(e.left) | _names_in(e.right)
+    elif isinstance(e, tuple):
+        for x in e:
+            out |= _names_in(x)
+    elif isinstance(e, Expr):
+        for f in getattr(e, "__dataclass_fields__", {}):
+            out |= _names_in(getattr(e, f))
+    return out
+
+
+def match(op: KernelOp, buffers: Mapping[str, Buffer], arg_order: Sequence[str], block: int,
+          smem_bytes: int) -> MatmulPlan | None:
+    t = op.body
+    if not isinstance(t, Tile) or not t.is_static_grid or t.aux_threads:
+        return None
+    body = t.body
+    inits = [s for s in body if isinstance(s, Init)]
+    smems = [s for s in body if isinstance(s, Smem)]
+    loops = [s for s in body if isinstance(s, Loop | StridedLoop)]
+    writes = [s for s in body if isinstance(s, Write)]
+    allowed = (Init, Smem, CpAsyncCopy, CpAsyncCommit, Loop, StridedLoop, Write)
+    if not all(isinstance(s, allowed) for s in body):
+        return None
+    if len(smems) != 2 or len(loops) != 1 or not writes or not inits:
+        return None
+    kloop = loops[0]
+    copies = [s for s in walk(body) if isinstance(s, CpAsyncCopy)]
+    feeds = {c.smem: c.src for c in copies}
+    if len(feeds) != 2 or len(set(feeds.values())) != 2:
+        return None
+    # the inner loop: loads from the two shared buffers, multiply, Accum add
+    inner = [s for s in kloop.body if isinstance(s, Loop | StridedLoop)]
+    if len(inner) != 1:
+        return None
+    loads, prods, accs = {}, {}, []
+    for s in inner[0].body:
+        if isinstance(s, Load) and s.input in feeds and len(s.names) == 1:
+            loads[s.names[0]] = s.input
+        elif isinstance(s, Assign) and s.op.name in ("multiply", "mul") and len(s.args) == 2:
+            prods[s.name] = tuple(s.args)
+        elif isinstance(s, Accum) and s.op.name in ("add", "sum") and s.base is None:
+            accs.append(s)
+        else:
+            return None
+    init_names = {i.name for i in inits if i.identity == 0.0 and i.dtype.name == "f32"}
+    for a in accs:
+        pair = prods.get(a.value)
+        if pair is None or a.name not in init_names or (a.dtype and a.dtype.name != "f32"):
+            return None
+        if {loads.get(pair[0]), loads.get(pair[1])} != set(feeds):
+            return None
+    if len(accs) != len(init_names):
+        return None
+    outs = {w.output for w in writes}
+    if len(outs) != 1:
+        return None
+    c = outs.pop()
+    written = {v for w in writes for v in w.values}
+    if written != {a.name for a in accs} or len({w.atomic for w in writes}) != 1:
+        return None
+    atomic = writes[0].atomic
+    cbuf = buffers.get(c)
+    if cbuf is None or cbuf.dtype != "f32" or len(cbuf.shape) != 2:
+        return None
+    m, n = cbuf.shape
+    # decide A and B by which shared buffer the inner loads index along the K loop's axis first
+    a_name, b_name = _which_is_a(inner[0], feeds, loads, buffers, m, n)
+    if a_name is None or b_name is None:
+        return None
+    abuf, bbuf = buffers[a_name], buffers[b_name]
+    if abuf.dtype != bbuf.dtype or abuf.dtype not in ("bf16", "f16"):
+        return None
+    k = abuf.shape[1]
+    if abuf.shape[0] != m or bbuf.shape != (k, n):
+        return None
+    # block axes: the ones windowing M and N, plus an optional split axis
+    # (the row index of C's Writes names the M block axis, the column index the N one)
+    axes = list(t.axes)
+    if any(len(w.index) != 2 for w in writes):
+        return None
+    row_names = set().union(*(_names_in(w.index[0]) for w in writes))
+    col_names = set().union(*(_names_in(w.index[1]) for w in writes))
+    mb = [i for i, ax in enumerate(axes) if ax.window is not None and ax.name in row_names and
+          ax.window.parent.extent.as_static() == m and m % ax.extent.as_static() == 0]
+    nb = [i for i, ax in enumerate(axes) if ax.window is not None and ax.name in col_names and
+          ax.window.parent.extent.as_static() == n and n % ax.extent.as_static() == 0 and
+          i not in mb]
+    if len(mb) != 1 or len(nb) != 1:
+        return None
+    mi, ni = mb[0], nb[0]
+    if m // axes[mi].extent.as_static() != BM:
+        return None
+    bn = n // axes[ni].extent.as_static()
+    if bn not in (64, 128, 256) or len(accs) * block != BM * bn:
+        return None
+    copy_names = set().union(*(_names_in(cp.src_index) for cp in copies))
+    extents = [ax.extent.as_static() for ax in axes]
+    strides = [math.prod(extents[i + 1:]) for i in range(len(extents))]
+    # a split axis is a block axis (its stride spans whole blocks) that offsets the copies' K
+    split_axes = [i for i, ax in enumerate(axes) if i not in (mi, ni) and ax.window is None and
+                  ax.name in copy_names and strides[i] % block == 0 and extents[i] > 1]
+    if len(split_axes) > 1:
+        return None
+    si = split_axes[0] if split_axes else None
+    splits = extents[si] if si is not None else 1
+    if (splits > 1) != atomic:
+        return None
+    if not kloop.axis.extent.is_static or kloop.axis.extent.as_static() * splits != k:
+        return None
+    block_axes = [i for i in (mi, ni, si) if i is not None]
+    if any(strides[i] % block for i in block_axes):
+        return None
+    thread_cells = math.prod(extents[i] for i in range(len(axes)) if i not in block_axes)
+    if thread_cells != block or block < 256 or block % 128:
+        return None
+    kc = k // splits
+    if kc % BK or k % 8 or n % 8:
+        return None
+    stage = (BM * BK + BK * bn) * 2
+    stages = min(MAX_STAGES, (smem_bytes - 2048) // stage)
+    if stages < 2:
+        return None
+    sched = _schedule(t, block, mi, ni, si)
+    return MatmulPlan(op.name, tuple(arg_order), a_name, b_name, c, abuf.dtype, m, n, k, bn,
+                      splits, block, stages, atomic, sched)
+
+
+def _which_is_a(inner: Loop | StridedLoop, feeds: dict[str, str], loads: dict[str, str],
+                buffers: Mapping[str, Buffer], m: int, n: int) -> tuple[str | None, str | None]:
+    """A is the operand whose shared tile the inner loop indexes with its axis last (row-major
+    [rows, k]); B the one it indexes with its axis first ([k, cols])."""
+    axis = inner.axis.name
+    a = b = None
+    for s in inner.body:
+        if not isinstance(s, Load) or s.input not in feeds or len(s.index) != 2:
+            continue
+        first, last = _names_in(s.index[0]), _names_in(s.index[1])
+        if axis in last and axis not in first:
+            a = feeds[s.input] if a in (None, feeds[s.input]) else "!"
+        elif axis in first and axis not in last:
+            b = feeds[s.input] if b in (None, feeds[s.input]) else "!"
+    if a in (None, "!") or b in (None, "!") or a == b:
+        return None, None
+    return a, b
+
+
+def _schedule(t: Tile, block: int, mi: int, ni: int, si: int | None
+              ) -> tuple[tuple[int, int, int], ...]:
+    """(m tile, n tile, split) of each CTA index, by the Tile's own decode of gid = cta*block:
+    row-major over the axes, with Emmy's grouped raster order for a raster pair."""
+    extents = list(t.extents)
+    strides = [math.prod(extents[i + 1:]) for i in range(len(extents))]
+    names = [a.name for a in t.axes]
+    raster = None
+    if t.raster_group and t.raster_axes and all(x in names for x in t.raster_axes):
+        ri, rj = (names.index(x) for x in t.raster_axes)
+        if rj == ri + 1:
+            gi, oi = (ri, rj) if t.raster_orient == "m" else (rj, ri)
+            g = min(t.raster_group, extents[gi])
+            if extents[gi] > 1 and g > 1:
+                raster = (gi, oi, g)
+    out = []
+    for cta in range(t.n_elements // block):
+        gid = cta * block
+        vals = [(gid // strides[i]) % extents[i] if i else gid // strides[i]
+                for i in range(len(extents))]
+        if raster is not None:
+            gi, oi, g = raster
+            ea, eb = extents[gi], extents[oi]
+            sub = gid // strides[max(gi, oi)]
+            if min(gi, oi):
+                sub %= ea * eb
+            grp, r = sub // (g * eb), sub % (g * eb)
+            gsz = min(ea - grp * g, g) if ea % g else g
+            vals[gi], vals[oi] = grp * g + r % gsz, r // gsz
+        out.append((vals[mi], vals[ni], vals[si] if si is not None else 0))
+    return tuple(out)
+
+
+# --- emission ----------------------------------------------------------------------------------
+
+
+class _Text:
+    def __init__(self) -> None:
+        self.lines: list[str] = []
+        self.regs: dict[str, str] = {}
+        self._n = 0
+
+    def reg(self, name: str, typ: str) -> str:
+        # bit types: tcgen05 operands want .b32 registers, and a .bN register serves any
+        # instruction type of that width
+        self.regs.setdefault(name, {"u32": "b32", "u64": "b64"}.get(typ, typ))
+        return f"%{name}"
+
+    def finish(self) -> list[str]:
+        """The body with every template register renamed %m_<name>, so none can collide with a
+        special register (%tid, %ctaid, ...)."""
+        import re
+
+        names = sorted(self.regs, key=len, reverse=True)
+        pat = re.compile(r"%(" + "|".join(map(re.escape, names)) + r")(?![\w.])")
+        return [pat.sub(r"%m_\1", line) for line in self.lines]
+
+    def label(self, hint: str) -> str:
+        self._n += 1
+        return f"$M_{hint}_{self._n}"
+
+    def __call__(self, line: str) -> None:
+        self.lines.append(line if line.endswith(":") else f"\t{line}")
+
+
+def bounded_wait(x: _Text, bar_addr: str, parity: str, code: int, fail: str,
+                 limit_ns: int = WAIT_NS) -> None:
+    """An mbarrier wait that gives up: it polls ``try_wait.parity`` until the phase of
+    ``parity`` completes or ``limit_ns`` of %globaltimer pass; then it sets bit ``code`` of the
+    module's ``ptxgen_status`` word and branches to ``fail``."""
+    top, ok = x.label("wait"), x.label("waited")
+    x(f"mov.u64 {x.reg('w_t0', 'u64')}, %globaltimer;")
+    x(f"{top}:")
+    x(f"mbarrier.try_wait.parity.shared::cta.b64 {x.reg('pw', 'pred')}, [{bar_addr}], {parity};")
+    x(f"@%pw bra {ok};")
+    x(f"mov.u64 {x.reg('w_t1', 'u64')}, %globaltimer;")
+    x("sub.u64 %w_t1, %w_t1, %w_t0;")
+    x(f"setp.lt.u64 {x.reg('pw2', 'pred')}, %w_t1, {limit_ns};")
+    x(f"@%pw2 bra {top};")
+    x(f"red.global.or.b32 [ptxgen_status], {1 << code};")
+    x(f"bra.uni {fail};")
+    x(f"{ok}:")
+
+
+def wait_probe_ptx(limit_ns: int, code: int = 7) -> str:
+    """A one-warp kernel that waits on an mbarrier nothing ever arrives at, through
+    ``bounded_wait``: it must give up after ``limit_ns`` and set status bit ``code``. Used to
+    test the give-up path without hanging a GPU."""
+    x = _Text()
+    x(f"mov.u32 {x.reg('smem', 'u32')}, probe_bar;")
+    x(f"mov.u32 {x.reg('tid', 'u32')}, %tid.x;")
+    x(f"setp.ne.u32 {x.reg('p', 'pred')}, %tid, 0;")
+    x("@%p bra $P_done;")
+    x("mbarrier.init.shared::cta.b64 [%smem], 1;")
+    x("fence.mbarrier_init.release.cluster;")
+    bounded_wait(x, "%smem", "0", code, "$P_done", limit_ns)
+    x("$P_done:")
+    x("ret;")
+    decls = "\n".join(f"\t.reg .{t} %m_{n};" for n, t in x.regs.items())
+    return "\n".join([
+        f".version {PTX_VERSION}\n.target {TARGET}\n.address_size 64\n",
+        ".global .align 4 .u32 ptxgen_status;",
+        ".visible .entry wait_probe(\n\t.param .u64 wait_probe_param_unused\n)\n"
+        ".maxntid 32, 1, 1\n{",
+        "\t.shared .align 8 .b64 probe_bar;", decls, *x.finish(), "}", ""])
+
+
+def _desc_hi(sbo: int, swizzle128: bool = True) -> int:
+    """Bits 32-63 of a tcgen05 shared-memory descriptor: stride byte offset (>>4) at 32,
+    the sm_100 descriptor version 1 at 46, the 128-byte swizzle mode (2) at 61."""
+    return (sbo >> 4) | (1 << 14) | ((2 if swizzle128 else 0) << 29)
+
+
+def instr_desc(dtype: str, bn: int, a_mn_major: bool = False, b_mn_major: bool = True) -> int:
+    """The 32-bit instruction descriptor of tcgen05.mma.kind::f16: f32 accumulator (bit 4),
+    A/B format bf16 = 1 or f16 = 0 (bits 7, 10), A/B major-ness (bits 15, 16: 1 = MN-major),
+    N >> 3 at bit 17, M >> 4 at bit 24."""
+    fmt = 1 if dtype == "bf16" else 0
+    return ((1 << 4) | (fmt << 7) | (fmt << 10) | (int(a_mn_major) << 15) |
+            (int(b_mn_major) << 16) | ((bn >> 3) << 17) | ((BM >> 4) << 24))
+
+
+def emit(p: MatmulPlan) -> str:
+    e = p.entry
+    x = _Text()
+    kb_count = p.kc // BK
+    a_stage = BM * BK * 2  # 16 KiB
+    b_chunk = BK * 64 * 2  # 8 KiB: 64 K rows x 64 columns
+    b_stage = BK * p.bn * 2
+    b_off = p.stages * a_stage
+    bar_off = p.stages * (a_stage + b_stage)
+    full, empty = 0, p.stages * BAR_BYTES
+    tfull = 2 * p.stages * BAR_BYTES
+    tempty = tfull + 2 * BAR_BYTES
+    drain = tempty + 2 * BAR_BYTES
+    slot = drain + BAR_BYTES
+    smem_total = 1024 + bar_off + slot + 16
+    tmem_cols = 2 * p.bn if 2 * p.bn <= 512 else p.bn
+    accs = tmem_cols // p.bn
+    if tmem_cols > 256:
+        # a CTA holding more than half of TMEM must be alone on its SM: ask for more than half
+        # of the SM's shared memory
+        smem_total = max(smem_total, 120 * 1024)
+    idesc = instr_desc(p.dtype, p.bn)
+    a_hi = _desc_hi(1024)  # K-major A: 8-row groups 1024 bytes apart
+    b_hi = _desc_hi(1024)  # MN-major B: 8-row (K) groups 1024 bytes apart
+    b_lbo = (BK * 128) >> 4  # MN-major B: 64-column swizzle atoms BK*128 bytes apart
+    ept = 32 * len(EPILOGUE_WARPS)
+
+    u32, u64, pred = "u32", "u64", "pred"
+    r = lambda n, t=u32: x.reg(n, t)  # noqa: E731
+
+    def wait(bar_addr: str, parity: str, code: int, fail: str) -> None:
+        bounded_wait(x, bar_addr, parity, code, fail)
+
+    def sched_lookup() -> None:
+        x(f"mul.wide.u32 {r('s_off', u64)}, %t, 4;")
+        x(f"add.s64 %s_off, {r('sched', u64)}, %s_off;")
+        x(f"ld.global.nc.u32 {r('code')}, [%s_off];")
+        x(f"and.b32 {r('mt')}, %code, 2047;")
+        x(f"shr.u32 {r('nt')}, %code, 11;")
+        x(f"and.b32 %nt, %nt, 2047;")
+        x(f"shr.u32 {r('st')}, %code, 22;")
+
+    def advance_stage() -> None:
+        x("add.u32 %it, %it, 1;")
+        x("add.u32 %s, %s, 1;")
+        x(f"setp.eq.u32 {r('pwrap', pred)}, %s, {p.stages};")
+        x("@%pwrap mov.u32 %s, 0;")
+        x("@%pwrap xor.b32 %ph, %ph, 1;")
+
+    def advance_acc() -> None:
+        x("add.u32 %tc, %tc, 1;")
+        x("add.u32 %ab, %ab, 1;")
+        x(f"setp.eq.u32 {r('pawrap', pred)}, %ab, {accs};")
+        x("@%pawrap mov.u32 %ab, 0;")
+        x("@%pawrap xor.b32 %aph, %aph, 1;")
+
+    # --- set-up: pointers, ids, shared-memory carve-up, barriers, TMEM -----------------------
+    x(f"ld.param.u64 {r('c_ptr', u64)}, [{e}_param_{p.c}];")
+    x("cvta.to.global.u64 %c_ptr, %c_ptr;")
+    x(f"mov.u32 {r('tid')}, %tid.x;")
+    x(f"setp.eq.u32 {r('ptrue', pred)}, %tid, %tid;")
+    x(f"mov.u32 {r('cta')}, %ctaid.x;")
+    x(f"mov.u32 {r('ncta')}, %nctaid.x;")
+    x(f"shr.u32 {r('warp')}, %tid, 5;")
+    x(f"and.b32 {r('lane')}, %tid, 31;")
+    x(f"mov.u32 {r('smem')}, smem_pool;")
+    x("add.u32 %smem, %smem, 1023;")
+    x("and.b32 %smem, %smem, -1024;")  # stages need 1024-byte alignment (128-byte swizzle)
+    x(f"add.u32 {r('bars')}, %smem, {bar_off};")
+    x(f"mov.u64 {r('tmap_a', u64)}, {e}_tmap_a;")
+    x("cvta.global.u64 %tmap_a, %tmap_a;")
+    x(f"mov.u64 {r('tmap_b', u64)}, {e}_tmap_b;")
+    x("cvta.global.u64 %tmap_b, %tmap_b;")
+    x(f"mov.u64 %sched, {e}_sched;")
+    x(f"setp.eq.u32 {r('p', pred)}, %tid, 0;")
+    init_done = x.label("init_done")
+    x(f"@!%p bra {init_done};")
+    for s in range(p.stages):
+        x(f"mbarrier.init.shared::cta.b64 [%bars+{full + 8 * s}], 1;")
+        x(f"mbarrier.init.shared::cta.b64 [%bars+{empty + 8 * s}], 1;")
+    for a in range(2):
+        x(f"mbarrier.init.shared::cta.b64 [%bars+{tfull + 8 * a}], 1;")
+        x(f"mbarrier.init.shared::cta.b64 [%bars+{tempty + 8 * a}], {ept};")
+    x(f"mbarrier.init.shared::cta.b64 [%bars+{drain}], 1;")
+    x("fence.mbarrier_init.release.cluster;")
+    x("fence.proxy.async.shared::cta;")
+    x("prefetch.tensormap [%tmap_a];")
+    x("prefetch.tensormap [%tmap_b];")
+    x(f"{init_done}:")
+    alloc_done = x.label("alloc_done")
+    x("setp.eq.u32 %p, %warp, 1;")
+    x(f"@!%p bra {alloc_done};")
+    x(f"add.u32 {r('slot')}, %bars, {slot};")
+    x(f"tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%slot], {tmem_cols};")
+    x("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;")
+    x(f"{alloc_done}:")
+    x("tcgen05.fence::before_thread_sync;")
+    x("barrier.sync 0;")  # not .aligned: warps 0 and 1 arrive from divergent branches
+    x("tcgen05.fence::after_thread_sync;")
+    x(f"ld.shared.b32 {r('tmem')}, [%bars+{slot}];")
+    teardown = "$M_teardown"
+    producer, mma, epi = "$M_producer", "$M_mma", "$M_epilogue"
+    x("setp.eq.u32 %p, %warp, 0;")
+    x(f"@%p bra {producer};")
+    x("setp.eq.u32 %p, %warp, 1;")
+    x(f"@%p bra {mma};")
+    x(f"setp.ge.u32 %p, %warp, {EPILOGUE_WARPS[0]};")
+    x(f"setp.le.u32 {r('q', pred)}, %warp, {EPILOGUE_WARPS[-1]};")
+    x("and.pred %p, %p, %q;")
+    x(f"@%p bra {epi};")
+    x(f"bra.uni {teardown};")
+
+    # --- producer: TMA loads into the stage ring ---------------------------------------------
+    x(f"{producer}:")
+    x("setp.ne.u32 %p, %lane, 0;")
+    x(f"@%p bra {teardown};")
+    for n in ("it", "s", "ph"):
+        x(f"mov.u32 {r(n)}, 0;")
+    x(f"mov.u32 {r('t')}, %cta;")
+    p_tile, p_k, p_drain, p_noempty = (x.label(h) for h in ("p_tile", "p_k", "p_drain",
+                                                            "p_noempty"))
+    x(f"{p_tile}:")
+    x(f"setp.ge.u32 %p, %t, {p.tiles};")
+    x(f"@%p bra {p_drain};")
+    sched_lookup()
+    x(f"shl.b32 {r('m0')}, %mt, 7;")
+    x(f"mul.lo.u32 {r('n0')}, %nt, {p.bn};")
+    x(f"mul.lo.u32 {r('kk')}, %st, {p.kc};")
+    x(f"mov.u32 {r('kb')}, 0;")
+    x(f"{p_k}:")
+    x(f"setp.lt.u32 %p, %it, {p.stages};")
+    x(f"@%p bra {p_noempty};")
+    x(f"mad.lo.u32 {r('ebar')}, %s, 8, %bars;")
+    x(f"add.u32 %ebar, %ebar, {empty};")
+    x(f"xor.b32 {r('par')}, %ph, 1;")
+    wait("%ebar", "%par", 1, p_drain)
+    x(f"{p_noempty}:")
+    x(f"mad.lo.u32 {r('fbar')}, %s, 8, %bars;")
+    x(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [%fbar], {p.stage_bytes};")
+    x(f"mad.lo.u32 {r('adst')}, %s, {a_stage}, %smem;")
+    x("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%adst], [%tmap_a, {%kk, %m0}], [%fbar];")
+    x(f"mad.lo.u32 {r('bdst')}, %s, {b_stage}, %smem;")
+    x(f"add.u32 %bdst, %bdst, {b_off};")
+    for cidx in range(p.bn // 64):
+        x(f"add.u32 {r('ncol')}, %n0, {cidx * 64};")
+        x(f"add.u32 {r('bdc')}, %bdst, {cidx * b_chunk};")
+        x("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+          "[%bdc], [%tmap_b, {%ncol, %kk}], [%fbar];")
+    advance_stage()
+    x(f"add.u32 %kk, %kk, {BK};")
+    x("add.u32 %kb, %kb, 1;")
+    x(f"setp.lt.u32 %p, %kb, {kb_count};")
+    x(f"@%p bra {p_k};")
+    x("add.u32 %t, %t, %ncta;")
+    x(f"bra.uni {p_tile};")
+    # drain: the loads of the last issued stages have landed before the CTA may exit
+    x(f"{p_drain}:")
+    for j in range(1, p.stages + 1):
+        skip = x.label("drain_skip")
+        x(f"setp.lt.u32 %p, %it, {j};")
+        x(f"@%p bra {skip};")
+        x(f"sub.u32 {r('db')}, %it, {j};")
+        x(f"rem.u32 {r('ds')}, %db, {p.stages};")
+        x(f"div.u32 {r('du')}, %db, {p.stages};")
+        x("and.b32 %du, %du, 1;")
+        x(f"mad.lo.u32 {r('dbar')}, %ds, 8, %bars;")
+        wait("%dbar", "%du", 5, teardown)
+        x(f"{skip}:")
+    x(f"bra.uni {teardown};")
+
+    # --- MMA issuer --------------------------------------------------------------------------
+    x(f"{mma}:")
+    x("setp.ne.u32 %p, %lane, 0;")
+    x(f"@%p bra {teardown};")
+    for n in ("it", "s", "ph", "tc", "ab", "aph"):
+        x(f"mov.u32 {r(n)}, 0;")
+    x("mov.u32 %t, %cta;")
+    x(f"mov.u32 {r('idesc')}, {idesc};")
+    m_tile, m_k, m_end, m_free = (x.label(h) for h in ("m_tile", "m_k", "m_end", "m_free"))
+    x(f"{m_tile}:")
+    x(f"setp.ge.u32 %p, %t, {p.tiles};")
+    x(f"@%p bra {m_end};")
+    x(f"setp.lt.u32 %p, %tc, {accs};")
+    x(f"@%p bra {m_free};")
+    x(f"mad.lo.u32 {r('tebar')}, %ab, 8, %bars;")
+    x(f"add.u32 %tebar, %tebar, {tempty};")
+    x("xor.b32 %par, %aph, 1;")
+    wait("%tebar", "%par", 3, m_end)
+    x(f"{m_free}:")
+    x("tcgen05.fence::after_thread_sync;")
+    x(f"mad.lo.u32 {r('dtm')}, %ab, {p.bn}, %tmem;")
+    x("mov.u32 %kb, 0;")
+    x(f"{m_k}:")
+    x("mad.lo.u32 %fbar, %s, 8, %bars;")
+    wait("%fbar", "%ph", 2, m_end)
+    x("tcgen05.fence::after_thread_sync;")
+    x(f"mad.lo.u32 {r('aaddr')}, %s, {a_stage}, %smem;")
+    x(f"mad.lo.u32 {r('baddr')}, %s, {b_stage}, %smem;")
+    x(f"add.u32 %baddr, %baddr, {b_off};")
+    x(f"shr.u32 {r('alo')}, %aaddr, 4;")
+    x("and.b32 %alo, %alo, 16383;")
+    x(f"or.b32 %alo, %alo, {1 << 16};")  # LBO field 1 (unused by a 128-byte swizzled K-major)
+    x(f"shr.u32 {r('blo')}, %baddr, 4;")
+    x("and.b32 %blo, %blo, 16383;")
+    x(f"or.b32 %blo, %blo, {b_lbo << 16};")
+    x(f"setp.ne.u32 {r('pacc', pred)}, %kb, 0;")
+    for kk in range(BK // UMMA_K):
+        # K step kk: A advances 32 bytes inside the swizzle row, B 16 rows of 128 bytes
+        x(f"add.u32 {r('alo_k')}, %alo, {kk * (UMMA_K * 2 >> 4)};")
+        x(f"add.u32 {r('blo_k')}, %blo, {kk * (UMMA_K * 128 >> 4)};")
+        x(f"mov.b64 {r('adesc', 'b64')}, {{%alo_k, {a_hi}}};")
+        x(f"mov.b64 {r('bdesc', 'b64')}, {{%blo_k, {b_hi}}};")
+        acc = "%pacc" if kk == 0 else r("ptrue", pred)
+        x(f"tcgen05.mma.cta_group::1.kind::f16 [%dtm], %adesc, %bdesc, %idesc, {acc};")
+    x("mad.lo.u32 %ebar, %s, 8, %bars;")
+    x(f"add.u32 %ebar, %ebar, {empty};")
+    x("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%ebar];")
+    advance_stage()
+    x("add.u32 %kb, %kb, 1;")
+    x(f"setp.lt.u32 %p, %kb, {kb_count};")
+    x(f"@%p bra {m_k};")
+    x(f"mad.lo.u32 {r('tfbar')}, %ab, 8, %bars;")
+    x(f"add.u32 %tfbar, %tfbar, {tfull};")
+    x("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%tfbar];")
+    advance_acc()
+    x("add.u32 %t, %t, %ncta;")
+    x(f"bra.uni {m_tile};")
+    x(f"{m_end}:")
+    x(f"add.u32 {r('dr')}, %bars, {drain};")
+    x("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%dr];")
+    wait("%dr", "0", 6, teardown)
+    x(f"bra.uni {teardown};")
+
+    # --- epilogue: TMEM -> registers -> C ------------------------------------------------------
+    x(f"{epi}:")
+    x(f"sub.u32 {r('quad')}, %warp, {EPILOGUE_WARPS[0]};")
+    x(f"shl.b32 {r('lanebase')}, %quad, 21;")  # TMEM lane (quad*32) in bits 16..31
+    for n in ("tc", "ab", "aph"):
+        x(f"mov.u32 %{n}, 0;")
+    x("mov.u32 %t, %cta;")
+    e_tile = x.label("e_tile")
+    x(f"{e_tile}:")
+    x(f"setp.ge.u32 %p, %t, {p.tiles};")
+    x(f"@%p bra {teardown};")
+    sched_lookup()
+    x("mad.lo.u32 %tfbar, %ab, 8, %bars;")
+    x(f"add.u32 %tfbar, %tfbar, {tfull};")
+    wait("%tfbar", "%aph", 4, teardown)
+    x("tcgen05.fence::after_thread_sync;")
+    # this thread's row of C and the accumulator's columns in TMEM
+    x("shl.b32 %m0, %mt, 7;")
+    x(f"mad.lo.u32 {r('row')}, %quad, 32, %lane;")
+    x("add.u32 %row, %row, %m0;")
+    x(f"mul.wide.u32 {r('crow', u64)}, %row, {p.n * 4};")
+    x(f"mul.lo.u32 %n0, %nt, {p.bn * 4};")
+    x(f"cvt.u64.u32 {r('ncol64', u64)}, %n0;")
+    x("add.s64 %crow, %crow, %ncol64;")
+    x("add.s64 %crow, %crow, %c_ptr;")
+    x(f"add.u32 {r('taddr')}, %tmem, %lanebase;")
+    x(f"mad.lo.u32 %taddr, %ab, {p.bn}, %taddr;")
+    vals = [r(f"v{i}", "b32") for i in range(32)]
+    for chunk in range(p.bn // 32):
+        x(f"add.u32 {r('tcol')}, %taddr, {chunk * 32};")
+        x(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(vals)}}}, [%tcol];")
+        x("tcgen05.wait::ld.sync.aligned;")
+        for j in range(8):
+            quad = ", ".join(vals[4 * j:4 * j + 4])
+            off = chunk * 128 + j * 16
+            if p.atomic:
+                x(f"red.global.add.v4.f32 [%crow+{off}], {{{quad}}};")
+            else:
+                x(f"st.global.v4.b32 [%crow+{off}], {{{quad}}};")
+    x("tcgen05.fence::before_thread_sync;")
+    x("mad.lo.u32 %tebar, %ab, 8, %bars;")
+    x(f"add.u32 %tebar, %tebar, {tempty};")
+    x("mbarrier.arrive.shared::cta.b64 _, [%tebar];")
+    advance_acc()
+    x("add.u32 %t, %t, %ncta;")
+    x(f"bra.uni {e_tile};")
+
+    # --- teardown ----------------------------------------------------------------------------
+    x(f"{teardown}:")
+    x("barrier.sync 0;")
+    x("setp.ne.u32 %p, %warp, 1;")
+    x("@%p bra $M_exit;")
+    x("bar.warp.sync -1;")
+    x("tcgen05.fence::after_thread_sync;")
+    x(f"tcgen05.dealloc.cta_group::1.sync.aligned.b32 %tmem, {tmem_cols};")
+    x("$M_exit:")
+    x("ret;")
+
+    # --- module ------------------------------------------------------------------------------
+    sched_words = []
+    for mt, nt, st in p.schedule:
+        if mt >= 2048 or nt >= 2048 or st >= 1024:
+            raise NotImplementedError("matmul template: more tiles than the schedule encodes")
+        sched_words.append(str(mt | (nt << 11) | (st << 22)))
+    rows = [", ".join(sched_words[i:i + 16]) for i in range(0, len(sched_words), 16)]
+    params = ",\n".join(f"\t.param .u64 {e}_param_{q}" for q in p.params)
+    decls = "\n".join(f"\t.reg .{t} %m_{n};" for n, t in x.regs.items())
+    esz = 2
+    head = [
+        "//\n// Generated by ptxgen (B200 backend): tcgen05 GEMM template\n//",
+        f"// @ptxgen launch grid={p.tiles} block={p.block} persistent=1",
+        f"// @ptxgen dynamic_smem={smem_total}",
+        f"// @ptxgen tensormap symbol={e}_tmap_a buffer={p.a} dtype={p.dtype} "
+        f"dims={p.k},{p.m} strides={p.k * esz} box={BK},{BM} swizzle=128",
+        f"// @ptxgen tensormap symbol={e}_tmap_b buffer={p.b} dtype={p.dtype} "
+        f"dims={p.n},{p.k} strides={p.n * esz} box=64,{BK} swizzle=128",
+        f"// @ptxgen matmul m={p.m} n={p.n} k={p.k} bn={p.bn} splits={p.splits} "
+        f"stages={p.stages} tiles={p.tiles}",
+        "",
+        f".version {PTX_VERSION}\n.target {TARGET}\n.address_size 64\n",
+        ".extern .shared .align 1024 .b8 smem_pool[];",
+        f".global .align 64 .b8 {e}_tmap_a[128];",
+        f".global .align 64 .b8 {e}_tmap_b[128];",
+        ".global .align 4 .u32 ptxgen_status;",
+        f".global .align 4 .u32 {e}_sched[{len(sched_words)}] = {{\n\t"
+        + ",\n\t".join(rows) + "\n};",
+        "",
+        f".visible .entry {e}(\n{params}\n)\n.maxntid {p.block}, 1, 1\n.minnctapersm 1\n{{",
+        decls,
+    ]
+    return "\n".join(head + x.finish() + ["}", ""])
