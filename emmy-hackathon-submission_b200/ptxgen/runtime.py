@@ -226,7 +226,7 @@ class Problem:
     meta: dict[str, Any]
     ptx: str = ""
     flags: dict[str, bool] = field(default_factory=dict)
-    device: int = 0
+    device: int | None = None  # None: the current CUDA device when first used
     _module: Module | None = None
     _kernel: Kernel | None = None
     _launch: dict[str, Any] | None = None
@@ -259,8 +259,16 @@ class Problem:
                               templates=not self.flags.get("no_templates", False))
         return self.ptx
 
+    def _dev(self) -> int:
+        if self.device is None:
+            import torch
+
+            self.device = torch.cuda.current_device()
+        return self.device
+
     def load(self) -> Kernel:
         if self._kernel is None:
+            self._dev()
             self._module = Module(self.compile(), self.device)
             self._kernel = self._module.kernel(self.launch_entry["entry"])
         return self._kernel
@@ -277,7 +285,7 @@ class Problem:
         if m.persistent and m.grid is not None:
             import torch
 
-            sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+            sms = torch.cuda.get_device_properties(self._dev()).multi_processor_count
             return max(1, min(m.grid, sms))
         return int(self.launch_entry["grid"][0])
 
@@ -289,7 +297,7 @@ class Problem:
         for a in self.launch_entry["args"]:
             n = int(np.prod(a["shape"]))
             out[a["name"]] = torch.empty(n + extra_guard, dtype=torch_dtype(a["dtype"]),
-                                         device=f"cuda:{self.device}")
+                                         device=f"cuda:{self._dev()}")
         return out
 
     def launch(self, tensors: dict[str, Any], stream: int | None = None, zero: bool = True,
@@ -299,7 +307,7 @@ class Problem:
         launch = self.launch_entry
         kernel = self.load()
         if stream is None:
-            stream = torch.cuda.current_stream(self.device).cuda_stream
+            stream = torch.cuda.current_stream(self._dev()).cuda_stream
         ptrs = {name: t.data_ptr() for name, t in tensors.items()}
         self.module.fill_tensormaps(ptrs)
         if zero:
@@ -312,7 +320,7 @@ class Problem:
         kernel.launch(self.grid(), launch["block"][0], int(launch.get("smem_bytes", 0)),
                       [ptrs[n] for n in launch["arg_order"]], stream)
         if check_status:
-            torch.cuda.synchronize(self.device)
+            torch.cuda.synchronize(self._dev())
             status = self.module.status()
             if status:
                 raise KernelStatusError(f"{launch['entry']}: status word 0x{status:08x}")

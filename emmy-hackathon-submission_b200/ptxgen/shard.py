@@ -9,16 +9,21 @@ contiguous share of it, with no collective on the data path:
   (split-K also splits further along K inside the rank so every rank keeps the same number of
   CTAs);
 * full sum: the element axis splits; each rank reduces its share to one partial, and the only
-  collective of the whole path, one NCCL all-reduce of those partials, combines them.
+  collective of the whole path, one all-reduce of those partials, combines them.
 
-``local_problem`` returns the rank's Kernel IR problem and the combine step; every rank's problem
-has the same shape, so each rank compiles the same module.
+``local_problem`` returns the rank's Plan: its Kernel IR problem (every rank's has the same
+shape, so each rank compiles the same module), which arguments are split along their first axis
+(``sharded``), and which outputs are summed across ranks (``allreduce``). ``slice_inputs`` and
+``combine`` apply that contract to concrete arrays.
 """
 
 from __future__ import annotations
 
 from collections.abc import Callable
-from dataclasses import dataclass
+from dataclasses import dataclass, field
+from typing import Any
+
+import numpy as np
 
 from . import problems
 from .problems import ProblemSpec
@@ -29,83 +34,104 @@ class Plan:
     name: str
     world: int
     spec: ProblemSpec
-    allreduce: tuple[str, ...] = ()  # outputs all-reduced (summed) across ranks after the kernel
+    sharded: tuple[str, ...] = ()  # arguments split along their first axis, rank-contiguous
+    allreduce: tuple[str, ...] = ()  # outputs summed across ranks after the kernel
     units: str = "bytes"  # what ``work`` counts: "bytes" (HBM) or "flops" (tensor)
     work: int = 0  # algorithmic bytes or flops of one rank's step
+    extra: dict[str, Any] = field(default_factory=dict)
+
+    def slice_inputs(self, full: dict[str, np.ndarray], rank: int) -> dict[str, np.ndarray]:
+        """This rank's input arrays, cut from the whole problem's."""
+        out = {}
+        for name, arr in full.items():
+            if name in self.sharded:
+                n = arr.shape[0] // self.world
+                out[name] = arr[rank * n:(rank + 1) * n]
+            else:
+                out[name] = arr
+        return out
+
+    def combine(self, local: dict[str, np.ndarray], group: Any = None) -> dict[str, np.ndarray]:
+        """Finish a rank's outputs: all-reduce (sum) the ``allreduce`` ones across ``group``
+        (a torch.distributed group; None is the default group). Sharded outputs stay local."""
+        if not self.allreduce or self.world == 1:
+            return local
+        import torch
+        import torch.distributed as dist
+
+        out = dict(local)
+        for name in self.allreduce:
+            t = torch.from_numpy(np.ascontiguousarray(local[name]))
+            dist.all_reduce(t, group=group)
+            out[name] = t.numpy()
+        return out
 
 
-def _bytes(c: int) -> int:
-    return c
+SIZES: dict[str, tuple[int, ...]] = {
+    "c1_vector_add": (1 << 24,), "c2_gelu_chain": (8192, 8192), "c3_row_softmax": (16384, 4096),
+    "c4_full_sum": (1 << 30,), "c5_matmul": (8192, 8192, 8192),
+    "c5b_matmul_splitk": (1024, 1024, 65536),
+}
 
 
-SIZES = {"c1_vector_add": 1 << 24, "c2_gelu_chain": (8192, 8192), "c3_row_softmax": (16384, 4096),
-         "c4_full_sum": 1 << 30, "c5_matmul": (8192, 8192, 8192),
-         "c5b_matmul_splitk": (1024, 1024, 65536)}
-
-
-def _check_split(total: int, world: int, what: str) -> int:
+def _split(total: int, world: int, what: str) -> int:
     if total % world:
         raise ValueError(f"{what} of {total} does not split over {world} ranks")
     return total // world
 
 
-BUILDERS: dict[str, Callable[[int], Plan]] = {}
+def _c1(world: int, size: tuple[int, ...]) -> Plan:
+    n = _split(size[0], world, "elements")
+    return Plan("c1_vector_add", world, problems.pointwise_add(n), ("x", "y", "add"),
+                work=12 * n)
 
 
-def _register(name: str) -> Callable[[Callable[[int], Plan]], Callable[[int], Plan]]:
-    def deco(fn: Callable[[int], Plan]) -> Callable[[int], Plan]:
-        BUILDERS[name] = fn
-        return fn
-    return deco
-
-
-@_register("c1_vector_add")
-def _c1(world: int) -> Plan:
-    n = _check_split(SIZES["c1_vector_add"], world, "elements")
-    return Plan("c1_vector_add", world, problems.pointwise_add(n), work=12 * n)
-
-
-@_register("c2_gelu_chain")
-def _c2(world: int) -> Plan:
-    rows, cols = SIZES["c2_gelu_chain"]
-    r = _check_split(rows, world, "rows")
-    return Plan("c2_gelu_chain", world, problems.gelu_chain(r, cols),
+def _c2(world: int, size: tuple[int, ...]) -> Plan:
+    rows, cols = size
+    r = _split(rows, world, "rows")
+    return Plan("c2_gelu_chain", world, problems.gelu_chain(r, cols), ("x", "s", "mul_1"),
                 work=4 * r * cols + 4 * r + 8)
 
 
-@_register("c3_row_softmax")
-def _c3(world: int) -> Plan:
-    rows, cols = SIZES["c3_row_softmax"]
-    r = _check_split(rows, world, "rows")
-    return Plan("c3_row_softmax", world, problems.row_softmax(r, cols), work=8 * r * cols)
+def _c3(world: int, size: tuple[int, ...]) -> Plan:
+    rows, cols = size
+    r = _split(rows, world, "rows")
+    return Plan("c3_row_softmax", world, problems.row_softmax(r, cols), ("x", "softmax"),
+                work=8 * r * cols)
 
 
-@_register("c4_full_sum")
-def _c4(world: int) -> Plan:
-    n = _check_split(SIZES["c4_full_sum"], world, "elements")
-    return Plan("c4_full_sum", world, problems.full_sum(n), allreduce=("sum_1",), work=4 * n + 4)
+def _c4(world: int, size: tuple[int, ...]) -> Plan:
+    n = _split(size[0], world, "elements")
+    blocks = 148 * 8 if n >= (1 << 24) else max(1, min(148 * 8, n // (256 * 16)))
+    return Plan("c4_full_sum", world, problems.full_sum(n, blocks=blocks), ("x",),
+                allreduce=("sum_1",), work=4 * n + 4)
 
 
-@_register("c5_matmul")
-def _c5(world: int) -> Plan:
-    m, n, k = SIZES["c5_matmul"]
-    ml = _check_split(m, world, "rows of A")
-    return Plan("c5_matmul", world, problems.matmul(ml, n, k), units="flops",
+def _c5(world: int, size: tuple[int, ...]) -> Plan:
+    m, n, k = size
+    ml = _split(m, world, "rows of A")
+    return Plan("c5_matmul", world, problems.matmul(ml, n, k), ("x0", "matmul"), units="flops",
                 work=2 * ml * n * k)
 
 
-@_register("c5b_matmul_splitk")
-def _c5b(world: int) -> Plan:
-    m, n, k = SIZES["c5b_matmul_splitk"]
-    ml = _check_split(m, world, "rows of A")
-    split = 4 * (m // ml) if (m // ml) * 4 * 64 <= k else 4
+def _c5b(world: int, size: tuple[int, ...]) -> Plan:
+    m, n, k = size
+    ml = _split(m, world, "rows of A")
+    split = 4 * world if k % (4 * world * 64) == 0 else 4
     return Plan("c5b_matmul_splitk", world,
                 problems.matmul(ml, n, k, split_k=split, raster_group=None),
-                units="flops", work=2 * ml * n * k)
+                ("x0", "matmul"), units="flops", work=2 * ml * n * k)
 
 
-def local_problem(name: str, world: int = 1) -> Plan:
-    """The problem one of ``world`` ranks runs for configuration ``name``."""
+BUILDERS: dict[str, Callable[[int, tuple[int, ...]], Plan]] = {
+    "c1_vector_add": _c1, "c2_gelu_chain": _c2, "c3_row_softmax": _c3, "c4_full_sum": _c4,
+    "c5_matmul": _c5, "c5b_matmul_splitk": _c5b,
+}
+
+
+def local_problem(name: str, world: int = 1, size: tuple[int, ...] | None = None) -> Plan:
+    """The plan one of ``world`` ranks runs for configuration ``name`` (at its benchmark size,
+    or at ``size``)."""
     if name not in BUILDERS:
         raise KeyError(f"unknown configuration {name!r} (have {', '.join(BUILDERS)})")
-    return BUILDERS[name](world)
+    return BUILDERS[name](world, tuple(size) if size is not None else SIZES[name])
