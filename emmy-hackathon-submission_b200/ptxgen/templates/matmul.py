@@ -31,7 +31,7 @@ a table. Tensor maps live in module ``.global`` symbols that the launcher fills
 parameters stay the plain device pointers of meta.json's arg_order. Every mbarrier wait is
 bounded by ``%globaltimer``; a wait that runs out sets a bit of the module's ``ptxgen_status``
 word, and the kernel winds down: the producer waits (bounded) for its own TMA loads to land, the
-MMA thread for its MMAs, then TMEM is freed. No load uses cluster multicast.
+MMA thread for its MMAs, then TMEM is freed. Every CTA loads its own tiles.
 """
 
 from __future__ import annotations

@@ -43,8 +43,20 @@ def test_shipped_compiles_and_assembles(name: str, flags: dict, tmp_path) -> Non
     graph, meta = shipped(name)
     ptx = to_ptx(Graph.from_dict(graph), meta, **flags)
     assert ".target sm_100a" in ptx
-    assert ".multicast::cluster" not in ptx
+    assert_plain_tma(ptx)
     ptxas(ptx, tmp_path)
+
+
+# The one form of TMA load the kernels may issue: each CTA fills its own shared memory.
+TMA_LOAD = re.compile(r"^\s*cp\.async\.bulk\.tensor\.2d\.shared::cluster\.global\.tile"
+                      r"\.mbarrier::complete_tx::bytes \[%\w+\], \[%\w+, \{%\w+, %\w+\}\], "
+                      r"\[%\w+\];$")
+
+
+def assert_plain_tma(ptx: str) -> None:
+    for line in ptx.splitlines():
+        if "cp.async.bulk" in line:
+            assert TMA_LOAD.match(line), f"unexpected bulk-copy form: {line.strip()}"
 
 
 SMALL = {
@@ -60,6 +72,7 @@ SMALL = {
 @pytest.mark.parametrize("key", sorted(SMALL))
 def test_configs_assemble(key: str, tmp_path) -> None:
     ptx = compile_spec(SMALL[key]())
+    assert_plain_tma(ptx)
     info = ptxas(ptx, tmp_path)
     assert "spill" in info
 
@@ -158,3 +171,14 @@ def test_unsupported_node_raises() -> None:
                                                                  "swizzle='XOR'")
     with pytest.raises(NotImplementedError):
         to_ptx(Graph.from_dict(graph), meta)
+
+
+def test_gemm_uses_the_tcgen05_template() -> None:
+    ptx = compile_spec(problems.CONFIGS["c5_matmul"]())
+    assert "tcgen05.mma.cta_group::1.kind::f16" in ptx and "tcgen05.alloc" in ptx
+    assert ptx.count("cp.async.bulk.tensor") == 1 + 256 // 64  # one A and four B loads a stage
+    assert "// @ptxgen tensormap symbol=" in ptx and "persistent=1" in ptx
+    assert_plain_tma(ptx)
+    generic = to_ptx(Graph.from_dict(problems.matmul(256, 256, 256).graph),
+                     problems.matmul(256, 256, 256).meta, templates=False)
+    assert "tcgen05" not in generic and "cp.async.cg.shared.global" in generic
