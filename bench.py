@@ -46,12 +46,24 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--workload", default=DEFAULT_WORKLOAD)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--no-extras", action="store_true", help="skip the other configurations")
+    p.add_argument("--scaling", choices=("weak", "strong"), default="weak",
+                   help="weak: each GPU keeps a full benchmark-sized share of an N-times larger "
+                        "problem; strong: the GPUs split the benchmark size")
     p.add_argument("--cpu-seconds", type=float, default=12.0,
                    help="target seconds of CPU work for the CPU baseline sample")
     return p.parse_args()
 
 
 # --- distributed plumbing ----------------------------------------------------------------------
+
+
+_T0 = time.perf_counter()
+
+
+def log(msg: str) -> None:
+    """Progress on stderr (stdout carries only the JSON line)."""
+    rank = os.environ.get("RANK", "0")
+    print(f"[bench r{rank} {time.perf_counter() - _T0:7.1f}s] {msg}", file=sys.stderr, flush=True)
 
 
 def dist_env() -> tuple[int, int, int]:
@@ -356,6 +368,7 @@ def run_ours(args: argparse.Namespace) -> None:
     from ptxgen.runtime import init
 
     rank, world, local_rank = dist_env()
+    log(f"start: world {world}, local rank {local_rank}, --gpus {args.gpus}")
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}: launch with torchrun")
     torch.cuda.set_device(local_rank)
@@ -370,7 +383,8 @@ def run_ours(args: argparse.Namespace) -> None:
     pk, pk_kind = peaks()
 
     def one(name: str, steps: int, warmup: int, with_e2e: bool) -> dict[str, Any]:
-        plan = shard.local_problem(name, world)
+        log(f"{name}: compile and inputs")
+        plan = shard.local_problem(name, world, weak=args.scaling == "weak")
         unit, bound, scale = unit_of(plan)
         m = measure_kernel(plan, steps, warmup, world)
         per_rank = plan.work / (m["mean_ms"] / 1e3) / scale
@@ -384,6 +398,7 @@ def run_ours(args: argparse.Namespace) -> None:
                            "unit": unit, "frac": per_rank / peak,
                            "traffic": traffic, "peak_source": pk_kind,
                            "algorithmic_per_launch": plan.work}
+        log(f"{name}: {res['ms_per_step']:.4f} ms per step, {res['value']:.1f} {unit}")
         if with_e2e:
             e = measure_e2e(plan, m["prob"], m["tensors"], max(3, min(steps, 20)), world)
             res["e2e"] = {"value": plan.work * world / e["mean_s"] / scale, "unit": unit,
@@ -404,15 +419,16 @@ def run_ours(args: argparse.Namespace) -> None:
                                                  "roofline")})
             except Exception as e:  # noqa: BLE001 - report and continue
                 extras.append({"workload": name, "error": f"{type(e).__name__}: {e}"[:300]})
+    log("measurements done")
     if rank != 0:
         return
-    plan = shard.local_problem(args.workload, world)
+    plan = shard.local_problem(args.workload, world, weak=args.scaling == "weak")
     cpu = cpu_baseline(args.workload, plan, args.cpu_seconds) if world == 1 else None
     line = {
         "metric": "Kernel time: HBM GB/s (% of ~8 TB/s), GEMM TFLOPS (% peak) at 1/2/4/8 B200",
         "value": head["value"], "unit": head["unit"], "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": _dtype(args.workload),
+        "scaling": args.scaling, "vs_baseline": None, "dtype": _dtype(args.workload),
         "data": "synthetic (seeded, the configuration's distributions, generated on the GPU)",
         "config": {"workload": args.workload, "per_rank": plan.spec.meta["id"],
                    "parallelism": f"tile-axis x{world}" if world > 1 else "single GPU",

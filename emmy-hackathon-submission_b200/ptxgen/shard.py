@@ -11,6 +11,9 @@ contiguous share of it, with no collective on the data path:
 * full sum: the element axis splits; each rank reduces its share to one partial, and the only
   collective of the whole path, one all-reduce of those partials, combines them.
 
+The benchmark scales weakly: each rank keeps a benchmark-sized share of a problem ``world``
+times larger along the split axis (``weak=True``); strong scaling splits the benchmark size.
+
 ``local_problem`` returns the rank's Plan: its Kernel IR problem (every rank's has the same
 shape, so each rank compiles the same module), which arguments are split along their first axis
 (``sharded``), and which outputs are summed across ranks (``allreduce``). ``slice_inputs`` and
@@ -117,7 +120,11 @@ def _c5(world: int, size: tuple[int, ...]) -> Plan:
 def _c5b(world: int, size: tuple[int, ...]) -> Plan:
     m, n, k = size
     ml = _split(m, world, "rows of A")
-    split = 4 * world if k % (4 * world * 64) == 0 else 4
+    # four K splits per 1024 rows, more when a rank holds fewer rows, so each rank keeps enough
+    # CTAs to fill its SMs
+    split = 4 * max(1, 1024 // ml)
+    if k % (split * 64):
+        split = 4
     return Plan("c5b_matmul_splitk", world,
                 problems.matmul(ml, n, k, split_k=split, raster_group=None),
                 ("x0", "matmul"), units="flops", work=2 * ml * n * k)
@@ -129,9 +136,15 @@ BUILDERS: dict[str, Callable[[int, tuple[int, ...]], Plan]] = {
 }
 
 
-def local_problem(name: str, world: int = 1, size: tuple[int, ...] | None = None) -> Plan:
-    """The plan one of ``world`` ranks runs for configuration ``name`` (at its benchmark size,
-    or at ``size``)."""
+def local_problem(name: str, world: int = 1, size: tuple[int, ...] | None = None,
+                  weak: bool = False) -> Plan:
+    """The plan one of ``world`` ranks runs for configuration ``name``. ``size`` is the whole
+    problem (default: the benchmark size). With ``weak`` the whole problem is ``world`` times
+    that size along the sharded axis, so each rank keeps a benchmark-sized share (weak scaling);
+    otherwise the ranks split the given size (strong scaling)."""
     if name not in BUILDERS:
         raise KeyError(f"unknown configuration {name!r} (have {', '.join(BUILDERS)})")
-    return BUILDERS[name](world, tuple(size) if size is not None else SIZES[name])
+    whole = tuple(size) if size is not None else SIZES[name]
+    if weak:
+        whole = (whole[0] * world, *whole[1:])
+    return BUILDERS[name](world, whole)
