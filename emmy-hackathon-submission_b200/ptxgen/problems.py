@@ -159,7 +159,7 @@ GELU_C = 0.044715
 GELU_K = math.sqrt(2.0 / math.pi)
 
 
-def gelu_chain(rows: int = 8192, cols: int = 8192, block: int = 256, unroll: int = 8,
+def gelu_chain(rows: int = 8192, cols: int = 8192, block: int = 256, unroll: int = 16,
                a: float | None = None, b: float | None = None) -> ProblemSpec:
     """y = gelu_tanh(a*x + b) * s[row] over a [rows, cols] bf16 x, computed in f32, y bf16."""
     rng = np.random.default_rng(1234)

@@ -307,9 +307,14 @@ class Kernel:
 
     # --- rendering --------------------------------------------------------------------
     def render(self) -> str:
+        from .slp import SLP
+
         self.drop_dead()
         self.vectorize()
         self.drop_dead()
+        if not self.no_cse:  # pairing reuses values across copies, as CSE does
+            self.body = SLP(self).run(self.body)
+            self.drop_dead()
         params = ",\n".join(f"\t.param .u64 {self.name}_param_{p}" for p in self.params)
         decls = []
         classes = {reg_class(t) for t in ("pred", "b16", "b32", "b64", "f32", "f64")}

@@ -95,16 +95,29 @@ def test_tail_guard_only_when_needed() -> None:
 
 
 def test_gelu_packs_bf16_128_bit() -> None:
-    ptx = compile_spec(problems.gelu_chain(64, 256))
+    ptx = compile_spec(problems.gelu_chain(64, 256, unroll=8))
     assert ptx.count("ld.global.nc.v4.b32") == 1 and ptx.count("st.global.v4.b32") == 1
     assert ptx.count("ld.global.nc.f32") == 3  # a, b and one s[row] for all eight elements
     assert "fma.rn.f32" in ptx and "ex2.approx.ftz.f32" in ptx
 
 
 def test_gelu_no_fusion_flag() -> None:
-    ptx = compile_spec(problems.gelu_chain(64, 256), no_fusion=True)
-    assert "fma.rn.f32" not in ptx.replace("fma.rn.f32 %f", "") or \
-        ptx.count("fma.rn.f32") == ptx.count("rcp.approx")  # only tanh's own fma remains
+    """Without fusion only tanh's own fma remains: one per element, against three with it
+    (a*x + b and u + c*u^3 fuse)."""
+    spec = problems.gelu_chain(64, 256, unroll=8)
+    fused, plain = compile_spec(spec), compile_spec(spec, no_fusion=True)
+
+    def fma_lanes(ptx: str) -> int:
+        return 2 * ptx.count("fma.rn.f32x2") + len(re.findall(r"fma\.rn\.f32 ", ptx))
+
+    assert fma_lanes(plain) == plain.count("rcp.approx") == 8
+    assert fma_lanes(fused) == 3 * 8
+
+
+def test_gelu_pairs_arithmetic_into_f32x2() -> None:
+    ptx = compile_spec(problems.gelu_chain(64, 256, unroll=16))
+    assert ptx.count(".f32x2") >= 16 * 10 // 2
+    assert not re.search(r"\b(add|sub|mul|fma)\.rn\.f32 ", ptx)  # no scalar f32 arithmetic left
 
 
 def test_softmax_reads_each_row_once() -> None:
