@@ -25,8 +25,16 @@ i * nctaid``, so any grid size computes every tile once):
   accumulator, stores into C (``red.global.add.v4.f32`` for split-K), then ``tmem_empty``; with
   two accumulators the epilogue of one tile overlaps the MMAs of the next.
 
-The tile order is the IR's own block order (its raster groups included), baked into the module as
-a table. Tensor maps live in module ``.global`` symbols that the launcher fills
+The work is a table of segments baked into the module: (m tile, n tile, first K block, K-block
+count), and CTA ``c`` takes entries ``c, c + nctaid, ...``. A plain GEMM has one whole-K segment
+per output tile in the IR's own block order (its raster groups included). A split-K GEMM (C
+zeroed, partials added with ``red.global.add``) takes its own split count instead of the IR's:
+the one that finishes soonest on ``SM_COUNT`` SMs, counting waves of CTAs times K blocks per
+split plus ``SEGMENT_COST`` per segment for its epilogue (for 32 tiles of 1024 K blocks: 9
+uneven splits, 288 segments in two full waves, where the IR's 4 splits fill 128 of 148 SMs
+once). Segments go split-major, so the CTAs running at one time read the same few K windows of A
+and B and share them in L2. The sum is the IR's (every K block of every tile is added once into
+zeroed C); only the f32 association differs, as it does between atomic orders. Tensor maps live in module ``.global`` symbols that the launcher fills
 (``pg_tensormap_fill``), named in ``// @ptxgen tensormap`` header lines, so the kernel's
 parameters stay the plain device pointers of meta.json's arg_order. Every mbarrier wait is
 bounded by ``%globaltimer``; a wait that runs out sets a bit of the module's ``ptxgen_status``
@@ -49,6 +57,9 @@ BM, BK = 128, 64  # tile rows (the MMA's M) and K per stage (64 bf16 = one 128-b
 UMMA_K = 16
 MAX_STAGES = 6
 WAIT_NS = 2_000_000_000  # a bounded wait gives up after 2 s of %globaltimer
+SM_COUNT = 148  # B200: a split-K GEMM's split count is chosen for this many SMs
+MIN_SEGMENT = 8  # K blocks a split-K segment has at least
+SEGMENT_COST = 2  # a segment's epilogue, in K blocks of MMA time, when choosing the split count
 EPILOGUE_WARPS = (4, 5, 6, 7)
 BAR_BYTES = 8
 
@@ -82,6 +93,25 @@ class MatmulPlan:
     @property
     def stage_bytes(self) -> int:
         return (BM * BK + BK * self.bn) * 2
+
+    def segments(self) -> tuple[tuple[tuple[int, int, int, int], ...], int]:
+        """The kernel's work table, (m tile, n tile, first K block, K blocks) per entry, and the
+        grid it is laid out for."""
+        kbs = self.k // BK
+        if not self.atomic:
+            per = self.kc // BK
+            table = tuple((mt, nt, st * per, per) for mt, nt, st in self.schedule)
+            return table, len(table)
+        tiles = list(dict.fromkeys((mt, nt) for mt, nt, _ in self.schedule))
+        best = (math.inf, 1)
+        for splits in range(1, max(1, kbs // MIN_SEGMENT) + 1):
+            waves = -(-len(tiles) * splits // SM_COUNT)
+            best = min(best, (waves * (-(-kbs // splits) + SEGMENT_COST), splits))
+        splits = best[1]
+        cut = [j * kbs // splits for j in range(splits + 1)]
+        table = tuple((mt, nt, cut[j], cut[j + 1] - cut[j])
+                      for j in range(splits) for mt, nt in tiles)
+        return table, min(SM_COUNT, len(table))
 
 
 # --- matching ----------------------------------------------------------------------------------
@@ -363,7 +393,8 @@ def instr_desc(dtype: str, bn: int, a_mn_major: bool = False, b_mn_major: bool =
 def emit(p: MatmulPlan) -> str:
     e = p.entry
     x = _Text()
-    kb_count = p.kc // BK
+    table, ctas = p.segments()
+    entries = len(table)
     a_stage = BM * BK * 2  # 16 KiB
     b_chunk = BK * 64 * 2  # 8 KiB: 64 K rows x 64 columns
     b_stage = BK * p.bn * 2
@@ -393,14 +424,17 @@ def emit(p: MatmulPlan) -> str:
     def wait(bar_addr: str, parity: str, code: int, fail: str) -> None:
         bounded_wait(x, bar_addr, parity, code, fail)
 
-    def sched_lookup() -> None:
-        x(f"mul.wide.u32 {r('s_off', u64)}, %t, 4;")
+    def sched_lookup(skip: str) -> None:
+        """Entry %t of the table into %mt, %nt, %kb0, %cnt; an empty entry branches to skip."""
+        x(f"mul.wide.u32 {r('s_off', u64)}, %t, 8;")
         x(f"add.s64 %s_off, {r('sched', u64)}, %s_off;")
-        x(f"ld.global.nc.u32 {r('code')}, [%s_off];")
-        x(f"and.b32 {r('mt')}, %code, 2047;")
-        x(f"shr.u32 {r('nt')}, %code, 11;")
-        x(f"and.b32 %nt, %nt, 2047;")
-        x(f"shr.u32 {r('st')}, %code, 22;")
+        x(f"ld.global.nc.v2.u32 {{{r('code')}, {r('code2')}}}, [%s_off];")
+        x(f"and.b32 {r('mt')}, %code, 65535;")
+        x(f"shr.u32 {r('nt')}, %code, 16;")
+        x(f"and.b32 {r('kb0')}, %code2, 65535;")
+        x(f"shr.u32 {r('cnt')}, %code2, 16;")
+        x("setp.eq.u32 %p, %cnt, 0;")
+        x(f"@%p bra {skip};")
 
     def advance_stage() -> None:
         x("add.u32 %it, %it, 1;")
@@ -479,15 +513,15 @@ def emit(p: MatmulPlan) -> str:
     for n in ("it", "s", "ph"):
         x(f"mov.u32 {r(n)}, 0;")
     x(f"mov.u32 {r('t')}, %cta;")
-    p_tile, p_k, p_drain, p_noempty = (x.label(h) for h in ("p_tile", "p_k", "p_drain",
-                                                            "p_noempty"))
+    p_tile, p_k, p_drain, p_noempty, p_next = (
+        x.label(h) for h in ("p_tile", "p_k", "p_drain", "p_noempty", "p_next"))
     x(f"{p_tile}:")
-    x(f"setp.ge.u32 %p, %t, {p.tiles};")
+    x(f"setp.ge.u32 %p, %t, {entries};")
     x(f"@%p bra {p_drain};")
-    sched_lookup()
+    sched_lookup(p_next)
     x(f"shl.b32 {r('m0')}, %mt, 7;")
     x(f"mul.lo.u32 {r('n0')}, %nt, {p.bn};")
-    x(f"mul.lo.u32 {r('kk')}, %st, {p.kc};")
+    x(f"mul.lo.u32 {r('kk')}, %kb0, {BK};")
     x(f"mov.u32 {r('kb')}, 0;")
     x(f"{p_k}:")
     x(f"setp.lt.u32 %p, %it, {p.stages};")
@@ -512,8 +546,9 @@ def emit(p: MatmulPlan) -> str:
     advance_stage()
     x(f"add.u32 %kk, %kk, {BK};")
     x("add.u32 %kb, %kb, 1;")
-    x(f"setp.lt.u32 %p, %kb, {kb_count};")
+    x("setp.lt.u32 %p, %kb, %cnt;")
     x(f"@%p bra {p_k};")
+    x(f"{p_next}:")
     x("add.u32 %t, %t, %ncta;")
     x(f"bra.uni {p_tile};")
     # drain: the loads of the last issued stages have landed before the CTA may exit
@@ -539,10 +574,12 @@ def emit(p: MatmulPlan) -> str:
         x(f"mov.u32 {r(n)}, 0;")
     x("mov.u32 %t, %cta;")
     x(f"mov.u32 {r('idesc')}, {idesc};")
-    m_tile, m_k, m_end, m_free = (x.label(h) for h in ("m_tile", "m_k", "m_end", "m_free"))
+    m_tile, m_k, m_end, m_free, m_next = (
+        x.label(h) for h in ("m_tile", "m_k", "m_end", "m_free", "m_next"))
     x(f"{m_tile}:")
-    x(f"setp.ge.u32 %p, %t, {p.tiles};")
+    x(f"setp.ge.u32 %p, %t, {entries};")
     x(f"@%p bra {m_end};")
+    sched_lookup(m_next)
     x(f"setp.lt.u32 %p, %tc, {accs};")
     x(f"@%p bra {m_free};")
     x(f"mad.lo.u32 {r('tebar')}, %ab, 8, %bars;")
@@ -580,12 +617,13 @@ def emit(p: MatmulPlan) -> str:
     x("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%ebar];")
     advance_stage()
     x("add.u32 %kb, %kb, 1;")
-    x(f"setp.lt.u32 %p, %kb, {kb_count};")
+    x("setp.lt.u32 %p, %kb, %cnt;")
     x(f"@%p bra {m_k};")
     x(f"mad.lo.u32 {r('tfbar')}, %ab, 8, %bars;")
     x(f"add.u32 %tfbar, %tfbar, {tfull};")
     x("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%tfbar];")
     advance_acc()
+    x(f"{m_next}:")
     x("add.u32 %t, %t, %ncta;")
     x(f"bra.uni {m_tile};")
     x(f"{m_end}:")
@@ -601,11 +639,11 @@ def emit(p: MatmulPlan) -> str:
     for n in ("tc", "ab", "aph"):
         x(f"mov.u32 %{n}, 0;")
     x("mov.u32 %t, %cta;")
-    e_tile = x.label("e_tile")
+    e_tile, e_next = x.label("e_tile"), x.label("e_next")
     x(f"{e_tile}:")
-    x(f"setp.ge.u32 %p, %t, {p.tiles};")
+    x(f"setp.ge.u32 %p, %t, {entries};")
     x(f"@%p bra {teardown};")
-    sched_lookup()
+    sched_lookup(e_next)
     x("mad.lo.u32 %tfbar, %ab, 8, %bars;")
     x(f"add.u32 %tfbar, %tfbar, {tfull};")
     wait("%tfbar", "%aph", 4, teardown)
@@ -638,6 +676,7 @@ def emit(p: MatmulPlan) -> str:
     x(f"add.u32 %tebar, %tebar, {tempty};")
     x("mbarrier.arrive.shared::cta.b64 _, [%tebar];")
     advance_acc()
+    x(f"{e_next}:")
     x("add.u32 %t, %t, %ncta;")
     x(f"bra.uni {e_tile};")
 
@@ -654,31 +693,31 @@ def emit(p: MatmulPlan) -> str:
 
     # --- module ------------------------------------------------------------------------------
     sched_words = []
-    for mt, nt, st in p.schedule:
-        if mt >= 2048 or nt >= 2048 or st >= 1024:
+    for mt, nt, kb0, cnt in table:
+        if max(mt, nt, kb0, cnt) >= 1 << 16:
             raise NotImplementedError("matmul template: more tiles than the schedule encodes")
-        sched_words.append(str(mt | (nt << 11) | (st << 22)))
+        sched_words += [str(mt | nt << 16), str(kb0 | cnt << 16)]
     rows = [", ".join(sched_words[i:i + 16]) for i in range(0, len(sched_words), 16)]
     params = ",\n".join(f"\t.param .u64 {e}_param_{q}" for q in p.params)
     decls = "\n".join(f"\t.reg .{t} %m_{n};" for n, t in x.regs.items())
     esz = 2
     head = [
         "//\n// Generated by ptxgen (B200 backend): tcgen05 GEMM template\n//",
-        f"// @ptxgen launch grid={p.tiles} block={p.block} persistent=1",
+        f"// @ptxgen launch grid={ctas} block={p.block} persistent=1",
         f"// @ptxgen dynamic_smem={smem_total}",
         f"// @ptxgen tensormap symbol={e}_tmap_a buffer={p.a} dtype={p.dtype} "
         f"dims={p.k},{p.m} strides={p.k * esz} box={BK},{BM} swizzle=128",
         f"// @ptxgen tensormap symbol={e}_tmap_b buffer={p.b} dtype={p.dtype} "
         f"dims={p.n},{p.k} strides={p.n * esz} box=64,{BK} swizzle=128",
         f"// @ptxgen matmul m={p.m} n={p.n} k={p.k} bn={p.bn} splits={p.splits} "
-        f"stages={p.stages} tiles={p.tiles}",
+        f"stages={p.stages} tiles={p.tiles} segments={entries}",
         "",
         f".version {PTX_VERSION}\n.target {TARGET}\n.address_size 64\n",
         ".extern .shared .align 1024 .b8 smem_pool[];",
         f".global .align 64 .b8 {e}_tmap_a[128];",
         f".global .align 64 .b8 {e}_tmap_b[128];",
         ".global .align 4 .u32 ptxgen_status;",
-        f".global .align 4 .u32 {e}_sched[{len(sched_words)}] = {{\n\t"
+        f".global .align 8 .u32 {e}_sched[{len(sched_words)}] = {{\n\t"
         + ",\n\t".join(rows) + "\n};",
         "",
         f".visible .entry {e}(\n{params}\n)\n.maxntid {p.block}, 1, 1\n.minnctapersm 1\n{{",

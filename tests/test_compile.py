@@ -195,3 +195,55 @@ def test_gemm_uses_the_tcgen05_template() -> None:
     generic = to_ptx(Graph.from_dict(problems.matmul(256, 256, 256).graph),
                      problems.matmul(256, 256, 256).meta, templates=False)
     assert "tcgen05" not in generic and "cp.async.cg.shared.global" in generic
+
+
+def gemm_plan(spec: problems.ProblemSpec):
+    from ptxgen.compiler import kernel_for_meta
+    from ptxgen.lower import Buffer
+    from ptxgen.templates import matmul
+
+    op, launch = kernel_for_meta(Graph.from_dict(spec.graph), spec.meta)
+    bufs = {a["name"]: Buffer(tuple(a["shape"]), a["dtype"],
+                              bool(a.get("output")) or a["name"] in op.outputs)
+            for a in launch["args"]}
+    return matmul.match(op, bufs, launch["arg_order"], launch["block"][0],
+                        int(launch.get("smem_bytes", 0)))
+
+
+@pytest.mark.parametrize("shape", [(8192, 8192, 8192, 1), (1024, 1024, 65536, 4),
+                                   (384, 512, 768, 3), (256, 256, 1024, 4),
+                                   (128, 1024, 65536, 32), (640, 768, 4096, 2)])
+def test_gemm_segments_cover_every_k_block_once(shape) -> None:
+    """The template's work table: every K block of every output tile exactly once; a plain GEMM
+    keeps the IR's tile order; a split-K GEMM goes split-major over the IR's tiles, with splits of
+    at least MIN_SEGMENT K blocks that differ by at most one, in as few waves of SM_COUNT CTAs as
+    its split count needs."""
+    from collections import Counter
+
+    from ptxgen.templates.matmul import BK, MIN_SEGMENT, SM_COUNT
+
+    m, n, k, split = shape
+    kw = {"split_k": split, "raster_group": None} if split > 1 else {}
+    p = gemm_plan(problems.matmul(m, n, k, **kw))
+    table, ctas = p.segments()
+    seen = Counter()
+    for mt, nt, kb0, cnt in table:
+        seen.update((mt, nt, kb) for kb in range(kb0, kb0 + cnt))
+    tiles = list(dict.fromkeys((mt, nt) for mt, nt, _ in p.schedule))
+    kbs = k // BK
+    assert set(seen) == {(mt, nt, kb) for mt, nt in tiles for kb in range(kbs)}
+    assert set(seen.values()) == {1}
+    if split == 1:
+        assert [(mt, nt) for mt, nt, _, _ in table] == [(mt, nt) for mt, nt, _ in p.schedule]
+        return
+    splits = len(table) // len(tiles)
+    assert [(mt, nt) for mt, nt, _, _ in table] == tiles * splits
+    counts = {cnt for _, _, _, cnt in table}
+    assert max(counts) - min(counts) <= 1 and min(counts) >= min(MIN_SEGMENT, kbs)
+    assert ctas == min(SM_COUNT, len(table))
+
+
+def test_splitk_config_fills_the_sms() -> None:
+    """Config 5b (32 tiles of 1024 K blocks): 9 splits, two full waves over 148 SMs."""
+    table, ctas = gemm_plan(problems.CONFIGS["c5b_matmul_splitk"]()).segments()
+    assert (len(table), ctas) == (288, 148)

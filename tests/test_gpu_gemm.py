@@ -47,6 +47,8 @@ CASES = {
     "raster_ragged": lambda: problems.matmul(1280, 512, 256, raster_group=4),
     "splitk4": lambda: problems.matmul(256, 256, 1024, split_k=4, raster_group=None),
     "splitk_odd": lambda: problems.matmul(384, 512, 768, split_k=3, raster_group=None),
+    # 8 tiles x 256 K blocks: the template's own 18 uneven splits (14 or 15 K blocks), 144 CTAs
+    "splitk_uneven": lambda: problems.matmul(512, 512, 16384, split_k=8, raster_group=None),
 }
 
 
