@@ -59,6 +59,7 @@ struct Driver {
                                    const cuuint32_t *, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion,
                                    CUtensorMapFloatOOBfill);
+  CUresult (*OccupancyMaxActiveClusters)(int *, CUfunction, const CUlaunchConfig *);
   CUresult (*GetErrorName)(CUresult, const char **);
   CUresult (*GetErrorString)(CUresult, const char **);
 };
@@ -99,6 +100,7 @@ int load_driver() {
   PG_SYM(StreamSynchronize, "cuStreamSynchronize")
   PG_SYM(CtxSynchronize, "cuCtxSynchronize")
   PG_SYM(TensorMapEncodeTiled, "cuTensorMapEncodeTiled")
+  PG_SYM(OccupancyMaxActiveClusters, "cuOccupancyMaxActiveClusters")
   PG_SYM(GetErrorName, "cuGetErrorName")
   PG_SYM(GetErrorString, "cuGetErrorString")
 #undef PG_SYM
@@ -235,6 +237,38 @@ int pg_kernel_launch(pg_kernel *kernel, uint32_t grid, uint32_t block, uint32_t 
   PG_CU(g_drv.LaunchKernel(kernel->fn, grid, 1, 1, block, 1, 1, smem_bytes,
                            reinterpret_cast<CUstream>(stream), args.data(), nullptr),
         "cuLaunchKernel");
+  return PG_OK;
+}
+
+int pg_kernel_max_clusters(pg_kernel *kernel, uint32_t block, uint32_t smem_bytes,
+                           uint32_t cluster, int *out) {
+  if (!kernel || !out || block == 0 || block > 1024 || cluster == 0 || cluster > 16)
+    return fail(PG_ERR_ARGUMENT, "pg_kernel_max_clusters: bad arguments");
+  int rc = ensure_current();
+  if (rc) return rc;
+  if (static_cast<int>(smem_bytes) > kernel->smem_optin) {
+    PG_CU(g_drv.FuncSetAttribute(kernel->fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
+                                 static_cast<int>(smem_bytes)),
+          "cuFuncSetAttribute(MAX_DYNAMIC_SHARED_SIZE_BYTES)");
+    kernel->smem_optin = static_cast<int>(smem_bytes);
+  }
+  CUlaunchAttribute attr;
+  std::memset(&attr, 0, sizeof attr);
+  attr.id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+  attr.value.clusterDim.x = cluster;
+  attr.value.clusterDim.y = 1;
+  attr.value.clusterDim.z = 1;
+  CUlaunchConfig cfg;
+  std::memset(&cfg, 0, sizeof cfg);
+  cfg.gridDimX = cluster;
+  cfg.gridDimY = cfg.gridDimZ = 1;
+  cfg.blockDimX = block;
+  cfg.blockDimY = cfg.blockDimZ = 1;
+  cfg.sharedMemBytes = smem_bytes;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  PG_CU(g_drv.OccupancyMaxActiveClusters(out, kernel->fn, &cfg),
+        "cuOccupancyMaxActiveClusters");
   return PG_OK;
 }
 

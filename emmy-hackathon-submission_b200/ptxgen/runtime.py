@@ -61,6 +61,7 @@ def library() -> ctypes.CDLL:
                 "pg_module_unload": [vp],
                 "pg_kernel_get": [vp, cp, ctypes.POINTER(vp)],
                 "pg_kernel_launch": [vp, u32, u32, u32, u64, pu64, i32],
+                "pg_kernel_max_clusters": [vp, u32, u32, u32, ctypes.POINTER(i32)],
                 "pg_tensormap_fill": [vp, cp, i32, i32, u64, pu64, pu64, pu32, i32],
                 "pg_status_take": [vp, pu32],
                 "pg_memset_async": [u64, ctypes.c_size_t, u64],
@@ -139,6 +140,8 @@ class Module:
         # a persistent kernel loops over its tiles (tile = ctaid + i * nctaid): any grid works,
         # and one CTA per SM is the right one
         self.persistent = launch.get("persistent") == "1"
+        # CTAs per cluster (the kernel's .reqnctapercluster): the grid is a multiple of it
+        self.cluster = int(launch.get("cluster", "1"))
         dyn = self.notes.get("dynamic_smem")
         self.dynamic_smem = int(dyn[0]) if dyn else 0
 
@@ -189,10 +192,21 @@ class Kernel:
         elif m.grid is not None and (grid, block) != (m.grid, m.block):
             raise LaunchError(f"{self.entry}: compiled for grid {m.grid} x block {m.block}, "
                               f"asked to launch {grid} x {block}")
+        if grid % m.cluster:
+            raise LaunchError(f"{self.entry}: grid {grid} is not a multiple of its cluster "
+                              f"size {m.cluster}")
         smem = max(smem, m.dynamic_smem)
         ptrs = (ctypes.c_uint64 * len(pointers))(*pointers)
         _check(library().pg_kernel_launch(self.handle, grid, block, smem, stream, ptrs,
                                           len(pointers)), f"pg_kernel_launch({self.entry})")
+
+    def max_clusters(self, block: int, smem: int) -> int:
+        """Clusters of this kernel that fit on the device at once."""
+        out = ctypes.c_int()
+        _check(library().pg_kernel_max_clusters(
+            self.handle, block, max(smem, self.module.dynamic_smem), self.module.cluster,
+            ctypes.byref(out)), f"pg_kernel_max_clusters({self.entry})")
+        return out.value
 
     def run_host(self, grid: int, block: int, smem: int, stream: int, dev: list[int],
                  host: list[int | None], nbytes: list[int], flags: list[int]) -> None:
@@ -230,6 +244,7 @@ class Problem:
     _module: Module | None = None
     _kernel: Kernel | None = None
     _launch: dict[str, Any] | None = None
+    _max_clusters: int | None = None
 
     @classmethod
     def from_dir(cls, path: str | Path, **flags: bool) -> Problem:
@@ -280,13 +295,20 @@ class Problem:
         return self._module
 
     def grid(self) -> int:
-        """meta.json's grid, or for a persistent kernel one CTA per SM (at most one per tile)."""
+        """meta.json's grid, or for a persistent kernel one CTA per SM (at most one per tile),
+        in whole clusters that can all be resident at once."""
         m = self.module
         if m.persistent and m.grid is not None:
             import torch
 
             sms = torch.cuda.get_device_properties(self._dev()).multi_processor_count
-            return max(1, min(m.grid, sms))
+            if m.cluster > 1:
+                if self._max_clusters is None:
+                    launch = self.launch_entry
+                    self._max_clusters = self.load().max_clusters(
+                        launch["block"][0], int(launch.get("smem_bytes", 0)))
+                sms = min(sms, self._max_clusters * m.cluster)
+            return max(m.cluster, min(m.grid, sms) // m.cluster * m.cluster)
         return int(self.launch_entry["grid"][0])
 
     def allocate(self, extra_guard: int = 0) -> dict[str, Any]:

@@ -81,6 +81,7 @@ class MatmulPlan:
     stages: int
     atomic: bool
     schedule: tuple[tuple[int, int, int], ...]  # (m tile, n tile, split) per tile index
+    pair: bool = False  # two CTAs (an SM pair) per 256-row tile, cta_group::2
 
     @property
     def kc(self) -> int:
@@ -98,20 +99,23 @@ class MatmulPlan:
         """The kernel's work table, (m tile, n tile, first K block, K blocks) per entry, and the
         grid it is laid out for."""
         kbs = self.k // BK
+        rows = 2 if self.pair else 1  # IR tiles (128 rows) per table tile
         if not self.atomic:
             per = self.kc // BK
-            table = tuple((mt, nt, st * per, per) for mt, nt, st in self.schedule)
-            return table, len(table)
-        tiles = list(dict.fromkeys((mt, nt) for mt, nt, _ in self.schedule))
+            table = tuple(dict.fromkeys((mt // rows, nt, st * per, per)
+                                        for mt, nt, st in self.schedule))
+            return table, len(table) * rows
+        tiles = list(dict.fromkeys((mt // rows, nt) for mt, nt, _ in self.schedule))
+        slots = SM_COUNT // rows
         best = (math.inf, 1)
         for splits in range(1, max(1, kbs // MIN_SEGMENT) + 1):
-            waves = -(-len(tiles) * splits // SM_COUNT)
+            waves = -(-len(tiles) * splits // slots)
             best = min(best, (waves * (-(-kbs // splits) + SEGMENT_COST), splits))
         splits = best[1]
         cut = [j * kbs // splits for j in range(splits + 1)]
         table = tuple((mt, nt, cut[j], cut[j + 1] - cut[j])
                       for j in range(splits) for mt, nt in tiles)
-        return table, min(SM_COUNT, len(table))
+        return table, min(slots, len(table)) * rows
 
 
 # --- matching ----------------------------------------------------------------------------------
@@ -245,8 +249,9 @@ def match(op: KernelOp, buffers: Mapping[str, Buffer], arg_order: Sequence[str],
     if stages < 2:
         return None
     sched = _schedule(t, block, mi, ni, si)
+    pair = bn == 256 and m % (2 * BM) == 0
     return MatmulPlan(op.name, tuple(arg_order), a_name, b_name, c, abuf.dtype, m, n, k, bn,
-                      splits, block, stages, atomic, sched)
+                      splits, block, stages, atomic, sched, pair)
 
 
 def _which_is_a(inner: Loop | StridedLoop, feeds: dict[str, str], loads: dict[str, str],
@@ -334,14 +339,16 @@ class _Text:
 
 
 def bounded_wait(x: _Text, bar_addr: str, parity: str, code: int, fail: str,
-                 limit_ns: int = WAIT_NS) -> None:
+                 limit_ns: int = WAIT_NS, sem: str = "") -> None:
     """An mbarrier wait that gives up: it polls ``try_wait.parity`` until the phase of
     ``parity`` completes or ``limit_ns`` of %globaltimer pass; then it sets bit ``code`` of the
-    module's ``ptxgen_status`` word and branches to ``fail``."""
+    module's ``ptxgen_status`` word and branches to ``fail``. ``sem`` is the wait's memory
+    order (``.acquire.cluster`` for a barrier another CTA of the cluster arrives at)."""
     top, ok = x.label("wait"), x.label("waited")
     x(f"mov.u64 {x.reg('w_t0', 'u64')}, %globaltimer;")
     x(f"{top}:")
-    x(f"mbarrier.try_wait.parity.shared::cta.b64 {x.reg('pw', 'pred')}, [{bar_addr}], {parity};")
+    x(f"mbarrier.try_wait.parity{sem}.shared::cta.b64 {x.reg('pw', 'pred')}, [{bar_addr}], "
+      f"{parity};")
     x(f"@%pw bra {ok};")
     x(f"mov.u64 {x.reg('w_t1', 'u64')}, %globaltimer;")
     x("sub.u64 %w_t1, %w_t1, %w_t0;")
@@ -381,13 +388,14 @@ def _desc_hi(sbo: int, swizzle128: bool = True) -> int:
     return (sbo >> 4) | (1 << 14) | ((2 if swizzle128 else 0) << 29)
 
 
-def instr_desc(dtype: str, bn: int, a_mn_major: bool = False, b_mn_major: bool = True) -> int:
+def instr_desc(dtype: str, bn: int, a_mn_major: bool = False, b_mn_major: bool = True,
+               m: int = BM) -> int:
     """The 32-bit instruction descriptor of tcgen05.mma.kind::f16: f32 accumulator (bit 4),
     A/B format bf16 = 1 or f16 = 0 (bits 7, 10), A/B major-ness (bits 15, 16: 1 = MN-major),
-    N >> 3 at bit 17, M >> 4 at bit 24."""
+    N >> 3 at bit 17, M >> 4 at bit 24 (M = 256 for a CTA pair's cta_group::2 MMA)."""
     fmt = 1 if dtype == "bf16" else 0
     return ((1 << 4) | (fmt << 7) | (fmt << 10) | (int(a_mn_major) << 15) |
-            (int(b_mn_major) << 16) | ((bn >> 3) << 17) | ((BM >> 4) << 24))
+            (int(b_mn_major) << 16) | ((bn >> 3) << 17) | ((m >> 4) << 24))
 
 
 def emit(p: MatmulPlan) -> str:
@@ -395,13 +403,18 @@ def emit(p: MatmulPlan) -> str:
     x = _Text()
     table, ctas = p.segments()
     entries = len(table)
+    pair = p.pair
+    g = 2 if pair else 1  # the tcgen05 cta_group
+    nb = p.bn // g  # B columns this CTA loads (a pair splits B by columns)
     a_stage = BM * BK * 2  # 16 KiB
     b_chunk = BK * 64 * 2  # 8 KiB: 64 K rows x 64 columns
-    b_stage = BK * p.bn * 2
-    b_off = p.stages * a_stage
-    bar_off = p.stages * (a_stage + b_stage)
-    full, empty = 0, p.stages * BAR_BYTES
-    tfull = 2 * p.stages * BAR_BYTES
+    b_stage = BK * nb * 2
+    stages = MAX_STAGES if pair else p.stages
+    stage_tx = g * (a_stage + b_stage)  # bytes the MMA's full barrier waits for
+    b_off = stages * a_stage
+    bar_off = stages * (a_stage + b_stage)
+    full, empty = 0, stages * BAR_BYTES
+    tfull = 2 * stages * BAR_BYTES
     tempty = tfull + 2 * BAR_BYTES
     drain = tempty + 2 * BAR_BYTES
     slot = drain + BAR_BYTES
@@ -412,7 +425,7 @@ def emit(p: MatmulPlan) -> str:
         # a CTA holding more than half of TMEM must be alone on its SM: ask for more than half
         # of the SM's shared memory
         smem_total = max(smem_total, 120 * 1024)
-    idesc = instr_desc(p.dtype, p.bn)
+    idesc = instr_desc(p.dtype, p.bn, m=g * BM)
     a_hi = _desc_hi(1024)  # K-major A: 8-row groups 1024 bytes apart
     b_hi = _desc_hi(1024)  # MN-major B: 8-row (K) groups 1024 bytes apart
     b_lbo = (BK * 128) >> 4  # MN-major B: 64-column swizzle atoms BK*128 bytes apart
@@ -421,8 +434,8 @@ def emit(p: MatmulPlan) -> str:
     u32, u64, pred = "u32", "u64", "pred"
     r = lambda n, t=u32: x.reg(n, t)  # noqa: E731
 
-    def wait(bar_addr: str, parity: str, code: int, fail: str) -> None:
-        bounded_wait(x, bar_addr, parity, code, fail)
+    def wait(bar_addr: str, parity: str, code: int, fail: str, sem: str = "") -> None:
+        bounded_wait(x, bar_addr, parity, code, fail, sem=sem)
 
     def sched_lookup(skip: str) -> None:
         """Entry %t of the table into %mt, %nt, %kb0, %cnt; an empty entry branches to skip."""
@@ -439,9 +452,18 @@ def emit(p: MatmulPlan) -> str:
     def advance_stage() -> None:
         x("add.u32 %it, %it, 1;")
         x("add.u32 %s, %s, 1;")
-        x(f"setp.eq.u32 {r('pwrap', pred)}, %s, {p.stages};")
+        x(f"setp.eq.u32 {r('pwrap', pred)}, %s, {stages};")
         x("@%pwrap mov.u32 %s, 0;")
         x("@%pwrap xor.b32 %ph, %ph, 1;")
+
+    def cta_sync() -> None:
+        """All threads of the CTA, or of both CTAs of a pair (whose barriers and TMEM the
+        other CTA uses), meet."""
+        if pair:
+            x("barrier.cluster.arrive.release;")
+            x("barrier.cluster.wait.acquire;")
+        else:
+            x("barrier.sync 0;")
 
     def advance_acc() -> None:
         x("add.u32 %tc, %tc, 1;")
@@ -455,8 +477,14 @@ def emit(p: MatmulPlan) -> str:
     x("cvta.to.global.u64 %c_ptr, %c_ptr;")
     x(f"mov.u32 {r('tid')}, %tid.x;")
     x(f"setp.eq.u32 {r('ptrue', pred)}, %tid, %tid;")
-    x(f"mov.u32 {r('cta')}, %ctaid.x;")
-    x(f"mov.u32 {r('ncta')}, %nctaid.x;")
+    if pair:  # a pair walks the table by cluster; rank 0 is the pair's leader
+        x(f"mov.u32 {r('rank')}, %cluster_ctarank;")
+        x(f"setp.eq.u32 {r('plead', pred)}, %rank, 0;")
+        x(f"mov.u32 {r('cta')}, %clusterid.x;")
+        x(f"mov.u32 {r('ncta')}, %nclusterid.x;")
+    else:
+        x(f"mov.u32 {r('cta')}, %ctaid.x;")
+        x(f"mov.u32 {r('ncta')}, %nctaid.x;")
     x(f"shr.u32 {r('warp')}, %tid, 5;")
     x(f"and.b32 {r('lane')}, %tid, 31;")
     x(f"mov.u32 {r('smem')}, smem_pool;")
@@ -471,12 +499,13 @@ def emit(p: MatmulPlan) -> str:
     x(f"setp.eq.u32 {r('p', pred)}, %tid, 0;")
     init_done = x.label("init_done")
     x(f"@!%p bra {init_done};")
-    for s in range(p.stages):
+    for s in range(stages):
         x(f"mbarrier.init.shared::cta.b64 [%bars+{full + 8 * s}], 1;")
         x(f"mbarrier.init.shared::cta.b64 [%bars+{empty + 8 * s}], 1;")
     for a in range(2):
         x(f"mbarrier.init.shared::cta.b64 [%bars+{tfull + 8 * a}], 1;")
-        x(f"mbarrier.init.shared::cta.b64 [%bars+{tempty + 8 * a}], {ept};")
+        # the leader's accumulator is released by both CTAs' epilogues
+        x(f"mbarrier.init.shared::cta.b64 [%bars+{tempty + 8 * a}], {g * ept};")
     x(f"mbarrier.init.shared::cta.b64 [%bars+{drain}], 1;")
     x("fence.mbarrier_init.release.cluster;")
     x("fence.proxy.async.shared::cta;")
@@ -487,11 +516,12 @@ def emit(p: MatmulPlan) -> str:
     x("setp.eq.u32 %p, %warp, 1;")
     x(f"@!%p bra {alloc_done};")
     x(f"add.u32 {r('slot')}, %bars, {slot};")
-    x(f"tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%slot], {tmem_cols};")
-    x("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;")
+    # a pair allocates the same columns in both CTAs: warp 1 of each runs the alloc
+    x(f"tcgen05.alloc.cta_group::{g}.sync.aligned.shared::cta.b32 [%slot], {tmem_cols};")
+    x(f"tcgen05.relinquish_alloc_permit.cta_group::{g}.sync.aligned;")
     x(f"{alloc_done}:")
     x("tcgen05.fence::before_thread_sync;")
-    x("barrier.sync 0;")  # not .aligned: warps 0 and 1 arrive from divergent branches
+    cta_sync()  # not .aligned: warps 0 and 1 arrive from divergent branches
     x("tcgen05.fence::after_thread_sync;")
     x(f"ld.shared.b32 {r('tmem')}, [%bars+{slot}];")
     teardown = "$M_teardown"
@@ -519,12 +549,17 @@ def emit(p: MatmulPlan) -> str:
     x(f"setp.ge.u32 %p, %t, {entries};")
     x(f"@%p bra {p_drain};")
     sched_lookup(p_next)
-    x(f"shl.b32 {r('m0')}, %mt, 7;")
-    x(f"mul.lo.u32 {r('n0')}, %nt, {p.bn};")
+    if pair:  # this CTA's half: rows rank*128 of the 256-row tile, B columns rank*128
+        x(f"shl.b32 {r('half')}, %rank, 7;")
+        x(f"mad.lo.u32 {r('m0')}, %mt, {g * BM}, %half;")
+        x(f"mad.lo.u32 {r('n0')}, %nt, {p.bn}, %half;")
+    else:
+        x(f"shl.b32 {r('m0')}, %mt, 7;")
+        x(f"mul.lo.u32 {r('n0')}, %nt, {p.bn};")
     x(f"mul.lo.u32 {r('kk')}, %kb0, {BK};")
     x(f"mov.u32 {r('kb')}, 0;")
     x(f"{p_k}:")
-    x(f"setp.lt.u32 %p, %it, {p.stages};")
+    x(f"setp.lt.u32 %p, %it, {stages};")
     x(f"@%p bra {p_noempty};")
     x(f"mad.lo.u32 {r('ebar')}, %s, 8, %bars;")
     x(f"add.u32 %ebar, %ebar, {empty};")
@@ -532,17 +567,25 @@ def emit(p: MatmulPlan) -> str:
     wait("%ebar", "%par", 1, p_drain)
     x(f"{p_noempty}:")
     x(f"mad.lo.u32 {r('fbar')}, %s, 8, %bars;")
-    x(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [%fbar], {p.stage_bytes};")
+    if pair:
+        # both CTAs' loads land on the leader's full barrier, which the MMA waits on; the
+        # leader expects the bytes of both halves
+        x(f"@%plead mbarrier.arrive.expect_tx.shared::cta.b64 _, [%fbar], {stage_tx};")
+        x(f"mapa.shared::cluster.u32 {r('fbar_l')}, %fbar, 0;")
+        tma, bar = ("cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global"
+                    ".mbarrier::complete_tx::bytes"), "%fbar_l"
+    else:
+        x(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [%fbar], {stage_tx};")
+        tma, bar = ("cp.async.bulk.tensor.2d.shared::cluster.global.tile"
+                    ".mbarrier::complete_tx::bytes"), "%fbar"
     x(f"mad.lo.u32 {r('adst')}, %s, {a_stage}, %smem;")
-    x("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-      "[%adst], [%tmap_a, {%kk, %m0}], [%fbar];")
+    x(f"{tma} [%adst], [%tmap_a, {{%kk, %m0}}], [{bar}];")
     x(f"mad.lo.u32 {r('bdst')}, %s, {b_stage}, %smem;")
     x(f"add.u32 %bdst, %bdst, {b_off};")
-    for cidx in range(p.bn // 64):
+    for cidx in range(nb // 64):
         x(f"add.u32 {r('ncol')}, %n0, {cidx * 64};")
         x(f"add.u32 {r('bdc')}, %bdst, {cidx * b_chunk};")
-        x("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-          "[%bdc], [%tmap_b, {%ncol, %kk}], [%fbar];")
+        x(f"{tma} [%bdc], [%tmap_b, {{%ncol, %kk}}], [{bar}];")
     advance_stage()
     x(f"add.u32 %kk, %kk, {BK};")
     x("add.u32 %kb, %kb, 1;")
@@ -551,15 +594,19 @@ def emit(p: MatmulPlan) -> str:
     x(f"{p_next}:")
     x("add.u32 %t, %t, %ncta;")
     x(f"bra.uni {p_tile};")
-    # drain: the loads of the last issued stages have landed before the CTA may exit
+    # drain: the loads of the last issued stages have landed before the CTA may exit (a
+    # pair's loads all land on the leader's barriers, so the leader drains for both, and the
+    # other CTA waits for it at the teardown's cluster barrier)
     x(f"{p_drain}:")
-    for j in range(1, p.stages + 1):
+    if pair:
+        x(f"@!%plead bra {teardown};")
+    for j in range(1, stages + 1):
         skip = x.label("drain_skip")
         x(f"setp.lt.u32 %p, %it, {j};")
         x(f"@%p bra {skip};")
         x(f"sub.u32 {r('db')}, %it, {j};")
-        x(f"rem.u32 {r('ds')}, %db, {p.stages};")
-        x(f"div.u32 {r('du')}, %db, {p.stages};")
+        x(f"rem.u32 {r('ds')}, %db, {stages};")
+        x(f"div.u32 {r('du')}, %db, {stages};")
         x("and.b32 %du, %du, 1;")
         x(f"mad.lo.u32 {r('dbar')}, %ds, 8, %bars;")
         wait("%dbar", "%du", 5, teardown)
@@ -570,6 +617,11 @@ def emit(p: MatmulPlan) -> str:
     x(f"{mma}:")
     x("setp.ne.u32 %p, %lane, 0;")
     x(f"@%p bra {teardown};")
+    if pair:  # the leader issues the pair's MMAs
+        x(f"@!%plead bra {teardown};")
+        x(f"mov.b16 {r('pmask', 'b16')}, 3;")
+    commit = (f"tcgen05.commit.cta_group::{g}.mbarrier::arrive::one.shared::cluster"
+              + (".multicast::cluster.b64 [{}], %pmask;" if pair else ".b64 [{}];"))
     for n in ("it", "s", "ph", "tc", "ab", "aph"):
         x(f"mov.u32 {r(n)}, 0;")
     x("mov.u32 %t, %cta;")
@@ -585,7 +637,7 @@ def emit(p: MatmulPlan) -> str:
     x(f"mad.lo.u32 {r('tebar')}, %ab, 8, %bars;")
     x(f"add.u32 %tebar, %tebar, {tempty};")
     x("xor.b32 %par, %aph, 1;")
-    wait("%tebar", "%par", 3, m_end)
+    wait("%tebar", "%par", 3, m_end, ".acquire.cluster" if pair else "")
     x(f"{m_free}:")
     x("tcgen05.fence::after_thread_sync;")
     x(f"mad.lo.u32 {r('dtm')}, %ab, {p.bn}, %tmem;")
@@ -611,24 +663,24 @@ def emit(p: MatmulPlan) -> str:
         x(f"mov.b64 {r('adesc', 'b64')}, {{%alo_k, {a_hi}}};")
         x(f"mov.b64 {r('bdesc', 'b64')}, {{%blo_k, {b_hi}}};")
         acc = "%pacc" if kk == 0 else r("ptrue", pred)
-        x(f"tcgen05.mma.cta_group::1.kind::f16 [%dtm], %adesc, %bdesc, %idesc, {acc};")
+        x(f"tcgen05.mma.cta_group::{g}.kind::f16 [%dtm], %adesc, %bdesc, %idesc, {acc};")
     x("mad.lo.u32 %ebar, %s, 8, %bars;")
     x(f"add.u32 %ebar, %ebar, {empty};")
-    x("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%ebar];")
+    x(commit.format("%ebar"))  # the stage is free again (in both CTAs of a pair)
     advance_stage()
     x("add.u32 %kb, %kb, 1;")
     x("setp.lt.u32 %p, %kb, %cnt;")
     x(f"@%p bra {m_k};")
     x(f"mad.lo.u32 {r('tfbar')}, %ab, 8, %bars;")
     x(f"add.u32 %tfbar, %tfbar, {tfull};")
-    x("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%tfbar];")
+    x(commit.format("%tfbar"))  # the accumulator is ready (for both CTAs' epilogues)
     advance_acc()
     x(f"{m_next}:")
     x("add.u32 %t, %t, %ncta;")
     x(f"bra.uni {m_tile};")
     x(f"{m_end}:")
     x(f"add.u32 {r('dr')}, %bars, {drain};")
-    x("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%dr];")
+    x(f"tcgen05.commit.cta_group::{g}.mbarrier::arrive::one.shared::cluster.b64 [%dr];")
     wait("%dr", "0", 6, teardown)
     x(f"bra.uni {teardown};")
 
@@ -648,8 +700,13 @@ def emit(p: MatmulPlan) -> str:
     x(f"add.u32 %tfbar, %tfbar, {tfull};")
     wait("%tfbar", "%aph", 4, teardown)
     x("tcgen05.fence::after_thread_sync;")
-    # this thread's row of C and the accumulator's columns in TMEM
-    x("shl.b32 %m0, %mt, 7;")
+    # this thread's row of C and the accumulator's columns in TMEM (a pair's CTA holds rows
+    # rank*128 of the 256-row tile, all BN columns)
+    if pair:
+        x("shl.b32 %half, %rank, 7;")
+        x(f"mad.lo.u32 %m0, %mt, {g * BM}, %half;")
+    else:
+        x("shl.b32 %m0, %mt, 7;")
     x(f"mad.lo.u32 {r('row')}, %quad, 32, %lane;")
     x("add.u32 %row, %row, %m0;")
     x(f"mul.wide.u32 {r('crow', u64)}, %row, {p.n * 4};")
@@ -674,7 +731,11 @@ def emit(p: MatmulPlan) -> str:
     x("tcgen05.fence::before_thread_sync;")
     x("mad.lo.u32 %tebar, %ab, 8, %bars;")
     x(f"add.u32 %tebar, %tebar, {tempty};")
-    x("mbarrier.arrive.shared::cta.b64 _, [%tebar];")
+    if pair:  # the leader's barrier, which its MMA waits on
+        x(f"mapa.shared::cluster.u32 {r('tebar_l')}, %tebar, 0;")
+        x("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%tebar_l];")
+    else:
+        x("mbarrier.arrive.shared::cta.b64 _, [%tebar];")
     advance_acc()
     x(f"{e_next}:")
     x("add.u32 %t, %t, %ncta;")
@@ -682,12 +743,13 @@ def emit(p: MatmulPlan) -> str:
 
     # --- teardown ----------------------------------------------------------------------------
     x(f"{teardown}:")
-    x("barrier.sync 0;")
+    x("tcgen05.fence::before_thread_sync;")
+    cta_sync()
     x("setp.ne.u32 %p, %warp, 1;")
     x("@%p bra $M_exit;")
     x("bar.warp.sync -1;")
     x("tcgen05.fence::after_thread_sync;")
-    x(f"tcgen05.dealloc.cta_group::1.sync.aligned.b32 %tmem, {tmem_cols};")
+    x(f"tcgen05.dealloc.cta_group::{g}.sync.aligned.b32 %tmem, {tmem_cols};")
     x("$M_exit:")
     x("ret;")
 
@@ -703,14 +765,15 @@ def emit(p: MatmulPlan) -> str:
     esz = 2
     head = [
         "//\n// Generated by ptxgen (B200 backend): tcgen05 GEMM template\n//",
-        f"// @ptxgen launch grid={ctas} block={p.block} persistent=1",
+        f"// @ptxgen launch grid={ctas} block={p.block} persistent=1"
+        + (f" cluster={g}" if pair else ""),
         f"// @ptxgen dynamic_smem={smem_total}",
         f"// @ptxgen tensormap symbol={e}_tmap_a buffer={p.a} dtype={p.dtype} "
         f"dims={p.k},{p.m} strides={p.k * esz} box={BK},{BM} swizzle=128",
         f"// @ptxgen tensormap symbol={e}_tmap_b buffer={p.b} dtype={p.dtype} "
         f"dims={p.n},{p.k} strides={p.n * esz} box=64,{BK} swizzle=128",
         f"// @ptxgen matmul m={p.m} n={p.n} k={p.k} bn={p.bn} splits={p.splits} "
-        f"stages={p.stages} tiles={p.tiles} segments={entries}",
+        f"stages={stages} tiles={p.tiles} segments={entries} cta_group={g}",
         "",
         f".version {PTX_VERSION}\n.target {TARGET}\n.address_size 64\n",
         ".extern .shared .align 1024 .b8 smem_pool[];",
@@ -720,7 +783,8 @@ def emit(p: MatmulPlan) -> str:
         f".global .align 8 .u32 {e}_sched[{len(sched_words)}] = {{\n\t"
         + ",\n\t".join(rows) + "\n};",
         "",
-        f".visible .entry {e}(\n{params}\n)\n.maxntid {p.block}, 1, 1\n.minnctapersm 1\n{{",
+        f".visible .entry {e}(\n{params}\n)\n.maxntid {p.block}, 1, 1\n.minnctapersm 1\n"
+        + (".reqnctapercluster 2, 1, 1\n" if pair else "") + "{",
         decls,
     ]
     return "\n".join(head + x.finish() + ["}", ""])

@@ -18,11 +18,12 @@
  *   pg_run_host        <- the whole evaluator step on host buffers: copy in, zero, launch,
  *                         copy out, check the kernel's status word
  *
- * Two entry points have no counterpart in the reference, because its kernels never needed
+ * Three entry points have no counterpart in the reference, because its kernels never needed
  * them: pg_tensormap_fill writes a TMA tensor map into a module's .global symbol (the tcgen05
  * templates read their operands through TMA, and a kernel's parameters must stay the plain
- * device pointers of meta.arg_order), and pg_status_take reads the status word that kernels
- * with bounded waits set instead of hanging.
+ * device pointers of meta.arg_order), pg_status_take reads the status word that kernels with
+ * bounded waits set instead of hanging, and pg_kernel_max_clusters sizes the grid of a
+ * persistent kernel whose CTAs run in pairs (the tcgen05 GEMM's 2-SM form).
  *
  * Plain C types only: device pointers and CUDA streams travel as uint64_t. Every function
  * returns 0 on success, a positive CUresult from the driver, or a negative PG_ERR_* code;
@@ -79,6 +80,12 @@ int pg_kernel_get(pg_module *module, const char *entry, pg_kernel **out);
  * is opted into automatically. Asynchronous on `stream` (0 = the legacy default stream). */
 int pg_kernel_launch(pg_kernel *kernel, uint32_t grid, uint32_t block, uint32_t smem_bytes,
                      uint64_t stream, const uint64_t *ptrs, int nptrs);
+
+/* How many clusters of `cluster` CTAs of `block` threads and `smem_bytes` of dynamic shared
+ * memory can be resident on the device at once (cuOccupancyMaxActiveClusters); a persistent
+ * kernel compiled for that cluster size launches at most that many clusters. */
+int pg_kernel_max_clusters(pg_kernel *kernel, uint32_t block, uint32_t smem_bytes,
+                           uint32_t cluster, int *out);
 
 /* Encode a tiled TMA tensor map (cuTensorMapEncodeTiled) over the row-major array at `base`
  * and write its 128 bytes into the module's .global symbol `symbol`. dims[0] is the innermost

@@ -47,8 +47,10 @@ def test_shipped_compiles_and_assembles(name: str, flags: dict, tmp_path) -> Non
     ptxas(ptx, tmp_path)
 
 
-# The one form of TMA load the kernels may issue: each CTA fills its own shared memory.
-TMA_LOAD = re.compile(r"^\s*cp\.async\.bulk\.tensor\.2d\.shared::cluster\.global\.tile"
+# The two forms of TMA load the kernels may issue: each CTA fills its own shared memory, and in
+# a CTA pair (cta_group::2) signals the pair leader's barrier. Neither form multicasts.
+TMA_LOAD = re.compile(r"^\s*cp\.async\.bulk\.tensor\.2d\.(shared::cluster\.global\.tile|"
+                      r"cta_group::2\.shared::cluster\.global)"
                       r"\.mbarrier::complete_tx::bytes \[%\w+\], \[%\w+, \{%\w+, %\w+\}\], "
                       r"\[%\w+\];$")
 
@@ -188,8 +190,15 @@ def test_unsupported_node_raises() -> None:
 
 def test_gemm_uses_the_tcgen05_template() -> None:
     ptx = compile_spec(problems.CONFIGS["c5_matmul"]())
-    assert "tcgen05.mma.cta_group::1.kind::f16" in ptx and "tcgen05.alloc" in ptx
-    assert ptx.count("cp.async.bulk.tensor") == 1 + 256 // 64  # one A and four B loads a stage
+    # 256-row tiles on SM pairs: one A and two B loads (this CTA's half of B) a stage
+    assert "tcgen05.mma.cta_group::2.kind::f16" in ptx and "tcgen05.alloc.cta_group::2" in ptx
+    assert ".reqnctapercluster 2, 1, 1" in ptx and "cluster=2" in ptx
+    assert ptx.count("cp.async.bulk.tensor") == 1 + 128 // 64
+    # an odd number of 128-row tiles keeps one SM per tile: one A and four B loads a stage
+    single = compile_spec(problems.matmul(384, 512, 512))
+    assert "tcgen05.mma.cta_group::1.kind::f16" in single and ".reqnctapercluster" not in single
+    assert single.count("cp.async.bulk.tensor") == 1 + 256 // 64
+    assert_plain_tma(single)
     assert "// @ptxgen tensormap symbol=" in ptx and "persistent=1" in ptx
     assert_plain_tma(ptx)
     generic = to_ptx(Graph.from_dict(problems.matmul(256, 256, 256).graph),
@@ -226,24 +235,28 @@ def test_gemm_segments_cover_every_k_block_once(shape) -> None:
     kw = {"split_k": split, "raster_group": None} if split > 1 else {}
     p = gemm_plan(problems.matmul(m, n, k, **kw))
     table, ctas = p.segments()
+    rows = 2 if p.pair else 1  # a pair's table tiles are two of the IR's 128-row tiles
+    assert p.pair == (m % 256 == 0)
     seen = Counter()
     for mt, nt, kb0, cnt in table:
-        seen.update((mt, nt, kb) for kb in range(kb0, kb0 + cnt))
+        seen.update((mt * rows + r, nt, kb) for kb in range(kb0, kb0 + cnt) for r in range(rows))
     tiles = list(dict.fromkeys((mt, nt) for mt, nt, _ in p.schedule))
     kbs = k // BK
     assert set(seen) == {(mt, nt, kb) for mt, nt in tiles for kb in range(kbs)}
     assert set(seen.values()) == {1}
+    order = list(dict.fromkeys((mt // rows, nt) for mt, nt, _ in p.schedule))
     if split == 1:
-        assert [(mt, nt) for mt, nt, _, _ in table] == [(mt, nt) for mt, nt, _ in p.schedule]
+        assert [(mt, nt) for mt, nt, _, _ in table] == order
+        assert ctas == len(table) * rows
         return
-    splits = len(table) // len(tiles)
-    assert [(mt, nt) for mt, nt, _, _ in table] == tiles * splits
+    splits = len(table) // len(order)
+    assert [(mt, nt) for mt, nt, _, _ in table] == order * splits
     counts = {cnt for _, _, _, cnt in table}
     assert max(counts) - min(counts) <= 1 and min(counts) >= min(MIN_SEGMENT, kbs)
-    assert ctas == min(SM_COUNT, len(table))
+    assert ctas == min(SM_COUNT // rows, len(table)) * rows
 
 
 def test_splitk_config_fills_the_sms() -> None:
-    """Config 5b (32 tiles of 1024 K blocks): 9 splits, two full waves over 148 SMs."""
+    """Config 5b (16 pair tiles of 1024 K blocks): 9 splits, two full waves over 74 SM pairs."""
     table, ctas = gemm_plan(problems.CONFIGS["c5b_matmul_splitk"]()).segments()
-    assert (len(table), ctas) == (288, 148)
+    assert (len(table), ctas) == (144, 148)
