@@ -49,6 +49,10 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--scaling", choices=("weak", "strong"), default="weak",
                    help="weak: each GPU keeps a full benchmark-sized share of an N-times larger "
                         "problem; strong: the GPUs split the benchmark size")
+    p.add_argument("--l2", choices=("write", "clean"), default="write",
+                   help="write: flush L2 with a 256 MiB write before each timed step, leaving it "
+                        "full of dirty lines the next kernel writes back; clean: follow that write "
+                        "with a 256 MiB read, so L2 holds clean unrelated lines")
     p.add_argument("--cpu-seconds", type=float, default=12.0,
                    help="target seconds of CPU work for the CPU baseline sample")
     return p.parse_args()
@@ -196,7 +200,8 @@ def device_tensors(prob: Any, seed: int) -> dict[str, Any]:
 # --- measurement ---------------------------------------------------------------------------------
 
 
-def measure_kernel(plan: Any, steps: int, warmup: int, world: int) -> dict[str, Any]:
+def measure_kernel(plan: Any, steps: int, warmup: int, world: int, l2: str = "write"
+                   ) -> dict[str, Any]:
     """Mean kernel time over ``steps`` timed launches (each after an L2 flush), the slowest
     rank's, with the launch count and NVML clocks of the timed region."""
     import torch
@@ -208,7 +213,14 @@ def measure_kernel(plan: Any, steps: int, warmup: int, world: int) -> dict[str, 
     prob.load()
     tensors = device_tensors(prob, seed=1000 + rank)
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    reread = torch.zeros(FLUSH_BYTES if l2 == "clean" else 8, dtype=torch.uint8, device="cuda")
+    sink = torch.empty((), dtype=torch.int64, device="cuda")
     stream = torch.cuda.current_stream()
+
+    def flush_l2() -> None:
+        flush.zero_()
+        if l2 == "clean":
+            torch.sum(reread.view(torch.int64), dim=(0,), out=sink)
 
     def step() -> None:
         prob.launch(tensors, stream=stream.cuda_stream)
@@ -219,7 +231,7 @@ def measure_kernel(plan: Any, steps: int, warmup: int, world: int) -> dict[str, 
                 tdist.all_reduce(tensors[name])
 
     for _ in range(warmup):
-        flush.zero_()
+        flush_l2()
         step()
     torch.cuda.synchronize()
     if world > 1:
@@ -232,7 +244,7 @@ def measure_kernel(plan: Any, steps: int, warmup: int, world: int) -> dict[str, 
     sampler = ClockSampler(torch.cuda.current_device())
     with sampler:
         for i in range(steps):
-            flush.zero_()
+            flush_l2()
             starts[i].record(stream)
             step()
             stops[i].record(stream)
@@ -386,7 +398,7 @@ def run_ours(args: argparse.Namespace) -> None:
         log(f"{name}: compile and inputs")
         plan = shard.local_problem(name, world, weak=args.scaling == "weak")
         unit, bound, scale = unit_of(plan)
-        m = measure_kernel(plan, steps, warmup, world)
+        m = measure_kernel(plan, steps, warmup, world, args.l2)
         per_rank = plan.work / (m["mean_ms"] / 1e3) / scale
         res: dict[str, Any] = {"workload": name, "value": per_rank * world, "unit": unit,
                                "ms_per_step": m["mean_ms"], "median_ms": m["median_ms"],
@@ -432,7 +444,9 @@ def run_ours(args: argparse.Namespace) -> None:
         "data": "synthetic (seeded, the configuration's distributions, generated on the GPU)",
         "config": {"workload": args.workload, "per_rank": plan.spec.meta["id"],
                    "parallelism": f"tile-axis x{world}" if world > 1 else "single GPU",
-                   "l2": "flushed (256 MiB write) before every timed step",
+                   "l2": ("flushed (256 MiB write) before every timed step" if args.l2 == "write"
+                          else "flushed (256 MiB write, then a 256 MiB read: clean) before "
+                               "every timed step"),
                    "allreduce": list(plan.allreduce)},
         "roofline": head["roofline"], "e2e": head["e2e"], "clocks": head["clocks"],
         "gpu_launches": head["launches"],
