@@ -150,7 +150,7 @@ class ClockSampler:
                 self.reasons |= {n for b, n in self.REASONS.items() if bits & b}
             except Exception:  # noqa: BLE001
                 pass
-            self._stop.wait(0.005)
+            self._stop.wait(0.001)
 
     def __enter__(self) -> ClockSampler:
         if self.nvml is not None:
