@@ -9,7 +9,10 @@ arithmetic instructions without changing a single bit of the results.
 The pass works on one straight-line segment at a time:
 
 1. **Seeds** are register pairs that are consumed together: the two f32 sources of a
-   ``cvt.rn.bf16x2.f32`` and the neighbouring registers of a vector store of f32.
+   ``cvt.rn.bf16x2.f32`` and the neighbouring registers of a vector store of f32. An add or
+   sub that reads a multiply's result is never packed: ptxas may contract a packed multiply
+   and add into an fma (the packed forms' mandatory ``.rn`` does not forbid it the way the
+   scalar forms' explicit ``.rn`` does), which would break the results' bit-reproducibility.
 2. **Trees** grow bottom-up from a seed: two results defined by pure instructions of one
    packable opcode, neither depending on the other and neither already paired, become a pair
    node, and their operands in the same position are paired recursively. An operand shared by
@@ -60,6 +63,7 @@ class SLP:
         # reads of every register anywhere in the kernel: a lane read by anything but its
         # parent pair must be unpacked, even when the reader sits in a later segment
         self.global_reads = Counter(r for ins in body for r in ins.reads())
+        self.products = {r for ins in body if ins.op == "mul.rn.f32" for r in ins.writes()}
         out: list[Ins] = []
         seg: list[Ins] = []
         for ins in body:
@@ -126,7 +130,16 @@ class SLP:
         return (a is not None and b is not None and a is not b and a.op in PACKABLE and
                 a.op == b.op and a.pure and b.pure and not a.pred and not b.pred and
                 len(a.src) == len(b.src) and len(a.dst) == 1 and len(b.dst) == 1 and
-                a.dst[0] not in self.variables and b.dst[0] not in self.variables)
+                a.dst[0] not in self.variables and b.dst[0] not in self.variables and
+                not self._contractible(a) and not self._contractible(b))
+
+    def _contractible(self, ins: Ins) -> bool:
+        """An add or sub of a product. Its scalar ``.rn`` form keeps ptxas from fusing the two
+        into an fma, but the packed forms' rounding modifier is mandatory and does not: a packed
+        ``mul`` + ``add`` pair came out fused on a B200. So such an add or sub stays scalar, and
+        the only fma contractions left are the lowering's own."""
+        return ins.op in ("add.rn.f32", "sub.rn.f32") and any(
+            r in self.products for r in ins.src)
 
     def _preds(self, ins: Ins) -> set[int]:
         """Ids of the segment instructions ``ins`` depends on through registers."""

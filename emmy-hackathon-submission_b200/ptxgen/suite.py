@@ -1,0 +1,579 @@
+"""Kernel IR for the reference's problem categories beyond the five benchmark configurations.
+
+The reference defines its problems as torch expressions, each with a NumPy formula of the
+expected output and a tolerance (reference ``tools/expressions_open.py``,
+``tools/expressions_closed.py``). Emmy traces each expression into Kernel IR, and the compiler
+lowers that. Emmy is absent here, so this module writes Kernel IR of the same kinds directly, in
+the statement shapes of the shipped IRs (``ptxgen.problems`` documents them):
+
+* pointwise chains over one flat Tile axis, with row and column broadcasts and ConstantOp
+  scalars (the ``p`` category: every op of the lowering's table, f32/f64/f16/bf16 and mixed
+  dtypes, odd sizes that need the tail guard);
+* one-block-per-row reductions and fused row passes (``r`` and ``f``: sum, mean, amax, sum of
+  squares, softmax, log-softmax, RMS norm, layer norm, L2 norm), with rows that are not a
+  multiple of the block;
+* column and middle-axis reductions (a Loop over the reduced axis per output element) and a
+  grid-stride reduction with an atomic Write;
+* small f32 matmuls through the SIMT nest (the ``m`` category's shapes).
+
+Each case keeps the reference id it stands for, its NumPy formula (restated from the
+reference's ``ref`` of that id, computing in the inputs' dtypes as it does), the reference's
+rtol/atol, and the bar its GPU result meets against the oracle's run of the same IR.
+"""
+
+from __future__ import annotations
+
+import math
+from collections.abc import Callable, Sequence
+from dataclasses import dataclass, field
+from typing import Any
+
+import numpy as np
+
+from .ir import (Accum, Assign, Axis, BinaryExpr, Cond, Dim, Init, Let, Literal, Load, Loop,
+                 Stmt, StridedLoop, Tile, Write, dt)
+from .problems import I, ProblemSpec, V, _arg, _block_reduce, _spec, add, div, matmul, mul, op, \
+    rem
+
+# --- case container ----------------------------------------------------------------------------
+
+
+@dataclass
+class SuiteCase:
+    """A generated problem with its NumPy formula and bars."""
+
+    spec: ProblemSpec
+    ref: Callable[..., np.ndarray]  # formula of the output from the inputs, in their dtypes
+    rtol: float  # the reference's tolerance of its formula
+    atol: float
+    bar: tuple[str, float]  # GPU against the oracle: ("exact" | "ulp" | "rel", bound)
+    note: str = ""
+
+    @property
+    def out(self) -> str:
+        return self.spec.meta["graph_outputs"][0]
+
+    @property
+    def out_dtype(self) -> str:
+        return next(a["dtype"] for a in self.spec.kernel["args"] if a["name"] == self.out)
+
+
+@dataclass
+class In:
+    """A graph input: ``bcast`` "rows" indexes it by the output row, "cols" by the column."""
+
+    name: str
+    dtype: str
+    shape: tuple[int, ...]
+    dist: Sequence[Any] = ("normal", 0.0, 1.0)
+    bcast: str | None = None
+
+
+@dataclass
+class Step:
+    name: str
+    fn: str
+    args: tuple[str, ...]
+    dtype: str | None = "f32"
+
+
+def S(name: str, fn: str, *args: str, dtype: str | None = "f32") -> Step:  # noqa: N802
+    return Step(name, fn, tuple(args), dtype)
+
+
+# --- pointwise ---------------------------------------------------------------------------------
+
+
+@dataclass
+class Pointwise:
+    pid: str
+    code: str
+    inputs: list[In]
+    out: tuple[str, str, tuple[int, ...]]  # name, dtype, shape
+    steps: list[Step]
+    result: str
+    consts: dict[str, float] = field(default_factory=dict)
+    unroll: int = 4
+    block: int = 256
+
+    def build(self) -> ProblemSpec:
+        oname, odt, oshape = self.out
+        n, cols = math.prod(oshape), oshape[-1]
+        u = self.unroll if n % self.unroll == 0 and cols % self.unroll == 0 else 1
+        a0 = V("a0")
+        body: list[Stmt] = [Load((c,), c, (I(0),), dt("f32")) for c in self.consts]
+        names = {i.name for i in self.inputs} | {s.name for s in self.steps}
+        for j in range(u):
+            sfx = f"__u{j}"
+            flat = add(mul(a0, I(u)), I(j)) if u > 1 else a0
+            for i in self.inputs:
+                idx = {None: flat, "cols": rem(flat, I(cols)), "rows": div(flat, I(cols))}
+                body.append(Load((i.name + sfx,), i.name, (idx[i.bcast],), dt(i.dtype)))
+            for s in self.steps:
+                args = tuple(a + sfx if a in names else a for a in s.args)
+                body.append(Assign(s.name + sfx, op(s.fn), args, dt(s.dtype) if s.dtype
+                                   else None))
+        rdt = next((s.dtype for s in self.steps if s.name == self.result), None) or \
+            next(i.dtype for i in self.inputs if i.name == self.result)
+        widx = (add(mul(a0, I(u)), I(0)),) if u > 1 else (a0,)
+        body.append(Write(oname, widx, tuple(f"{self.result}__u{j}" for j in range(u)),
+                          dt(rdt)))
+        tile = Tile((Axis("a0", Dim(n // u)),), tuple(body), None)
+        args = [_arg(c, "f32", [1], data=[v]) for c, v in self.consts.items()]
+        args += [_arg(i.name, i.dtype, i.shape, seed=k, dist=list(i.dist))
+                 for k, i in enumerate(self.inputs)]
+        args.append(_arg(oname, odt, oshape, output=True))
+        return _spec(self.pid, self.code, 0, 0, f"k_{self.pid}", tile, args,
+                     [i.name for i in self.inputs], [oname], dict(self.consts), self.block)
+
+
+# --- row-wise (one block per row) ----------------------------------------------------------------
+
+
+@dataclass
+class Rowwise:
+    """Passes over the rows of x [rows, cols], one block per row. A pass is
+    ``("reduce", acc, op, steps, value)`` -- a strided sweep accumulating ``value`` and a block
+    reduction; ``("scalar", step)`` -- a per-row value; ``("write", steps, value)`` -- a sweep
+    writing ``value`` into out [rows, cols]; or ``("row", value)`` -- out [rows] from thread 0.
+    Steps name the sweep's element of x ``xv``."""
+
+    pid: str
+    code: str
+    x: In
+    out: tuple[str, str]  # name, dtype
+    passes: list[tuple[Any, ...]]
+    consts: dict[str, float] = field(default_factory=dict)
+    block: int = 128
+
+    def build(self) -> ProblemSpec:
+        rows, cols = self.x.shape
+        a0, t = V("a0"), V("a1_co")
+        xdt = dt(self.x.dtype)
+        body: list[Stmt] = [Load((c,), c, (I(0),), dt("f32")) for c in self.consts]
+        body.append(Let("n_cols", Literal(float(cols), "float"), dt("f32")))
+        per_row = False
+
+        def sweep(stmts: list[Stmt]) -> StridedLoop:
+            return StridedLoop(Axis("a1", Dim(cols)), t, I(self.block), tuple(stmts), False,
+                               None, True)
+
+        for k, p in enumerate(self.passes):
+            # each sweep loads x under its own name
+            xv = f"xv{k}"
+
+            def steps(ss: Sequence[Step], xv: str = xv) -> list[Stmt]:
+                return [Assign(s.name, op(s.fn), tuple(xv if a == "xv" else a for a in s.args),
+                               dt(s.dtype) if s.dtype else None) for s in ss]
+
+            def val(v: str, xv: str = xv) -> str:
+                return xv if v == "xv" else v
+
+            load = Load((xv,), "x", (a0, V("a1")), xdt)
+            if p[0] == "reduce":
+                _, acc, fn, ss, value = p
+                body.append(sweep([load, *steps(ss),
+                                   Accum(acc, val(value), op(fn), dt("f32"), ("a1",), None)]))
+                body += _block_reduce(acc, fn, self.block, f"{acc}_smem")
+            elif p[0] == "scalar":
+                body += steps([p[1]])
+            elif p[0] == "write":
+                _, ss, value = p
+                body.append(sweep([load, *steps(ss),
+                                   Write(self.out[0], (a0, V("a1")), (val(value),),
+                                         dt("f32"))]))
+            elif p[0] == "row":
+                per_row = True
+                body.append(Cond(BinaryExpr("==", t, I(0)),
+                                 (Write(self.out[0], (a0,), (p[1],), dt("f32")),), ()))
+            else:
+                raise ValueError(f"pass {k}: {p[0]!r}")
+        tile = Tile((Axis("a0", Dim(rows)), Axis("a1_co", Dim(self.block))), tuple(body),
+                    self.block)
+        oshape = [rows] if per_row else [rows, cols]
+        args = [_arg(c, "f32", [1], data=[v]) for c, v in self.consts.items()]
+        args += [_arg("x", self.x.dtype, self.x.shape, seed=0, dist=list(self.x.dist)),
+                 _arg(self.out[0], self.out[1], oshape, output=True)]
+        return _spec(self.pid, self.code, 0, 0, f"k_{self.pid}", tile, args, ["x"],
+                     [self.out[0]], dict(self.consts), self.block)
+
+
+# --- reductions along other axes -------------------------------------------------------------
+
+
+def axis_reduce(pid: str, code: str, shape: tuple[int, int, int], fn: str, mean: bool,
+                dtype: str = "f32", block: int = 128) -> ProblemSpec:
+    """out[a, c] = fn over b of x[a, b, c] (mean: divided by the extent of b): one thread per
+    output element, a Loop over the reduced axis into an Init'ed accumulator. A leading extent
+    of 1 makes it a column reduction of a [b, c] matrix."""
+    na, nb, nc = shape
+    a0 = V("a0")
+    ia, ic = div(a0, I(nc)), rem(a0, I(nc))
+    identity = {"add": 0.0, "maximum": -math.inf, "minimum": math.inf}[fn]
+    body: list[Stmt] = [
+        Init("acc0", identity, dt("f32")),
+        Loop(Axis("a1", Dim(nb)), (Load(("xv",), "x", (ia, V("a1"), ic), dt(dtype)),
+                                   Accum("acc0", "xv", op(fn), dt("f32"), ("a1",), None))),
+    ]
+    value = "acc0"
+    if mean:
+        body += [Let("n_b", Literal(float(nb), "float"), dt("f32")),
+                 Assign("mean0", op("divide"), ("acc0", "n_b"), dt("f32"))]
+        value = "mean0"
+    body.append(Write("out", (a0,), (value,), dt("f32")))
+    tile = Tile((Axis("a0", Dim(na * nc)),), tuple(body), None)
+    args = [_arg("x", dtype, [na, nb, nc], seed=0), _arg("out", "f32", [na, nc], output=True)]
+    return _spec(pid, code, 0, 0, f"k_{pid}", tile, args, ["x"], ["out"], {}, block)
+
+
+def grid_reduce(pid: str, code: str, n: int, square: bool, block: int = 256,
+                blocks: int = 64) -> ProblemSpec:
+    """sum(x) or sum(x*x) over n f32: a grid-stride sweep per thread, a block reduction and an
+    atomic add of each block's total into the zeroed output (Emmy's grid-atomic plan)."""
+    ab, at = V("a0_b"), V("a0_t")
+    sweep: list[Stmt] = [Load(("xv",), "x", (V("a0"),), dt("f32"))]
+    value = "xv"
+    if square:
+        sweep.append(Assign("sq", op("multiply"), ("xv", "xv"), dt("f32")))
+        value = "sq"
+    sweep.append(Accum("acc0", value, op("add"), dt("f32"), ("a0",), None))
+    body: list[Stmt] = [
+        StridedLoop(Axis("a0", Dim(n)), add(mul(ab, I(block)), at), I(block * blocks),
+                    tuple(sweep), False, None, True),
+        *_block_reduce("acc0", "add", block, "acc0_smem"),
+        Cond(BinaryExpr("==", at, I(0)), (Write("out", (), ("acc0",), dt("f32"), True),), ()),
+    ]
+    tile = Tile((Axis("a0_b", Dim(blocks)), Axis("a0_t", Dim(block))), tuple(body), block)
+    args = [_arg("x", "f32", [n], seed=0), _arg("out", "f32", [1], output=True)]
+    return _spec(pid, code, 0, 0, f"k_{pid}", tile, args, ["x"], ["out"], {}, block,
+                 zero_outputs=["out"])
+
+
+# --- the cases -----------------------------------------------------------------------------------
+
+SQRT1_2 = 1.0 / math.sqrt(2.0)
+
+
+def _erf(x: np.ndarray) -> np.ndarray:
+    return np.vectorize(math.erf, otypes=[np.float64])(x)
+
+
+def _softmax(x: np.ndarray) -> np.ndarray:
+    e = np.exp(x - x.max(axis=-1, keepdims=True))
+    return e / e.sum(axis=-1, keepdims=True)
+
+
+def _pw(pid: str, code: str, inputs: list[In], out: tuple[str, str, tuple[int, ...]],
+        steps: list[Step], result: str, ref: Callable[..., np.ndarray], rtol: float,
+        atol: float, bar: tuple[str, float], consts: dict[str, float] | None = None,
+        note: str = "") -> Callable[[], SuiteCase]:
+    return lambda: SuiteCase(Pointwise(pid, code, inputs, out, steps, result,
+                                       consts or {}).build(), ref, rtol, atol, bar, note)
+
+
+def _x(n: int | tuple[int, ...], dtype: str = "f32", name: str = "x", **kw: Any) -> In:
+    return In(name, dtype, (n,) if isinstance(n, int) else n, **kw)
+
+
+EXACT, FAST, FAST_REL = ("exact", 0.0), ("ulp", 4.0), ("rel", 2e-5)
+f16x, bf16x = "f16", "bf16"
+
+POINTWISE: dict[str, Callable[[], SuiteCase]] = {
+    "p00_small_sub": _pw("p00_small_sub", "torch.randn(64) - torch.randn(64)",
+                         [_x(64), _x(64, name="y")], ("out", "f32", (64,)),
+                         [S("v0", "subtract", "x", "y")], "v0",
+                         lambda x, y: x - y, 0, 0, EXACT),
+    "p01_odd_add": _pw("p01_odd_add", "torch.randn(1000) + torch.randn(1000)",
+                       [_x(1000), _x(1000, name="y")], ("out", "f32", (1000,)),
+                       [S("v0", "add", "x", "y")], "v0", lambda x, y: x + y, 0, 0, EXACT),
+    "p02_v2_mul": _pw("p02_v2_mul", "torch.randn(1538) * torch.randn(1538)",
+                      [_x(1538), _x(1538, name="y")], ("out", "f32", (1538,)),
+                      [S("v0", "multiply", "x", "y")], "v0", lambda x, y: x * y, 0, 0, EXACT),
+    "p03_div": _pw("p03_div", "x / y", [_x(2048), _x(2048, name="y")], ("out", "f32", (2048,)),
+                   [S("v0", "divide", "x", "y")], "v0", lambda x, y: x / y, 1e-6, 1e-6, EXACT),
+    "p04_max_min": _pw("p04_max_min", "torch.maximum(x, y) - torch.minimum(x, y)",
+                       [_x(4096), _x(4096, name="y")], ("out", "f32", (4096,)),
+                       [S("v0", "maximum", "x", "y"), S("v1", "minimum", "x", "y"),
+                        S("v2", "subtract", "v0", "v1")], "v2",
+                       lambda x, y: np.maximum(x, y) - np.minimum(x, y), 0, 0, EXACT),
+    "p06_bias_bcast": _pw("p06_bias_bcast", "x + b (x [64, 256], b [256])",
+                          [_x((64, 256)), In("b", "f32", (256,), bcast="cols")],
+                          ("out", "f32", (64, 256)), [S("v0", "add", "x", "b")], "v0",
+                          lambda x, b: x + b, 0, 0, EXACT),
+    "p07_fma3": _pw("p07_fma3", "a * b + c", [_x(8192, name="a"), _x(8192, name="b"),
+                                              _x(8192, name="c")], ("out", "f32", (8192,)),
+                    [S("v0", "multiply", "a", "b"), S("v1", "add", "v0", "c")], "v1",
+                    lambda a, b, c: a * b + c, 1e-6, 1e-6, EXACT),
+    "p08_relu_affine_odd": _pw("p08_relu_affine_odd", "torch.relu(x * 0.5 - 0.25)",
+                               [_x(3000)], ("out", "f32", (3000,)),
+                               [S("v0", "multiply", "x", "mul_c1"),
+                                S("v1", "subtract", "v0", "sub_c1"), S("v2", "relu", "v1")],
+                               "v2", lambda x: np.maximum(x * 0.5 - 0.25, 0), 1e-6, 1e-6, EXACT,
+                               {"mul_c1": 0.5, "sub_c1": 0.25}),
+    "p09_exp": _pw("p09_exp", "torch.exp(x)", [_x(4096)], ("out", "f32", (4096,)),
+                   [S("v0", "exp", "x")], "v0", np.exp, 1e-5, 1e-5, FAST),
+    "p10_inv_norm": _pw("p10_inv_norm", "1.0 / torch.sqrt(x * x + 1.0)", [_x(2048)],
+                        ("out", "f32", (2048,)),
+                        [S("v0", "multiply", "x", "x"), S("v1", "add", "v0", "add_c1"),
+                         S("v2", "sqrt", "v1"), S("v3", "divide", "div_c1", "v2")], "v3",
+                        lambda x: 1.0 / np.sqrt(x * x + 1.0), 1e-5, 1e-5, EXACT,
+                        {"add_c1": 1.0, "div_c1": 1.0}),
+    "p12_neg": _pw("p12_neg", "-x", [_x(1024)], ("out", "f32", (1024,)),
+                   [S("v0", "negative", "x")], "v0", lambda x: -x, 0, 0, EXACT),
+    "p13_square": _pw("p13_square", "torch.square(x)", [_x(2048)], ("out", "f32", (2048,)),
+                      [S("v0", "square", "x")], "v0", lambda x: x * x, 0, 0, EXACT),
+    "p14_abs": _pw("p14_abs", "torch.abs(x)", [_x(2048)], ("out", "f32", (2048,)),
+                   [S("v0", "abs", "x")], "v0", np.abs, 0, 0, EXACT),
+    "p15_rsqrt": _pw("p15_rsqrt", "torch.rsqrt(x * x + 1.0)", [_x(2048)],
+                     ("out", "f32", (2048,)),
+                     [S("v0", "multiply", "x", "x"), S("v1", "add", "v0", "add_c1"),
+                      S("v2", "rsqrt", "v1")], "v2", lambda x: 1.0 / np.sqrt(x * x + 1.0),
+                     1e-5, 1e-5, FAST, {"add_c1": 1.0}),
+    "p16_log": _pw("p16_log", "torch.log(x * x + 1.0) * 0.5", [_x(2048)],
+                   ("out", "f32", (2048,)),
+                   [S("v0", "multiply", "x", "x"), S("v1", "add", "v0", "add_c1"),
+                    S("v2", "log", "v1"), S("v3", "multiply", "v2", "mul_c1")], "v3",
+                   lambda x: np.log(x * x + 1.0) * 0.5, 1e-5, 1e-5, FAST_REL,
+                   {"add_c1": 1.0, "mul_c1": 0.5}),
+    "p17_sin_cos": _pw("p17_sin_cos", "torch.sin(x) + torch.cos(y)",
+                       [_x(4096), _x(4096, name="y")], ("out", "f32", (4096,)),
+                       [S("v0", "sin", "x"), S("v1", "cos", "y"), S("v2", "add", "v0", "v1")],
+                       "v2", lambda x, y: np.sin(x) + np.cos(y), 1e-5, 1e-5, FAST_REL),
+    "p18_tanh": _pw("p18_tanh", "torch.tanh(x)", [_x(4096)], ("out", "f32", (4096,)),
+                    [S("v0", "tanh", "x")], "v0", np.tanh, 1e-5, 1e-5, FAST_REL),
+    "p19_sigmoid": _pw("p19_sigmoid", "torch.sigmoid(x)", [_x(4096)], ("out", "f32", (4096,)),
+                       [S("v0", "sigmoid", "x")], "v0", lambda x: 1 / (1 + np.exp(-x)),
+                       1e-5, 1e-5, FAST),
+    "p20_silu_odd": _pw("p20_silu_odd", "torch.nn.functional.silu(x)", [_x(3000)],
+                        ("out", "f32", (3000,)),
+                        [S("v0", "sigmoid", "x"), S("v1", "multiply", "x", "v0")], "v1",
+                        lambda x: x / (1 + np.exp(-x)), 1e-5, 1e-5, FAST),
+    "p21_gelu": _pw("p21_gelu", "torch.nn.functional.gelu(x)", [_x(4096)],
+                    ("out", "f32", (4096,)),
+                    [S("v0", "multiply", "x", "c_rsqrt2"), S("v1", "erf", "v0"),
+                     S("v2", "add", "v1", "c_one"), S("v3", "multiply", "x", "c_half"),
+                     S("v4", "multiply", "v3", "v2")], "v4",
+                    lambda x: 0.5 * x * (1.0 + _erf(x * SQRT1_2)), 1e-5, 1e-5, FAST_REL,
+                    {"c_rsqrt2": SQRT1_2, "c_one": 1.0, "c_half": 0.5},
+                    "erf by Abramowitz & Stegun 7.1.26 (|error| < 1.5e-7), as the reference's "
+                    "fastmath.erf"),
+    "p23_sigmoid_gate": _pw("p23_sigmoid_gate", "torch.sigmoid(x) * torch.tanh(y)",
+                            [_x((64, 256)), _x((64, 256), name="y")],
+                            ("out", "f32", (64, 256)),
+                            [S("v0", "sigmoid", "x"), S("v1", "tanh", "y"),
+                             S("v2", "multiply", "v0", "v1")], "v2",
+                            lambda x, y: np.tanh(y) / (1 + np.exp(-x)), 1e-5, 1e-5, FAST_REL),
+    "p24_add_f64": _pw("p24_add_f64", "f64 a + b", [_x(4096, "f64", name="a"),
+                                                    _x(4096, "f64", name="b")],
+                       ("out", "f64", (4096,)), [S("v0", "add", "a", "b", dtype="f64")], "v0",
+                       lambda a, b: a + b, 0, 0, EXACT),
+    "p25_fma_f64_odd": _pw("p25_fma_f64_odd", "f64 a * b + c",
+                           [_x(3000, "f64", name="a"), _x(3000, "f64", name="b"),
+                            _x(3000, "f64", name="c")], ("out", "f64", (3000,)),
+                           [S("v0", "multiply", "a", "b", dtype="f64"),
+                            S("v1", "add", "v0", "c", dtype="f64")], "v1",
+                           lambda a, b, c: a * b + c, 1e-12, 1e-12, EXACT),
+    "p26_exp_f64": _pw("p26_exp_f64", "torch.exp(x) in f64", [_x(4096, "f64")],
+                       ("out", "f64", (4096,)), [S("v0", "exp", "x", dtype="f64")], "v0",
+                       np.exp, 1e-6, 1e-6, FAST_REL,
+                       note="the reference's dtype rule computes an f64 op without an f64 PTX "
+                            "form (exp) in f32 (reference ptxgen/ops.py:173-192), so the "
+                            "formula holds to f32 accuracy, not the reference's rtol 1e-10"),
+    "p27_add_bf16": _pw("p27_add_bf16", "bf16 a + b", [_x(2048, bf16x, name="a"),
+                                                       _x(2048, bf16x, name="b")],
+                        ("out", "bf16", (2048,)), [S("v0", "add", "a", "b", dtype="bf16")],
+                        "v0", lambda a, b: a + b, 1e-2, 1e-2, EXACT),
+    "p28_relu_affine_bf16_odd": _pw("p28_relu_affine_bf16_odd", "relu(bf16 x * 0.5 - 0.25)",
+                                    [_x(3000, bf16x)], ("out", "bf16", (3000,)),
+                                    [S("v0", "multiply", "x", "mul_c1", dtype="bf16"),
+                                     S("v1", "subtract", "v0", "sub_c1", dtype="bf16"),
+                                     S("v2", "relu", "v1", dtype="bf16")], "v2",
+                                    lambda x: np.maximum(x * 0.5 - 0.25, 0), 1e-2, 1e-2, EXACT,
+                                    {"mul_c1": 0.5, "sub_c1": 0.25}),
+    "p29_sigmoid_bf16": _pw("p29_sigmoid_bf16", "torch.sigmoid(bf16 x)", [_x(4096, bf16x)],
+                            ("out", "bf16", (4096,)), [S("v0", "sigmoid", "x", dtype="bf16")],
+                            "v0", lambda x: 1 / (1 + np.exp(-x)), 1e-2, 1e-2, ("ulp", 1)),
+    "p30_add_f16": _pw("p30_add_f16", "f16 a + b", [_x(2048, f16x, name="a"),
+                                                    _x(2048, f16x, name="b")],
+                       ("out", "f16", (2048,)), [S("v0", "add", "a", "b", dtype="f16")], "v0",
+                       lambda a, b: a + b, 1e-3, 1e-3, EXACT),
+    "p31_tanh_f16": _pw("p31_tanh_f16", "torch.tanh(f16 x)", [_x(4096, f16x)],
+                        ("out", "f16", (4096,)), [S("v0", "tanh", "x", dtype="f16")], "v0",
+                        np.tanh, 1e-3, 1e-3, ("rel", 1e-3)),
+    "p32_bf16_to_f32": _pw("p32_bf16_to_f32", "x.float() * y (x bf16)",
+                           [_x(4096, bf16x), _x(4096, name="y")], ("out", "f32", (4096,)),
+                           [S("v0", "cast", "x"), S("v1", "multiply", "v0", "y")], "v1",
+                           lambda x, y: x * y, 1e-6, 1e-6, EXACT),
+    "p37_div": _pw("p37_div", "a / (b.abs() + 1.0)", [_x(1024, name="a"), _x(1024, name="b")],
+                   ("out", "f32", (1024,)),
+                   [S("v0", "abs", "b"), S("v1", "add", "v0", "add_c1"),
+                    S("v2", "divide", "a", "v1")], "v2",
+                   lambda a, b: a / (np.abs(b) + 1.0), 1e-6, 1e-6, EXACT, {"add_c1": 1.0}),
+    "p44_leaky_where": _pw("p44_leaky_where", "torch.where(x > 0, x, 0.01 * x)", [_x(4096)],
+                           ("out", "f32", (4096,)),
+                           [S("v0", "greater", "x", "c_zero", dtype="bool"),
+                            S("v1", "multiply", "x", "c_slope"),
+                            S("v2", "where", "v0", "x", "v1")], "v2",
+                           lambda x: np.where(x > 0, x, 0.01 * x), 1e-6, 1e-6, EXACT,
+                           {"c_zero": 0.0, "c_slope": 0.01}),
+    "p50_clamp": _pw("p50_clamp", "torch.clamp(x, -0.5, 0.5)", [_x(4096)],
+                     ("out", "f32", (4096,)),
+                     [S("v0", "maximum", "x", "c_lo"), S("v1", "minimum", "v0", "c_hi")], "v1",
+                     lambda x: np.clip(x, -0.5, 0.5), 0, 0, EXACT,
+                     {"c_lo": -0.5, "c_hi": 0.5}),
+    "p52_swiglu": _pw("p52_swiglu", "silu(a) * b", [_x((32, 512), name="a"),
+                                                    _x((32, 512), name="b")],
+                      ("out", "f32", (32, 512)),
+                      [S("v0", "sigmoid", "a"), S("v1", "multiply", "a", "v0"),
+                       S("v2", "multiply", "v1", "b")], "v2",
+                      lambda a, b: a / (1 + np.exp(-a)) * b, 1e-5, 1e-5, FAST_REL),
+    "p54_residual_scale": _pw("p54_residual_scale", "x + 0.5 * r * s (s per row)",
+                              [_x((64, 256)), _x((64, 256), name="r"),
+                               In("s", "f32", (64,), bcast="rows")],
+                              ("out", "f32", (64, 256)),
+                              [S("v0", "multiply", "r", "c_half"),
+                               S("v1", "multiply", "v0", "s"), S("v2", "add", "x", "v1")],
+                              "v2", lambda x, r, s: x + 0.5 * r * s[:, None], 1e-6, 1e-6,
+                              EXACT, {"c_half": 0.5}),
+    "p57_pow": _pw("p57_pow", "torch.pow(x.abs() + 0.5, 1.5)", [_x(4096)],
+                   ("out", "f32", (4096,)),
+                   [S("v0", "abs", "x"), S("v1", "add", "v0", "c_half"),
+                    S("v2", "pow", "v1", "c_exp")], "v2",
+                   lambda x: (np.abs(x) + 0.5) ** 1.5, 1e-5, 1e-5, FAST_REL,
+                   {"c_half": 0.5, "c_exp": 1.5}),
+    "p61_f16_silu": _pw("p61_f16_silu", "silu(f16 x)", [_x(4096, f16x)],
+                        ("out", "f16", (4096,)),
+                        [S("v0", "sigmoid", "x", dtype="f16"),
+                         S("v1", "multiply", "x", "v0", dtype="f16")], "v1",
+                        lambda x: x / (1 + np.exp(-x)), 1e-3, 1e-3, ("rel", 1e-3)),
+}
+
+
+def _rw(pid: str, code: str, shape: tuple[int, int], out: tuple[str, str],
+        passes: list[tuple[Any, ...]], ref: Callable[..., np.ndarray], rtol: float, atol: float,
+        bar: tuple[str, float], block: int = 128, dtype: str = "f32",
+        consts: dict[str, float] | None = None) -> Callable[[], SuiteCase]:
+    return lambda: SuiteCase(Rowwise(pid, code, In("x", dtype, shape), out, passes,
+                                     consts or {}, block).build(), ref, rtol, atol, bar)
+
+
+SUM = ("reduce", "acc0", "add", [], "xv")
+MAX = ("reduce", "acc0", "maximum", [], "xv")
+SUMSQ = ("reduce", "acc0", "add", [S("sq", "multiply", "xv", "xv")], "sq")
+ATOMIC = ("rel", 1e-6)
+
+ROWWISE: dict[str, Callable[[], SuiteCase]] = {
+    "r02_row_mean": _rw("r02_row_mean", "x.mean(dim=-1)", (64, 1024), ("out", "f32"),
+                        [SUM, ("scalar", S("m", "divide", "acc0", "n_cols")), ("row", "m")],
+                        lambda x: x.mean(-1), 1e-5, 1e-5, EXACT),
+    "r03_row_amax": _rw("r03_row_amax", "x.amax(dim=-1)", (64, 1000), ("out", "f32"),
+                        [MAX, ("row", "acc0")], lambda x: x.max(-1), 0, 0, EXACT),
+    "r04_row_sum_odd": _rw("r04_row_sum_odd", "x.sum(dim=-1)", (37, 777), ("out", "f32"),
+                           [SUM, ("row", "acc0")], lambda x: x.sum(-1), 1e-5, 1e-5, EXACT),
+    "r05_sum_squares": _rw("r05_sum_squares", "(x * x).sum(dim=-1)", (32, 2048),
+                           ("out", "f32"), [SUMSQ, ("row", "acc0")],
+                           lambda x: (x * x).sum(-1), 1e-5, 1e-5, EXACT),
+    "r11_t64_rows": _rw("r11_t64_rows", "x.sum(dim=-1), 64 threads a row", (128, 512),
+                        ("out", "f32"), [SUM, ("row", "acc0")], lambda x: x.sum(-1),
+                        1e-5, 1e-5, EXACT, block=64),
+    "r12_t32_rows": _rw("r12_t32_rows", "x.sum(dim=-1), one warp a row", (128, 256),
+                        ("out", "f32"), [SUM, ("row", "acc0")], lambda x: x.sum(-1),
+                        1e-5, 1e-5, EXACT, block=32),
+    "r21_f16_rowsum": _rw("r21_f16_rowsum", "f16 x.sum(dim=-1) in f32", (32, 1024),
+                          ("out", "f32"), [SUM, ("row", "acc0")], lambda x: x.sum(-1),
+                          1e-3, 1e-3, EXACT, dtype="f16"),
+    "f00_softmax_1000": _rw("f00_softmax_1000", "torch.softmax(x, dim=-1)", (32, 1000),
+                            ("out", "f32"),
+                            [MAX, ("reduce", "acc1", "add", [S("d", "subtract", "xv", "acc0"),
+                                                            S("e", "exp", "d")], "e"),
+                             ("scalar", S("r", "reciprocal", "acc1")),
+                             ("write", [S("d2", "subtract", "xv", "acc0"), S("e2", "exp", "d2"),
+                                        S("y", "multiply", "e2", "r")], "y")],
+                            _softmax, 1e-3, 1e-5, FAST_REL),
+    "f01_rmsnorm_2048": _rw("f01_rmsnorm_2048", "x * rsqrt(mean(x^2) + 1e-6)", (16, 2048),
+                            ("out", "f32"),
+                            [SUMSQ, ("scalar", S("ms", "divide", "acc0", "n_cols")),
+                             ("scalar", S("mse", "add", "ms", "c_eps")),
+                             ("scalar", S("inv", "rsqrt", "mse")),
+                             ("write", [S("y", "multiply", "xv", "inv")], "y")],
+                            lambda x: x / np.sqrt((x * x).mean(-1, keepdims=True) + 1e-6),
+                            1e-4, 1e-5, FAST_REL, consts={"c_eps": 1e-6}),
+    "f04_l2norm_eps": _rw("f04_l2norm_eps", "x / (x.norm(dim=-1) + 1e-6)", (32, 1024),
+                          ("out", "f32"),
+                          [SUMSQ, ("scalar", S("nrm", "sqrt", "acc0")),
+                           ("scalar", S("den", "add", "nrm", "c_eps")),
+                           ("write", [S("y", "divide", "xv", "den")], "y")],
+                          lambda x: x / (np.sqrt((x * x).sum(-1, keepdims=True)) + 1e-6),
+                          1e-5, 1e-5, EXACT, consts={"c_eps": 1e-6}),
+    "f08_layernorm": _rw("f08_layernorm", "torch.nn.functional.layer_norm(x, (768,))",
+                         (16, 768), ("out", "f32"),
+                         [SUM, ("scalar", S("mu", "divide", "acc0", "n_cols")),
+                          ("reduce", "acc1", "add", [S("c", "subtract", "xv", "mu"),
+                                                     S("c2", "multiply", "c", "c")], "c2"),
+                          ("scalar", S("var", "divide", "acc1", "n_cols")),
+                          ("scalar", S("vare", "add", "var", "c_eps")),
+                          ("scalar", S("inv", "rsqrt", "vare")),
+                          ("write", [S("cc", "subtract", "xv", "mu"),
+                                     S("y", "multiply", "cc", "inv")], "y")],
+                         lambda x: (x - x.mean(-1, keepdims=True))
+                         / np.sqrt(x.var(-1, keepdims=True) + 1e-5),
+                         1e-4, 1e-4, FAST_REL, consts={"c_eps": 1e-5}),
+    "f12_log_softmax": _rw("f12_log_softmax", "torch.log_softmax(x, dim=-1)", (32, 512),
+                           ("out", "f32"),
+                           [MAX, ("reduce", "acc1", "add", [S("d", "subtract", "xv", "acc0"),
+                                                           S("e", "exp", "d")], "e"),
+                            ("scalar", S("lse", "log", "acc1")),
+                            ("write", [S("d2", "subtract", "xv", "acc0"),
+                                       S("y", "subtract", "d2", "lse")], "y")],
+                           lambda x: np.log(_softmax(x)), 1e-4, 1e-5, FAST_REL),
+}
+
+AXES: dict[str, Callable[[], SuiteCase]] = {
+    "r06_col_sum": lambda: SuiteCase(axis_reduce("r06_col_sum", "x.sum(dim=0)", (1, 512, 384),
+                                                 "add", False), lambda x: x.sum(1),
+                                     1e-4, 1e-4, EXACT),
+    "r18_amax_mid": lambda: SuiteCase(axis_reduce("r18_amax_mid", "x.amax(dim=1)",
+                                                  (8, 64, 96), "maximum", False),
+                                      lambda x: x.max(1), 0, 0, EXACT),
+    "r19_mean_mid_axis": lambda: SuiteCase(axis_reduce("r19_mean_mid_axis", "x.mean(dim=1)",
+                                                       (16, 100, 48), "add", True),
+                                           lambda x: x.mean(1), 1e-5, 1e-5, EXACT),
+    "r16_grid_atomic": lambda: SuiteCase(grid_reduce("r16_grid_atomic", "x.sum()", 1 << 18,
+                                                     False), lambda x: np.atleast_1d(x.sum()),
+                                         1e-5, 1e-5, ATOMIC),
+    "r05b_grid_sum_squares": lambda: SuiteCase(grid_reduce("r05b_grid_sum_squares",
+                                                           "(x * x).sum()", 100_003, True),
+                                               lambda x: np.atleast_1d((x * x).sum()),
+                                               1e-5, 1e-5, ATOMIC),
+}
+
+
+def _mm(pid: str, m: int, n: int, k: int, **kw: Any) -> Callable[[], SuiteCase]:
+    def make() -> SuiteCase:
+        spec = matmul(m, n, k, dtype="f32", raster_group=None, **kw)
+        spec.meta["id"] = pid
+        return SuiteCase(spec, lambda x0, x1: x0 @ x1, 1e-3, 1e-3, EXACT)
+    return make
+
+
+MATMUL: dict[str, Callable[[], SuiteCase]] = {
+    "m00_256x128x256": _mm("m00_256x128x256", 256, 256, 128, bm=64, bn=64, bk=16, block=256),
+    "m01_64sq": _mm("m01_64sq", 64, 64, 64, bm=64, bn=64, bk=16, block=256),
+    "m03_tall": _mm("m03_tall", 1024, 32, 64, bm=64, bn=32, bk=16, block=128),
+    "m04_deep_k": _mm("m04_deep_k", 32, 128, 1024, bm=32, bn=64, bk=32, block=128),
+}
+
+SUITE: dict[str, Callable[[], SuiteCase]] = {**POINTWISE, **ROWWISE, **AXES, **MATMUL}
+
+
+def ref_inputs(case: SuiteCase, inputs: dict[str, np.ndarray]) -> list[np.ndarray]:
+    """The case's graph inputs in graph-input order, in their own dtypes (bf16 as the f32
+    values of its bits), so a formula computes in NumPy the way the reference's does."""
+    from .problems import bf16_values
+
+    out = []
+    for name in case.spec.meta["graph_inputs"]:
+        a = next(x for x in case.spec.kernel["args"] if x["name"] == name)
+        v = inputs[name]
+        out.append(bf16_values(v) if a["dtype"] == "bf16" else v)
+    return out

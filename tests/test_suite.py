@@ -1,0 +1,53 @@
+"""The op/dtype suite (``ptxgen.suite``) on the CPU: every case compiles to PTX that ptxas
+accepts for sm_100a under each flag set, and the oracle's run of its Kernel IR meets the
+reference's NumPy formula for that problem within the reference's tolerance. This pins each
+generated IR to the reference's problem and the oracle to its semantics; the GPU tests then hold
+the kernels to the oracle."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+from conftest import oracle_run, reference_inputs
+from test_compile import FLAG_SETS, assert_plain_tma, ptxas
+
+from ptxgen.compiler import to_ptx
+from ptxgen.ir import Graph
+from ptxgen.suite import SUITE, ref_inputs
+
+
+def as_values(case, got: np.ndarray) -> np.ndarray:
+    from ptxgen.problems import bf16_values
+
+    return bf16_values(got) if case.out_dtype == "bf16" else got
+
+
+@pytest.mark.parametrize("name", sorted(SUITE))
+def test_suite_compiles(name: str, tmp_path) -> None:
+    spec = SUITE[name]().spec
+    for flags in FLAG_SETS:
+        ptx = to_ptx(Graph.from_dict(spec.graph), spec.meta, **flags)
+        assert ".target sm_100a" in ptx
+        assert_plain_tma(ptx)
+        if not flags:
+            ptxas(ptx, tmp_path)
+
+
+@pytest.mark.parametrize("name", sorted(SUITE))
+def test_suite_oracle_meets_reference_formula(name: str) -> None:
+    case = SUITE[name]()
+    ins = reference_inputs(case.spec.meta)
+    got = as_values(case, oracle_run(case.spec.graph, case.spec.meta, ins)[case.out])
+    want = np.asarray(case.ref(*ref_inputs(case, ins)))
+    got, want = got.astype(np.float64).reshape(want.shape), want.astype(np.float64)
+    np.testing.assert_allclose(got, want, rtol=case.rtol, atol=case.atol)
+
+
+def test_packed_add_of_a_product_stays_scalar() -> None:
+    """With fusion off, a multiply feeding an add must stay two roundings: the SLP pass keeps
+    such an add scalar (its explicit .rn forbids ptxas to contract), since the packed f32x2
+    forms came out contracted on a B200."""
+    spec = SUITE["p07_fma3"]().spec
+    ptx = to_ptx(Graph.from_dict(spec.graph), spec.meta, no_fusion=True)
+    assert "add.rn.f32x2" not in ptx and "fma.rn" not in ptx
+    assert ptx.count("add.rn.f32 ") == 4
