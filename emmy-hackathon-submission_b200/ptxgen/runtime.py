@@ -3,7 +3,8 @@
 ``Module`` loads a PTX module, ``Module.kernel`` finds an entry, and ``Kernel.launch`` starts it
 on device pointers. ``Problem`` is one meta.json kernel end to end: compile the IR, allocate the
 buffers (PyTorch is used for device memory only), fill its inputs, zero ``zero_outputs``, launch
-with meta.json's geometry, and read the status word.
+with meta.json's geometry, and read the status word. ``ProblemSet`` runs a meta.json problem of
+several kernels in order, chaining the intermediates one kernel writes into the next.
 
 The emitted module states the launch it was compiled for in ``// @ptxgen`` header lines
 (``launch grid=G block=B``, ``dynamic_smem=N``, ``tensormap ...``); a launch that disagrees is
@@ -346,3 +347,63 @@ class Problem:
             status = self.module.status()
             if status:
                 raise KernelStatusError(f"{launch['entry']}: status word 0x{status:08x}")
+
+
+# --- problems of several kernels -----------------------------------------------------------------
+
+
+def problem_args(meta: dict[str, Any]) -> dict[str, dict[str, Any]]:
+    """Every buffer a meta.json problem names, once, checked for chaining: an ``intermediate``
+    argument (reference ``tools/generate.py:142-144``: neither written by its kernel nor an
+    input or a constant) must be an output of an earlier kernel, of the same dtype and size."""
+    out: dict[str, dict[str, Any]] = {}
+    written: set[str] = set()
+    for k in meta["kernels"]:
+        for a in k["args"]:
+            seen = out.get(a["name"])
+            if a.get("intermediate") and a["name"] not in written:
+                raise ValueError(f"{k['entry']}: intermediate {a['name']!r} is not written by "
+                                 "an earlier kernel")
+            if seen is not None and (seen["dtype"] != a["dtype"] or
+                                     int(np.prod(seen["shape"] or [1])) !=
+                                     int(np.prod(a["shape"] or [1]))):
+                raise ValueError(f"{k['entry']}: {a['name']!r} disagrees with an earlier kernel")
+            out.setdefault(a["name"], a)
+        written |= {a["name"] for a in k["args"] if a.get("output")}
+    return out
+
+
+class ProblemSet:
+    """A meta.json problem of one or more kernels: each kernel has its own ``<entry>.ir.json``
+    (reference ``tools/generate.py:180-199``) and they run in meta.json order on one stream,
+    each after its own zero_outputs are cleared, every buffer shared by name, so an
+    intermediate one kernel writes is what the next one reads."""
+
+    def __init__(self, graphs: dict[str, dict[str, Any]], meta: dict[str, Any],
+                 flags: dict[str, bool] | None = None, device: int | None = None):
+        self.meta = meta
+        self.args = problem_args(meta)
+        self.problems = [Problem(graphs[k["entry"]], meta, flags=dict(flags or {}),
+                                 device=device) for k in meta["kernels"]]
+
+    @classmethod
+    def from_dir(cls, path: str | Path, **flags: bool) -> ProblemSet:
+        path = Path(path)
+        meta = json.loads((path / "meta.json").read_text())
+        graphs = {k["entry"]: json.loads((path / f"{k['entry']}.ir.json").read_text())
+                  for k in meta["kernels"]}
+        return cls(graphs, meta, flags)
+
+    def allocate(self, extra_guard: int = 0) -> dict[str, Any]:
+        """Device tensors for every buffer of every kernel (uninitialised)."""
+        import torch
+
+        dev = self.problems[0]._dev()
+        return {name: torch.empty(int(np.prod(a["shape"] or [1])) + extra_guard,
+                                  dtype=torch_dtype(a["dtype"]), device=f"cuda:{dev}")
+                for name, a in self.args.items()}
+
+    def launch(self, tensors: dict[str, Any], stream: int | None = None,
+               check_status: bool = False) -> None:
+        for p in self.problems:
+            p.launch(tensors, stream, check_status=check_status)

@@ -14,7 +14,10 @@ the statement shapes of the shipped IRs (``ptxgen.problems`` documents them):
   multiple of the block;
 * column and middle-axis reductions (a Loop over the reduced axis per output element) and a
   grid-stride reduction with an atomic Write;
-* small f32 matmuls through the SIMT nest (the ``m`` category's shapes).
+* small f32 matmuls through the SIMT nest (the ``m`` category's shapes);
+* problems of two kernels chained through ``intermediate`` buffers (reference
+  ``tools/generate.py:142-144``): the grid-kernel reduce plan (per-block partials, then one
+  block over them) and a two-pass softmax (row statistics, then a pointwise normalisation).
 
 Each case keeps the reference id it stands for, its NumPy formula (restated from the
 reference's ``ref`` of that id, computing in the inputs' dtypes as it does), the reference's
@@ -31,7 +34,8 @@ from typing import Any
 import numpy as np
 
 from .ir import (Accum, Assign, Axis, BinaryExpr, Cond, Dim, Init, Let, Literal, Load, Loop,
-                 Stmt, StridedLoop, Tile, Write, dt)
+                 Stmt, StridedLoop, TensorSpec, Tile, Write, constant_node, dt, input_node,
+                 kernel_node)
 from .problems import I, ProblemSpec, V, _arg, _block_reduce, _spec, add, div, matmul, mul, op, \
     rem
 
@@ -577,3 +581,150 @@ def ref_inputs(case: SuiteCase, inputs: dict[str, np.ndarray]) -> list[np.ndarra
         v = inputs[name]
         out.append(bf16_values(v) if a["dtype"] == "bf16" else v)
     return out
+
+
+# --- problems of several kernels ---------------------------------------------------------------
+
+
+@dataclass
+class MultiSpec:
+    """A problem of several kernels: one Kernel IR graph per kernel entry, one meta.json."""
+
+    graphs: dict[str, dict[str, Any]]
+    meta: dict[str, Any]
+
+    def write(self, directory: Any) -> Any:
+        import json
+        from pathlib import Path
+
+        d = Path(directory)
+        d.mkdir(parents=True, exist_ok=True)
+        for entry, g in self.graphs.items():
+            (d / f"{entry}.ir.json").write_text(json.dumps(g, indent=2))
+        (d / "meta.json").write_text(json.dumps(self.meta, indent=1))
+        return d
+
+
+@dataclass
+class Kern:
+    entry: str
+    tile: Tile
+    args: list[dict[str, Any]]  # in arg order; outputs marked, chained buffers "intermediate"
+    block: int
+    zero_outputs: Sequence[str] = ()
+
+
+def _multi(pid: str, code: str, kernels: list[Kern], inputs: list[str], outputs: list[str],
+           consts: dict[str, float]) -> MultiSpec:
+    """Per-kernel graphs and the meta.json of a chained problem, as the reference's packager
+    lays it out: one ``<entry>.ir.json`` per kernel, meta.json's kernels in launch order."""
+    graphs, metas = {}, []
+    for k in kernels:
+        specs = {a["name"]: TensorSpec(a["name"], tuple(a["shape"]), a["dtype"]) for a in k.args}
+        nodes: dict[str, Any] = {}
+        for a in k.args:
+            if "data" in a:
+                nodes[a["name"]] = constant_node(a["name"], consts[a["name"]])
+            elif not a.get("output"):
+                nodes[a["name"]] = input_node(specs[a["name"]])
+        outs = [a["name"] for a in k.args if a.get("output")]
+        nodes[outs[0]] = kernel_node(k.entry, k.tile,
+                                     [a["name"] for a in k.args if not a.get("output")],
+                                     [specs[o] for o in outs])
+        graphs[k.entry] = {"inputs": [a["name"] for a in k.args
+                                      if not a.get("output") and "data" not in a],
+                           "outputs": outs, "nodes": nodes}
+        metas.append({"node": outs[0], "entry": k.entry, "arg_order": [a["name"] for a in k.args],
+                      "grid": [-(-k.tile.n_elements // k.block), 1, 1], "block": [k.block, 1, 1],
+                      "smem_bytes": 0, "zero_outputs": list(k.zero_outputs), "args": k.args,
+                      "final": bool(set(outs) & set(outputs))})
+    meta = {"id": pid, "code": code, "rtol": 0, "atol": 0, "graph_inputs": inputs,
+            "graph_outputs": outputs, "kernels": metas}
+    return MultiSpec(graphs, meta)
+
+
+def grid_kernel_sum(n: int = 1 << 20, block: int = 256, blocks: int = 128) -> MultiSpec:
+    """sum(x) by the grid-kernel plan: kernel 1 reduces a grid-stride share per block and
+    writes each block's total into ``partials`` [blocks]; kernel 2, one block, sums those. No
+    atomics, so the result is deterministic."""
+    ab, at = V("a0_b"), V("a0_t")
+    k1 = Tile((Axis("a0_b", Dim(blocks)), Axis("a0_t", Dim(block))), (
+        StridedLoop(Axis("a0", Dim(n)), add(mul(ab, I(block)), at), I(block * blocks),
+                    (Load(("xv",), "x", (V("a0"),), dt("f32")),
+                     Accum("acc0", "xv", op("add"), dt("f32"), ("a0",), None)),
+                    False, None, True),
+        *_block_reduce("acc0", "add", block, "acc0_smem"),
+        Cond(BinaryExpr("==", at, I(0)), (Write("partials", (ab,), ("acc0",), dt("f32")),), ()),
+    ), block)
+    t2 = V("a0_t")
+    k2 = Tile((Axis("a0_b", Dim(1)), Axis("a0_t", Dim(block))), (
+        StridedLoop(Axis("a1", Dim(blocks)), t2, I(block),
+                    (Load(("pv",), "partials", (V("a1"),), dt("f32")),
+                     Accum("acc1", "pv", op("add"), dt("f32"), ("a1",), None)),
+                    False, None, True),
+        *_block_reduce("acc1", "add", block, "acc1_smem"),
+        Cond(BinaryExpr("==", t2, I(0)), (Write("out", (), ("acc1",), dt("f32")),), ()),
+    ), block)
+    return _multi("r17_grid_kernel", "x.sum() (grid-kernel reduce plan)", [
+        Kern("k_sum_partials", k1, [_arg("x", "f32", [n], seed=0),
+                                    _arg("partials", "f32", [blocks], output=True)], block),
+        Kern("k_sum_final", k2, [_arg("partials", "f32", [blocks], intermediate=True),
+                                 _arg("out", "f32", [1], output=True)], block),
+    ], ["x"], ["out"], {})
+
+
+def two_pass_softmax(rows: int = 64, cols: int = 1024, block: int = 128) -> MultiSpec:
+    """softmax(x, dim=-1) in two kernels: a row pass writes each row's max and sum of
+    exp(x - max) into ``row_max`` and ``row_sum`` [rows]; a pointwise pass over all elements
+    reads them by row and writes exp(x - max) / sum."""
+    a0, t = V("a0"), V("a1_co")
+    sweep = lambda body: StridedLoop(Axis("a1", Dim(cols)), t, I(block), tuple(body),  # noqa
+                                     False, None, True)
+    k1 = Tile((Axis("a0", Dim(rows)), Axis("a1_co", Dim(block))), (
+        sweep([Load(("x0",), "x", (a0, V("a1")), dt("f32")),
+               Accum("acc0", "x0", op("maximum"), dt("f32"), ("a1",), None)]),
+        *_block_reduce("acc0", "maximum", block, "acc0_smem"),
+        sweep([Load(("x1",), "x", (a0, V("a1")), dt("f32")),
+               Assign("d", op("subtract"), ("x1", "acc0"), dt("f32")),
+               Assign("e", op("exp"), ("d",), dt("f32")),
+               Accum("acc1", "e", op("add"), dt("f32"), ("a1",), None)]),
+        *_block_reduce("acc1", "add", block, "acc1_smem"),
+        Cond(BinaryExpr("==", t, I(0)), (Write("row_max", (a0,), ("acc0",), dt("f32")),
+                                          Write("row_sum", (a0,), ("acc1",), dt("f32"))), ()),
+    ), block)
+    e0, pw = V("a0"), 256
+    k2 = Tile((Axis("a0", Dim(rows * cols)),), (
+        Load(("xv",), "x", (e0,), dt("f32")),
+        Load(("mx",), "row_max", (div(e0, I(cols)),), dt("f32")),
+        Load(("sm",), "row_sum", (div(e0, I(cols)),), dt("f32")),
+        Assign("d", op("subtract"), ("xv", "mx"), dt("f32")),
+        Assign("e", op("exp"), ("d",), dt("f32")),
+        Assign("y", op("divide"), ("e", "sm"), dt("f32")),
+        Write("out", (e0,), ("y",), dt("f32")),
+    ), None)
+    return _multi("f13_softmax_two_pass", "torch.softmax(x, dim=-1) in two kernels", [
+        Kern("k_softmax_stats", k1, [_arg("x", "f32", [rows, cols], seed=0),
+                                     _arg("row_max", "f32", [rows], output=True),
+                                     _arg("row_sum", "f32", [rows], output=True)], block),
+        Kern("k_softmax_normalise", k2, [_arg("x", "f32", [rows, cols], seed=0),
+                                         _arg("row_max", "f32", [rows], intermediate=True),
+                                         _arg("row_sum", "f32", [rows], intermediate=True),
+                                         _arg("out", "f32", [rows, cols], output=True)], pw),
+    ], ["x"], ["out"], {})
+
+
+@dataclass
+class MultiCase:
+    spec: MultiSpec
+    ref: Callable[..., np.ndarray]
+    rtol: float
+    atol: float
+    bar: tuple[str, float]
+
+
+MULTI: dict[str, Callable[[], MultiCase]] = {
+    "r17_grid_kernel": lambda: MultiCase(grid_kernel_sum(), lambda x: np.atleast_1d(x.sum()),
+                                         1e-5, 1e-5, EXACT),
+    "f13_softmax_two_pass": lambda: MultiCase(two_pass_softmax(), _softmax, 1e-3, 1e-5,
+                                              FAST_REL),
+}

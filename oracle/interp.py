@@ -859,3 +859,14 @@ def run_kernel(graph: Graph | dict[str, Any], meta: dict[str, Any],
                inputs: dict[str, np.ndarray], no_fusion: bool = False) -> dict[str, np.ndarray]:
     """The output buffers of the meta.json kernel on ``inputs`` (bf16 as uint16 bits or f32)."""
     return Interpreter(graph, meta, inputs, Options(no_fusion=no_fusion)).run()
+
+
+def run_problem(graphs: dict[str, Graph | dict[str, Any]], meta: dict[str, Any],
+                inputs: dict[str, np.ndarray], no_fusion: bool = False
+                ) -> dict[str, np.ndarray]:
+    """Every buffer a meta.json problem of several kernels writes: each kernel, in meta.json
+    order, runs on the inputs and on what the kernels before it wrote (its intermediates)."""
+    env = dict(inputs)
+    for k in meta["kernels"]:
+        env.update(run_kernel(graphs[k["entry"]], meta, env, no_fusion=no_fusion))
+    return {name: v for name, v in env.items() if name not in inputs}

@@ -12,7 +12,7 @@ import pytest
 from conftest import gpu_run, oracle_run, reference_inputs
 from test_gpu_parity import check
 
-from ptxgen.suite import SUITE
+from ptxgen.suite import MULTI, SUITE
 
 pytestmark = pytest.mark.gpu
 
@@ -29,3 +29,32 @@ def test_suite_parity(cuda, name: str, flags: dict) -> None:
                       no_fusion=flags.get("no_fusion", False))[case.out]
     kind, bound = case.bar
     check(kind, got.reshape(want.shape), want, case.out_dtype, bound)
+
+
+@pytest.mark.parametrize("name", sorted(MULTI))
+def test_multi_kernel_parity(cuda, name: str) -> None:
+    """A chained problem through ``ProblemSet``: the kernels in meta.json order on one stream,
+    the intermediates one writes read by the next, against the oracle's chained run."""
+    import numpy as np
+    import torch
+    from test_suite import multi_inputs
+
+    from oracle.interp import run_problem
+    from ptxgen.runtime import ProblemSet
+
+    case = MULTI[name]()
+    ins = multi_inputs(case.spec.meta)
+    ps = ProblemSet(case.spec.graphs, case.spec.meta)
+    tensors = ps.allocate()
+    for n, t in tensors.items():
+        if n in ins:
+            t.copy_(torch.from_numpy(np.ascontiguousarray(ins[n]).reshape(-1)))
+        else:
+            t.fill_(float("nan"))
+    ps.launch(tensors, check_status=True)
+    torch.cuda.synchronize()
+    want = run_problem(case.spec.graphs, case.spec.meta, ins)
+    for out in case.spec.meta["graph_outputs"]:
+        got = tensors[out].cpu().numpy()
+        kind, bound = case.bar
+        check(kind, got, want[out].reshape(-1), "f32", bound)

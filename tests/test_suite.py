@@ -13,7 +13,7 @@ from test_compile import FLAG_SETS, assert_plain_tma, ptxas
 
 from ptxgen.compiler import to_ptx
 from ptxgen.ir import Graph
-from ptxgen.suite import SUITE, ref_inputs
+from ptxgen.suite import MULTI, SUITE, ref_inputs
 
 
 def as_values(case, got: np.ndarray) -> np.ndarray:
@@ -51,3 +51,53 @@ def test_packed_add_of_a_product_stays_scalar() -> None:
     ptx = to_ptx(Graph.from_dict(spec.graph), spec.meta, no_fusion=True)
     assert "add.rn.f32x2" not in ptx and "fma.rn" not in ptx
     assert ptx.count("add.rn.f32 ") == 4
+
+
+# --- problems of several kernels ---------------------------------------------------------------
+
+
+def multi_inputs(meta) -> dict[str, np.ndarray]:
+    from ptxgen.problems import seeded_input
+    from ptxgen.runtime import problem_args
+
+    return {n: seeded_input(a) for n, a in problem_args(meta).items()
+            if not a.get("output") and not a.get("intermediate")}
+
+
+@pytest.mark.parametrize("name", sorted(MULTI))
+def test_multi_kernel_problem_compiles_and_meets_formula(name: str, tmp_path) -> None:
+    from oracle.interp import run_problem
+
+    case = MULTI[name]()
+    for k in case.spec.meta["kernels"]:
+        ptxas(to_ptx(Graph.from_dict(case.spec.graphs[k["entry"]]), case.spec.meta), tmp_path)
+    ins = multi_inputs(case.spec.meta)
+    out = run_problem(case.spec.graphs, case.spec.meta, ins)["out"]
+    want = np.asarray(case.ref(*[ins[n] for n in case.spec.meta["graph_inputs"]]))
+    np.testing.assert_allclose(out.reshape(want.shape), want, rtol=case.rtol, atol=case.atol)
+
+
+def test_multi_kernel_dir_through_the_cli(tmp_path) -> None:
+    """The drop-in CLI compiles each kernel of a chained problem from its own IR file, reading
+    the shared meta.json beside it (reference compile.py:58-69)."""
+    import subprocess
+    import sys
+
+    from conftest import ROOT
+
+    case = MULTI["f13_softmax_two_pass"]()
+    d = case.spec.write(tmp_path / "f13")
+    for k in case.spec.meta["kernels"]:
+        r = subprocess.run([sys.executable, str(ROOT / "compile.py"),
+                            str(d / f"{k['entry']}.ir.json")], capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr
+        assert f".visible .entry {k['entry']}(" in r.stdout
+
+
+def test_intermediate_without_producer_is_rejected() -> None:
+    from ptxgen.runtime import problem_args
+
+    meta = MULTI["r17_grid_kernel"]().spec.meta
+    meta["kernels"] = meta["kernels"][1:]  # the consumer alone
+    with pytest.raises(ValueError, match="intermediate"):
+        problem_args(meta)
