@@ -15,6 +15,10 @@ the statement shapes of the shipped IRs (``ptxgen.problems`` documents them):
 * column and middle-axis reductions (a Loop over the reduced axis per output element) and a
   grid-stride reduction with an atomic Write;
 * small f32 matmuls through the SIMT nest (the ``m`` category's shapes);
+* fused attention, softmax(q @ kt * scale) @ v, in the shipped a01/a03 nest's shape: per query
+  row an inner product over d for each key, an online-softmax update of the running max, the
+  denominator and the numerators, then one reciprocal scaling (the ``a`` category, batched and
+  multi-head included);
 * problems of two kernels chained through ``intermediate`` buffers (reference
   ``tools/generate.py:142-144``): the grid-kernel reduce plan (per-block partials, then one
   block over them) and a two-pass softmax (row statistics, then a pointwise normalisation).
@@ -567,7 +571,7 @@ MATMUL: dict[str, Callable[[], SuiteCase]] = {
     "m04_deep_k": _mm("m04_deep_k", 32, 128, 1024, bm=32, bn=64, bk=32, block=128),
 }
 
-SUITE: dict[str, Callable[[], SuiteCase]] = {**POINTWISE, **ROWWISE, **AXES, **MATMUL}
+
 
 
 def ref_inputs(case: SuiteCase, inputs: dict[str, np.ndarray]) -> list[np.ndarray]:
@@ -581,6 +585,112 @@ def ref_inputs(case: SuiteCase, inputs: dict[str, np.ndarray]) -> list[np.ndarra
         v = inputs[name]
         out.append(bf16_values(v) if a["dtype"] == "bf16" else v)
     return out
+
+
+# --- fused attention ---------------------------------------------------------------------------
+
+
+def attention(pid: str, code: str, b: int, m: int, n: int, d: int, dv: int, scale: str,
+              value: float, rb: int, r: int, cb: int, c: int) -> ProblemSpec:
+    """softmax(q @ kt * s) @ v over f32 q [b, m, d], kt [b, d, n], v [b, n, dv] (b = 1: 2-D),
+    in the shipped a01 nest's shape (reference ``examples/op_fusion/a01_attention``): a Tile over
+    (batch,) row blocks of ``rb``, column blocks of ``cb`` and threads holding ``r`` rows x ``c``
+    columns; per key a1 an inner-product Loop over d per row, then per (row, column) the online
+    update -- running max ``mx``, alpha = exp(mx_old - mx_new), beta = exp(s - mx_new), the
+    denominator ``den`` <- alpha*den + beta and the numerator ``num`` <- alpha*num + beta*v --
+    and after the keys num / den. ``scale`` is "div" (s = score / value, as a reciprocal of the
+    ConstantOp), "mul" (s = score * value) or "none"."""
+    bt = b > 1
+    axes = ([Axis("ab", Dim(b))] if bt else []) + [
+        Axis("a0_b", Dim(m // rb)), Axis("a5_b", Dim(dv // cb)),
+        Axis("a0_u", Dim(rb // r)), Axis("a5_u", Dim(cb // c))]
+    block = (rb // r) * (cb // c)
+    bi: tuple[Any, ...] = (V("ab"),) if bt else ()
+    row = lambda i: add(add(mul(V("a0_b"), I(rb)), mul(V("a0_u"), I(r))), I(i))  # noqa: E731
+    col = add(mul(V("a5_b"), I(cb)), mul(V("a5_u"), I(c)))
+    body: list[Stmt] = []
+    consts: dict[str, float] = {}
+    if scale == "div":
+        consts["div_c1"] = value
+        body += [Load(("sc_in",), "div_c1", (I(0),), dt("f32")),
+                 Assign("sc", op("reciprocal"), ("sc_in",), dt("f32"))]
+    elif scale == "mul":
+        consts["mul_c1"] = value
+        body.append(Load(("sc",), "mul_c1", (I(0),), dt("f32")))
+    keys: list[Stmt] = []
+    for i in range(r):
+        keys.append(Loop(Axis("a2", Dim(d)), (
+            Load((f"q__r{i}",), "q", (*bi, row(i), V("a2")), dt("f32")),
+            Load((f"k__r{i}",), "kt", (*bi, V("a2"), V("a1")), dt("f32")),
+            Assign(f"qk__r{i}", op("multiply"), (f"k__r{i}", f"q__r{i}"), dt("f32")),
+            Accum(f"dot__r{i}", f"qk__r{i}", op("add"), dt("f32"), ("a2",), None))))
+    keys.append(Load(tuple(f"v__c{j}" for j in range(c)), "v", (*bi, V("a1"), col), dt("f32")))
+    for i in range(r):
+        s_ = f"dot__r{i}"
+        if scale != "none":
+            keys.append(Assign(f"s__r{i}", op("multiply"), (s_, "sc"), dt("f32")))
+            s_ = f"s__r{i}"
+        for j in range(c):
+            u = f"__r{i}c{j}"
+            keys += [
+                Let(f"one{u}", Literal(1.0, "float"), dt("f32")),
+                Assign(f"gn{u}", op("maximum"), (s_, f"mx{u}"), dt("f32")),
+                Assign(f"dg{u}", op("subtract"), (f"mx{u}", f"gn{u}"), dt("f32")),
+                Assign(f"alpha{u}", op("exp"), (f"dg{u}",), dt("f32")),
+                Assign(f"dgo{u}", op("subtract"), (s_, f"gn{u}"), dt("f32")),
+                Assign(f"beta{u}", op("exp"), (f"dgo{u}",), dt("f32")),
+                Assign(f"den_sa{u}", op("multiply"), (f"alpha{u}", f"den{u}"), dt("f32")),
+                Assign(f"den_sb{u}", op("multiply"), (f"beta{u}", f"one{u}"), dt("f32")),
+                Accum(f"den{u}", f"den_sb{u}", op("add"), dt("f32"), ("a1",), f"den_sa{u}"),
+                Assign(f"num_sa{u}", op("multiply"), (f"alpha{u}", f"num{u}"), dt("f32")),
+                Assign(f"num_sb{u}", op("multiply"), (f"beta{u}", f"v__c{j}"), dt("f32")),
+                Accum(f"num{u}", f"num_sb{u}", op("add"), dt("f32"), ("a1",), f"num_sa{u}"),
+                Accum(f"mx{u}", s_, op("maximum"), dt("f32"), ("a1",), None),
+            ]
+    body.append(Loop(Axis("a1", Dim(n)), tuple(keys)))
+    for i in range(r):
+        for j in range(c):
+            u = f"__r{i}c{j}"
+            body += [Assign(f"rcp{u}", op("reciprocal"), (f"den{u}",), dt("f32")),
+                     Assign(f"o{u}", op("multiply"), (f"num{u}", f"rcp{u}"), dt("f32")),
+                     Write("out", (*bi, row(i), add(col, I(j))), (f"o{u}",), dt("f32"))]
+    tile = Tile(tuple(axes), tuple(body), block)
+    lead = [b] if bt else []
+    args = [_arg(k, "f32", [1], data=[v]) for k, v in consts.items()]
+    args += [_arg("q", "f32", lead + [m, d], seed=0), _arg("kt", "f32", lead + [d, n], seed=1),
+             _arg("v", "f32", lead + [n, dv], seed=2),
+             _arg("out", "f32", lead + [m, dv], output=True)]
+    return _spec(pid, code, 1e-3, 1e-4, f"k_{pid}", tile, args, ["q", "kt", "v"], ["out"],
+                 consts, block)
+
+
+def _attn(scale: float) -> Callable[..., np.ndarray]:
+    def ref(q: np.ndarray, kt: np.ndarray, v: np.ndarray) -> np.ndarray:
+        q, kt, v = (x.astype(np.float64) for x in (q, kt, v))
+        return (_softmax(q @ kt * scale) @ v).astype(np.float32)
+    return ref
+
+
+def _at(pid: str, shape: tuple[int, int, int, int, int], scale: str, value: float,
+        layout: tuple[int, int, int, int]) -> Callable[[], SuiteCase]:
+    b, m, n, d, dv = shape
+    factor = {"div": 1.0 / value if value else 1.0, "mul": value, "none": 1.0}[scale]
+    code = (f"q [{b}, {m}, {d}], kt [{b}, {d}, {n}], v [{b}, {n}, {dv}]: "
+            f"torch.softmax(q @ kt {'/' if scale == 'div' else '*'} {value}, dim=-1) @ v")
+    return lambda: SuiteCase(attention(pid, code, b, m, n, d, dv, scale, value, *layout),
+                             _attn(factor), 1e-3, 1e-4, FAST_REL)
+
+
+ATTENTION: dict[str, Callable[[], SuiteCase]] = {
+    "a00_small": _at("a00_small", (1, 32, 32, 16, 16), "div", 4.0, (32, 4, 16, 2)),
+    "a01_256": _at("a01_256", (1, 256, 256, 64, 64), "div", 8.0, (32, 4, 64, 2)),
+    "a02_rect": _at("a02_rect", (1, 64, 128, 32, 64), "mul", 0.1767767, (32, 4, 64, 2)),
+    "a03_noscale": _at("a03_noscale", (1, 64, 64, 64, 64), "none", 0.0, (32, 4, 64, 2)),
+    "a04_batched": _at("a04_batched", (2, 64, 64, 32, 32), "div", 5.656854, (32, 4, 32, 2)),
+    "a05_heads": _at("a05_heads", (4, 32, 48, 16, 16), "mul", 0.25, (32, 4, 16, 2)),
+    "a06_long_kv": _at("a06_long_kv", (1, 16, 512, 64, 64), "div", 8.0, (16, 2, 64, 2)),
+    "a07_tall_q": _at("a07_tall_q", (1, 256, 64, 16, 16), "div", 4.0, (64, 4, 16, 2)),
+}
 
 
 # --- problems of several kernels ---------------------------------------------------------------
@@ -728,3 +838,7 @@ MULTI: dict[str, Callable[[], MultiCase]] = {
     "f13_softmax_two_pass": lambda: MultiCase(two_pass_softmax(), _softmax, 1e-3, 1e-5,
                                               FAST_REL),
 }
+
+
+SUITE: dict[str, Callable[[], SuiteCase]] = {**POINTWISE, **ROWWISE, **AXES, **MATMUL,
+                                             **ATTENTION}
