@@ -49,6 +49,9 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--scaling", choices=("weak", "strong"), default="weak",
                    help="weak: each GPU keeps a full benchmark-sized share of an N-times larger "
                         "problem; strong: the GPUs split the benchmark size")
+    p.add_argument("--share", type=int, default=1,
+                   help="on one GPU, run one share of a K-way strong split of the workload (a "
+                        "smaller case of the same kernel, e.g. for a profiler capture)")
     p.add_argument("--l2", choices=("write", "clean"), default="write",
                    help="write: flush L2 with a 256 MiB write before each timed step, leaving it "
                         "full of dirty lines the next kernel writes back; clean: follow that write "
@@ -393,10 +396,17 @@ def run_ours(args: argparse.Namespace) -> None:
         tdist.barrier()
     init(local_rank)
     pk, pk_kind = peaks()
+    if args.share > 1 and world > 1:
+        raise SystemExit("--share runs a share of the workload on one GPU; use it without torchrun")
+
+    def plan_for(name: str) -> Any:
+        if args.share > 1:
+            return shard.local_problem(name, args.share)
+        return shard.local_problem(name, world, weak=args.scaling == "weak")
 
     def one(name: str, steps: int, warmup: int, with_e2e: bool) -> dict[str, Any]:
         log(f"{name}: compile and inputs")
-        plan = shard.local_problem(name, world, weak=args.scaling == "weak")
+        plan = plan_for(name)
         unit, bound, scale = unit_of(plan)
         m = measure_kernel(plan, steps, warmup, world, args.l2)
         per_rank = plan.work / (m["mean_ms"] / 1e3) / scale
@@ -434,7 +444,7 @@ def run_ours(args: argparse.Namespace) -> None:
     log("measurements done")
     if rank != 0:
         return
-    plan = shard.local_problem(args.workload, world, weak=args.scaling == "weak")
+    plan = plan_for(args.workload)
     cpu = cpu_baseline(args.workload, plan, args.cpu_seconds) if world == 1 else None
     line = {
         "metric": "Kernel time: HBM GB/s (% of ~8 TB/s), GEMM TFLOPS (% peak) at 1/2/4/8 B200",
@@ -444,6 +454,7 @@ def run_ours(args: argparse.Namespace) -> None:
         "data": "synthetic (seeded, the configuration's distributions, generated on the GPU)",
         "config": {"workload": args.workload, "per_rank": plan.spec.meta["id"],
                    "parallelism": f"tile-axis x{world}" if world > 1 else "single GPU",
+                   "share": f"1/{args.share} of the workload" if args.share > 1 else "whole",
                    "l2": ("flushed (256 MiB write) before every timed step" if args.l2 == "write"
                           else "flushed (256 MiB write, then a 256 MiB read: clean) before "
                                "every timed step"),
