@@ -9,6 +9,10 @@ it writes are committed, so tests never read the reference at run time.
 * ``literals.json`` -- PTX immediates of a set of values written by the reference's own literal
   encoder (``ptxgen/dtypes.py:60-76``, importable without Emmy), and bf16 roundings by its
   packaging rule (``tools/generate.py:57-60``).
+* ``fastmath.json`` -- the instruction sequence each of the reference's fast-math functions
+  (``ptxgen/fastmath.py:23-74``, importable without Emmy) writes into its PTX builder for one
+  input register (two for pow): opcode and operands per instruction, registers renamed in
+  order of first appearance.
 """
 
 from __future__ import annotations
@@ -40,6 +44,7 @@ def _load(path: Path, name: str):
     spec = importlib.util.spec_from_file_location(name, path)
     mod = importlib.util.module_from_spec(spec)
     assert spec.loader is not None
+    sys.modules[name] = mod  # dataclasses look their module up while it loads
     spec.loader.exec_module(mod)
     return mod
 
@@ -68,6 +73,17 @@ def main() -> None:
         "bf16_inputs_f32_bits": [int(x) for x in xs.view(np.uint32)],
         "bf16_rounded_f32_bits": [int(x) for x in rounded],
     }, indent=1))
+    # the reference's fastmath imports ``ptxgen.builder`` and ``ptxgen.dtypes``: its own files
+    sys.modules["ptxgen.dtypes"] = dtypes
+    builder = _load(REFERENCE / "ptxgen" / "builder.py", "ptxgen.builder")
+    fastmath = _load(REFERENCE / "ptxgen" / "fastmath.py", "ref_fastmath")
+    seqs = {}
+    for name, fn in fastmath.F32_FUNCS.items():
+        k = builder.PTXKernel("t", [], 32)
+        ins = ["%in0", "%in1"][:2 if name == "pow" else 1]
+        out = fn(k, *ins)
+        seqs[name] = {"body": [line.strip().rstrip(";") for line in k.body], "out": out}
+    (HERE / "fastmath.json").write_text(json.dumps(seqs, indent=1))
     print("fixtures written to", HERE)
 
 

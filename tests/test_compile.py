@@ -260,3 +260,41 @@ def test_splitk_config_fills_the_sms() -> None:
     """Config 5b (16 pair tiles of 1024 K blocks): 9 splits, two full waves over 74 SM pairs."""
     table, ctas = gemm_plan(problems.CONFIGS["c5b_matmul_splitk"]()).segments()
     assert (len(table), ctas) == (144, 148)
+
+
+def _normalised(lines: list[str]) -> list[str]:
+    """Instruction lines with registers renamed by first appearance (inputs kept), and the
+    explicit ``.rn`` of an f32 mul/add dropped: a lone IEEE multiply or add rounds to nearest
+    either way, the suffix only bars ptxas from contracting it with a neighbour."""
+    names: dict[str, str] = {}
+
+    def rename(m: re.Match) -> str:
+        r = m.group(0)
+        if r.startswith("%in"):
+            return r
+        return names.setdefault(r, f"%v{len(names)}")
+
+    out = []
+    for line in lines:
+        line = line.strip().rstrip(";").replace("mul.rn.f32 ", "mul.f32 ").replace(
+            "add.rn.f32 ", "add.f32 ")
+        out.append(re.sub(r"%[a-z]+\d+", rename, line))
+    return out
+
+
+@pytest.mark.parametrize("name", ["exp", "log", "pow", "tanh", "erf", "sin", "cos", "sigmoid"])
+def test_fastmath_matches_reference_sequence(name: str) -> None:
+    """Each fast-math function emits the instruction sequence the reference's does (fixture
+    ``tests/golden/fastmath.json``, written by the reference's own ``ptxgen/fastmath.py``), so a
+    fast-math result is the reference's bit for bit on the same hardware."""
+    from conftest import ROOT
+
+    from ptxgen.fastmath import F32_FUNCS
+    from ptxgen.ptx import Kernel
+
+    golden = json.loads((ROOT / "tests" / "golden" / "fastmath.json").read_text())[name]
+    k = Kernel("t", [], 32)
+    out = F32_FUNCS[name](k, *["%in0", "%in1"][:2 if name == "pow" else 1])
+    ours = _normalised([ins.render() for ins in k.body] + [f"result {out}"])
+    want = _normalised(golden["body"] + [f"result {golden['out']}"])
+    assert ours == want
