@@ -351,8 +351,25 @@ def measure_e2e(plan: Any, prob: Any, tensors: dict[str, Any], steps: int, world
             "in_flight": len(lanes)}
 
 
-def cpu_baseline(name: str, plan: Any, seconds: float) -> dict[str, Any]:
-    """The NumPy path of the same configuration on a bounded sample, timed on this host."""
+# inputs the CPU path splits across threads: contiguous rows / elements of each
+_SPLIT = {"c1_vector_add": ("x", "y"), "c2_gelu_chain": ("x", "s"), "c3_row_softmax": ("x",),
+          "c4_full_sum": ("x",)}
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # not Linux
+        return os.cpu_count() or 1
+
+
+def cpu_baseline(name: str, plan: Any, seconds: float, threads: int = 1) -> dict[str, Any]:
+    """The NumPy path of the same configuration on a bounded sample, timed on this host. With
+    ``threads`` > 1 the sample's rows (elements) are cut into that many contiguous chunks, each
+    evaluated by one thread (NumPy releases the GIL in its array loops); the GEMMs use the
+    BLAS's own threads."""
+    from concurrent.futures import ThreadPoolExecutor
+
     from oracle.semantics import FORMULAS
     from ptxgen import problems, shard
 
@@ -367,27 +384,35 @@ def cpu_baseline(name: str, plan: Any, seconds: float) -> dict[str, Any]:
         "c5b_matmul_splitk": lambda f: problems.matmul(128, 1024, 65536, split_k=4,
                                                         raster_group=None),
     }
-    frac = 1 / 64
+    split = _SPLIT.get(name)
+    threads = max(1, threads) if split else 1
+    frac = min(1 / 4, threads / 64)
     spec = samples[name](frac)
     ins = {a["name"]: problems.seeded_input(a) for a in spec.kernel["args"]
            if not a.get("output")}
+    parts = [ins]
+    if threads > 1:
+        cut = {n: np.array_split(ins[n], threads) for n in split}
+        parts = [{**ins, **{n: cut[n][i] for n in split}} for i in range(threads)]
     work = shard.local_problem(name, 1).work
     full = problems.CONFIGS[name]().kernel["args"]
     scale = _elements(spec.kernel["args"]) / _elements(full)
-    t0 = time.perf_counter()
-    reps = 0
-    while True:
-        fn(ins, spec.meta)
-        reps += 1
-        el = time.perf_counter() - t0
-        if el >= seconds or reps >= 1000:
-            break
+    with ThreadPoolExecutor(threads) as pool:
+        t0 = time.perf_counter()
+        reps = 0
+        while True:
+            list(pool.map(lambda part: fn(part, spec.meta), parts))
+            reps += 1
+            el = time.perf_counter() - t0
+            if el >= seconds or reps >= 1000:
+                break
     per_rep = el / reps
     value = work * scale / per_rep
-    threads = os.cpu_count() if name.startswith("c5") else 1
-    return {"value": value, "per_rep_s": per_rep, "reps": reps, "cores": threads,
+    cores = host_threads() if name.startswith("c5") else threads
+    return {"value": value, "per_rep_s": per_rep, "reps": reps, "cores": cores,
             "sample": f"{spec.meta['id']} at {scale:.4f} of the full size "
-                      f"({_elements(spec.kernel['args'])} elements), {reps} repetitions"}
+                      f"({_elements(spec.kernel['args'])} elements), {reps} repetitions"
+                      + (f", split over {threads} threads" if threads > 1 else "")}
 
 
 def _elements(args: list[dict[str, Any]]) -> int:
@@ -474,7 +499,8 @@ def run_ours(args: argparse.Namespace) -> None:
     if rank != 0:
         return
     plan = plan_for(args.workload)
-    cpu = cpu_baseline(args.workload, plan, args.cpu_seconds) if world == 1 else None
+    cpu = (cpu_baseline(args.workload, plan, args.cpu_seconds, host_threads()) if world == 1
+           else None)
     line = {
         "metric": "Kernel time: HBM GB/s (% of ~8 TB/s), GEMM TFLOPS (% peak) at 1/2/4/8 B200",
         "value": head["value"], "unit": head["unit"], "n_gpus": world, "steps": args.steps,
@@ -516,7 +542,7 @@ def run_reference(args: argparse.Namespace) -> None:
     per_step = max(1.0, args.cpu_seconds / max(1, args.steps + args.warmup))
     vals = []
     for i in range(args.warmup + args.steps):
-        r = cpu_baseline(args.workload, plan, per_step)
+        r = cpu_baseline(args.workload, plan, per_step, host_threads())
         if i >= args.warmup:
             vals.append(r["value"])
     value = statistics.fmean(vals) / scale
