@@ -60,6 +60,11 @@ struct Driver {
                                    CUtensorMapSwizzle, CUtensorMapL2promotion,
                                    CUtensorMapFloatOOBfill);
   CUresult (*OccupancyMaxActiveClusters)(int *, CUfunction, const CUlaunchConfig *);
+  CUresult (*EventCreate)(CUevent *, unsigned);
+  CUresult (*EventRecord)(CUevent, CUstream);
+  CUresult (*EventSynchronize)(CUevent);
+  CUresult (*EventElapsedTime)(float *, CUevent, CUevent);
+  CUresult (*EventDestroy)(CUevent);
   CUresult (*GetErrorName)(CUresult, const char **);
   CUresult (*GetErrorString)(CUresult, const char **);
 };
@@ -101,6 +106,11 @@ int load_driver() {
   PG_SYM(CtxSynchronize, "cuCtxSynchronize")
   PG_SYM(TensorMapEncodeTiled, "cuTensorMapEncodeTiled")
   PG_SYM(OccupancyMaxActiveClusters, "cuOccupancyMaxActiveClusters")
+  PG_SYM(EventCreate, "cuEventCreate")
+  PG_SYM(EventRecord, "cuEventRecord")
+  PG_SYM(EventSynchronize, "cuEventSynchronize")
+  PG_SYM(EventElapsedTime, "cuEventElapsedTime")
+  PG_SYM(EventDestroy, "cuEventDestroy_v2")
   PG_SYM(GetErrorName, "cuGetErrorName")
   PG_SYM(GetErrorString, "cuGetErrorString")
 #undef PG_SYM
@@ -269,6 +279,42 @@ int pg_kernel_max_clusters(pg_kernel *kernel, uint32_t block, uint32_t smem_byte
   cfg.numAttrs = 1;
   PG_CU(g_drv.OccupancyMaxActiveClusters(out, kernel->fn, &cfg),
         "cuOccupancyMaxActiveClusters");
+  return PG_OK;
+}
+
+int pg_kernel_time(pg_kernel *kernel, uint32_t grid, uint32_t block, uint32_t smem_bytes,
+                   uint64_t stream, const uint64_t *ptrs, int nptrs, int warmup, int reps,
+                   float *ms_out) {
+  if (!kernel || warmup < 0 || reps < 1 || reps > 100000 || !ms_out)
+    return fail(PG_ERR_ARGUMENT, "pg_kernel_time: bad arguments");
+  int rc;
+  for (int i = 0; i < warmup; ++i)
+    if ((rc = pg_kernel_launch(kernel, grid, block, smem_bytes, stream, ptrs, nptrs))) return rc;
+  std::vector<CUevent> ev(2 * static_cast<size_t>(reps), nullptr);
+  CUstream s = reinterpret_cast<CUstream>(stream);
+  auto destroy = [&ev]() {
+    for (CUevent e : ev)
+      if (e) g_drv.EventDestroy(e);
+  };
+  CUresult r = CUDA_SUCCESS;
+  for (size_t i = 0; i < ev.size() && r == CUDA_SUCCESS; ++i) r = g_drv.EventCreate(&ev[i], 0);
+  if (r != CUDA_SUCCESS) {
+    destroy();
+    return cu_fail(r, "cuEventCreate");
+  }
+  for (int i = 0; i < reps; ++i) {
+    if ((r = g_drv.EventRecord(ev[2 * i], s)) != CUDA_SUCCESS) break;
+    if ((rc = pg_kernel_launch(kernel, grid, block, smem_bytes, stream, ptrs, nptrs))) {
+      destroy();
+      return rc;
+    }
+    if ((r = g_drv.EventRecord(ev[2 * i + 1], s)) != CUDA_SUCCESS) break;
+  }
+  if (r == CUDA_SUCCESS) r = g_drv.EventSynchronize(ev.back());
+  for (int i = 0; i < reps && r == CUDA_SUCCESS; ++i)
+    r = g_drv.EventElapsedTime(&ms_out[i], ev[2 * i], ev[2 * i + 1]);
+  destroy();
+  if (r != CUDA_SUCCESS) return cu_fail(r, "timing events");
   return PG_OK;
 }
 

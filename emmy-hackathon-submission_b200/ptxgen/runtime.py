@@ -63,6 +63,8 @@ def library() -> ctypes.CDLL:
                 "pg_kernel_get": [vp, cp, ctypes.POINTER(vp)],
                 "pg_kernel_launch": [vp, u32, u32, u32, u64, pu64, i32],
                 "pg_kernel_max_clusters": [vp, u32, u32, u32, ctypes.POINTER(i32)],
+                "pg_kernel_time": [vp, u32, u32, u32, u64, pu64, i32, i32, i32,
+                                   ctypes.POINTER(ctypes.c_float)],
                 "pg_tensormap_fill": [vp, cp, i32, i32, u64, pu64, pu64, pu32, i32],
                 "pg_status_take": [vp, pu32],
                 "pg_memset_async": [u64, ctypes.c_size_t, u64],
@@ -200,6 +202,18 @@ class Kernel:
         ptrs = (ctypes.c_uint64 * len(pointers))(*pointers)
         _check(library().pg_kernel_launch(self.handle, grid, block, smem, stream, ptrs,
                                           len(pointers)), f"pg_kernel_launch({self.entry})")
+
+    def time(self, grid: int, block: int, smem: int, pointers: list[int], warmup: int = 3,
+             reps: int = 20, stream: int = 0) -> list[float]:
+        """Device milliseconds of each of ``reps`` back-to-back launches after ``warmup``
+        untimed ones (``pg_kernel_time``: CUDA events around every launch)."""
+        out = (ctypes.c_float * reps)()
+        ptrs = (ctypes.c_uint64 * len(pointers))(*pointers)
+        _check(library().pg_kernel_time(self.handle, grid, block,
+                                        max(smem, self.module.dynamic_smem), stream, ptrs,
+                                        len(pointers), warmup, reps, out),
+               f"pg_kernel_time({self.entry})")
+        return list(out)
 
     def max_clusters(self, block: int, smem: int) -> int:
         """Clusters of this kernel that fit on the device at once."""
@@ -347,6 +361,21 @@ class Problem:
             status = self.module.status()
             if status:
                 raise KernelStatusError(f"{launch['entry']}: status word 0x{status:08x}")
+
+    def time(self, tensors: dict[str, Any], warmup: int = 3, reps: int = 20,
+             stream: int | None = None) -> list[float]:
+        """Device milliseconds of ``reps`` back-to-back launches (after ``warmup``) on the
+        buffers in ``tensors``; zero_outputs are cleared once, before the warm-up."""
+        import torch
+
+        if stream is None:
+            stream = torch.cuda.current_stream(self._dev()).cuda_stream
+        self.launch(tensors, stream)  # tensor maps filled, zero_outputs cleared
+        launch = self.launch_entry
+        ptrs = {name: t.data_ptr() for name, t in tensors.items()}
+        return self.load().time(self.grid(), launch["block"][0],
+                                int(launch.get("smem_bytes", 0)),
+                                [ptrs[n] for n in launch["arg_order"]], warmup, reps, stream)
 
 
 # --- problems of several kernels -----------------------------------------------------------------

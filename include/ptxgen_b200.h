@@ -18,6 +18,9 @@
  *   pg_run_host        <- the whole evaluator step on host buffers: copy in, zero, launch,
  *                         copy out, check the kernel's status word
  *
+ * pg_kernel_time is the timing the evaluator did around its launches (warm-up launches, then
+ * one CUDA event pair per timed launch), for callers that have no other timer.
+ *
  * Three entry points have no counterpart in the reference, because its kernels never needed
  * them: pg_tensormap_fill writes a TMA tensor map into a module's .global symbol (the tcgen05
  * templates read their operands through TMA, and a kernel's parameters must stay the plain
@@ -80,6 +83,13 @@ int pg_kernel_get(pg_module *module, const char *entry, pg_kernel **out);
  * is opted into automatically. Asynchronous on `stream` (0 = the legacy default stream). */
 int pg_kernel_launch(pg_kernel *kernel, uint32_t grid, uint32_t block, uint32_t smem_bytes,
                      uint64_t stream, const uint64_t *ptrs, int nptrs);
+
+/* Launch like pg_kernel_launch `warmup` times untimed, then `reps` times, each bracketed by
+ * CUDA events on `stream`; waits for the last and writes launch i's device time in
+ * milliseconds to ms_out[i]. Launches run back to back (no cache flush between them). */
+int pg_kernel_time(pg_kernel *kernel, uint32_t grid, uint32_t block, uint32_t smem_bytes,
+                   uint64_t stream, const uint64_t *ptrs, int nptrs, int warmup, int reps,
+                   float *ms_out);
 
 /* How many clusters of `cluster` CTAs of `block` threads and `smem_bytes` of dynamic shared
  * memory can be resident on the device at once (cuOccupancyMaxActiveClusters); a persistent

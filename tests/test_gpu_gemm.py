@@ -47,6 +47,11 @@ CASES = {
     "raster_ragged": lambda: problems.matmul(1280, 512, 256, raster_group=4),
     "splitk4": lambda: problems.matmul(256, 256, 1024, split_k=4, raster_group=None),
     "splitk_odd": lambda: problems.matmul(384, 512, 768, split_k=3, raster_group=None),
+    # the mbarrier ring at its edges: one K block, and one more K block than stages (6 on a
+    # pair, 4 on one SM) so the ring wraps once
+    "k64_one_block": lambda: problems.matmul(256, 256, 64),
+    "k448_ring_wraps_pair": lambda: problems.matmul(256, 512, 448),
+    "k320_ring_wraps_1sm": lambda: problems.matmul(128, 256, 320),
     # 8 tiles x 256 K blocks: the template's own 18 uneven splits (14 or 15 K blocks), 144 CTAs
     "splitk_uneven": lambda: problems.matmul(512, 512, 16384, split_k=8, raster_group=None),
 }
@@ -102,3 +107,28 @@ def test_bounded_wait_gives_up(cuda) -> None:
     dummy += 1  # the context still runs work
     torch.cuda.synchronize()
     assert dummy.item() == 1.0
+
+
+def test_launcher_times_launches(cuda) -> None:
+    """``pg_kernel_time`` (CUDA events around each launch) agrees with PyTorch's events on the
+    same back-to-back launches of the config-5 template, within a factor of 1.5."""
+    import torch
+
+    from ptxgen.runtime import Problem
+
+    spec = problems.matmul(1024, 1024, 1024)
+    prob = Problem(spec.graph, spec.meta)
+    tensors = prob.allocate()
+    for t in tensors.values():
+        t.zero_()
+    ms = prob.time(tensors, warmup=3, reps=10)
+    assert len(ms) == 10 and all(0 < t < 100 for t in ms), ms
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(10):
+        prob.launch(tensors)
+    stop.record()
+    torch.cuda.synchronize()
+    theirs = start.elapsed_time(stop) / 10
+    ours = sorted(ms)[5]
+    assert theirs / 1.5 < ours < theirs * 1.5, (ours, theirs)
