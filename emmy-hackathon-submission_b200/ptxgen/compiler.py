@@ -34,10 +34,20 @@ def compile_module(op: KernelOp, buffers: Mapping[str, Buffer], arg_order: Seque
     return k.render()
 
 
-def kernel_for_meta(graph: Graph, meta: dict[str, Any]) -> tuple[KernelOp, dict[str, Any]]:
-    """The KernelOp whose name a meta.json kernel names, and that launch entry."""
+def as_graph(graph: Any) -> Graph:
+    """This loader's Graph from a Graph, a graph JSON dict, or a live Emmy graph."""
+    if isinstance(graph, Graph):
+        return graph
+    if isinstance(graph, dict):
+        return Graph.from_dict(graph)
+    return Graph.from_emmy(graph)
+
+
+def kernel_for_meta(graph: Graph | Any, meta: dict[str, Any]) -> tuple[KernelOp, dict[str, Any]]:
+    """The KernelOp whose name a meta.json kernel names, and that launch entry. ``graph`` may
+    also be a graph JSON dict or a live Emmy graph (the reference's ``to_ptx`` argument)."""
     launches = {k["entry"]: k for k in meta["kernels"]}
-    ops = graph.kernel_ops()
+    ops = as_graph(graph).kernel_ops()
     op = next((o for o in ops if o.name in launches), None)
     if op is None:
         raise ValueError(f"no KernelOp named like a meta.json kernel ({', '.join(launches)})")

@@ -562,6 +562,40 @@ class Graph:
     def load(cls, path: str | Path) -> Graph:
         return cls.from_dict(json.loads(Path(path).read_text()))
 
+    @classmethod
+    def from_emmy(cls, g: Any) -> Graph:
+        """A live Emmy graph -- the object the reference's ``to_ptx`` receives (reference
+        ``compile.py:24-33``: ``graph.nodes`` maps node ids to nodes whose ``op`` is an Emmy op)
+        -- in the JSON form this loader reads. A KernelOp's body becomes the ``repr`` strings of
+        its statements, which is what Emmy's JSON holds; other nodes keep their op's class name.
+        Uses only ``repr``, class names and the ``name``/``body``/``outputs`` attributes, so it
+        needs no Emmy import."""
+        def names(ts: Any) -> list[dict[str, Any]]:
+            out = []
+            for t in ts or ():
+                shape = getattr(t, "shape", None)
+                out.append({"name": getattr(t, "name", str(t)),
+                            "shape": list(shape) if shape is not None else [],
+                            "dtype": str(getattr(getattr(t, "dtype", None), "name",
+                                                 getattr(t, "dtype", "")))})
+            return out
+
+        nodes: dict[str, dict[str, Any]] = {}
+        for nid, n in dict(g.nodes).items():
+            op = getattr(n, "op", n)
+            kind = type(op).__name__
+            fields: dict[str, Any] = {}
+            if kind == "KernelOp":
+                body = op.body
+                stmts = list(body) if isinstance(body, list | tuple) else [body]
+                fields = {"body": [repr(st) for st in stmts],
+                          "name": getattr(op, "name", None) or nid}
+            nodes[str(nid)] = {"op": kind, "op_fields": fields,
+                               "inputs": [str(i) for i in getattr(n, "inputs", None) or ()],
+                               "outputs": names(getattr(n, "outputs", None))}
+        return cls([str(i) for i in getattr(g, "inputs", None) or ()],
+                   [str(o) for o in getattr(g, "outputs", None) or ()], nodes)
+
     def kernel_ops(self) -> list[KernelOp]:
         out = []
         for node_id, n in self.nodes.items():

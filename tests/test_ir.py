@@ -83,3 +83,42 @@ def test_bf16_rounding_golden() -> None:
     x = np.array(data["bf16_inputs_f32_bits"], np.uint32).view(np.float32)
     want = np.array(data["bf16_rounded_f32_bits"], np.uint32) >> 16
     assert np.array_equal(bf16_bits(x).astype(np.uint32), want)
+
+
+def test_to_ptx_takes_a_live_emmy_graph() -> None:
+    """``to_ptx`` accepts the object the reference's ``to_ptx`` receives: an Emmy graph whose
+    ``nodes`` hold Emmy op objects. Emmy is absent here, so the test stands in objects with
+    Emmy's class names whose ``repr`` is Emmy's (the strings its JSON holds)."""
+    import json
+    from types import SimpleNamespace
+
+    from conftest import shipped
+
+    from ptxgen.compiler import to_ptx
+    from ptxgen.ir import Graph
+
+    graph, meta = shipped("a01_attention")
+
+    class Stmt:
+        def __init__(self, text: str):
+            self.text = text
+
+        def __repr__(self) -> str:
+            return self.text
+
+    def op_of(node: dict):
+        cls = type(node["op"], (), {})
+        op = cls()
+        if node["op"] == "KernelOp":
+            body = node["op_fields"]["body"]
+            op.body = [Stmt(t) for t in (json.loads(body) if isinstance(body, str) else body)]
+            op.name = node["op_fields"]["name"]
+        return op
+
+    emmy = SimpleNamespace(
+        inputs=graph["inputs"], outputs=graph["outputs"],
+        nodes={nid: SimpleNamespace(op=op_of(n), inputs=n.get("inputs", []),
+                                    outputs=[SimpleNamespace(name=t["name"])
+                                             for t in n.get("outputs", [])])
+               for nid, n in graph["nodes"].items()})
+    assert to_ptx(emmy, meta) == to_ptx(Graph.from_dict(graph), meta)
