@@ -362,6 +362,13 @@ class Problem:
             if status:
                 raise KernelStatusError(f"{launch['entry']}: status word 0x{status:08x}")
 
+    def capture(self, tensors: dict[str, Any]) -> Any:
+        """A CUDA graph of one launch on ``tensors`` (zero_outputs cleared, kernel launched),
+        for replay with ``.replay()`` when the launch itself is the cost. One eager launch first
+        JIT-loads the module and writes its tensor maps, so nothing synchronises during the
+        capture; the graph keeps the buffers' addresses, so replay it only with these tensors."""
+        return capture_launches([self], tensors)
+
     def time(self, tensors: dict[str, Any], warmup: int = 3, reps: int = 20,
              stream: int | None = None) -> list[float]:
         """Device milliseconds of ``reps`` back-to-back launches (after ``warmup``) on the
@@ -436,3 +443,24 @@ class ProblemSet:
                check_status: bool = False) -> None:
         for p in self.problems:
             p.launch(tensors, stream, check_status=check_status)
+
+    def capture(self, tensors: dict[str, Any]) -> Any:
+        """A CUDA graph of every kernel of the problem in order (see ``Problem.capture``)."""
+        return capture_launches(self.problems, tensors)
+
+
+def capture_launches(problems: list[Problem], tensors: dict[str, Any]) -> Any:
+    """Record ``problems``' launches (each clearing its zero_outputs first) on a capture stream
+    into a ``torch.cuda.CUDAGraph``; one eager pass first loads every module and fills its
+    tensor maps, so the captured calls are only memsets and kernel launches."""
+    import torch
+
+    for p in problems:
+        p.launch(tensors, check_status=True)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    with torch.cuda.graph(graph, stream=side):
+        for p in problems:
+            p.launch(tensors, side.cuda_stream)
+    return graph

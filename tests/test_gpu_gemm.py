@@ -132,3 +132,28 @@ def test_launcher_times_launches(cuda) -> None:
     theirs = start.elapsed_time(stop) / 10
     ours = sorted(ms)[5]
     assert theirs / 1.5 < ours < theirs * 1.5, (ours, theirs)
+
+
+def test_gemm_graph_replay(cuda) -> None:
+    """The tcgen05 template (tensor maps in module globals, a paired persistent grid) captured
+    as a CUDA graph replays to the eager launch's result bit for bit."""
+    import numpy as np
+    import torch
+
+    from ptxgen.runtime import Problem
+
+    spec = problems.matmul(512, 512, 512)
+    ins = reference_inputs(spec.meta)
+    prob = Problem(spec.graph, spec.meta)
+    tensors = prob.allocate()
+    for name, arr in ins.items():
+        tensors[name].copy_(torch.from_numpy(arr.reshape(-1).view(np.int16)).view(torch.bfloat16))
+    prob.launch(tensors, check_status=True)
+    torch.cuda.synchronize()
+    eager = tensors["matmul"].clone()
+    graph = prob.capture(tensors)
+    tensors["matmul"].fill_(float("nan"))
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(tensors["matmul"], eager)
+    assert prob.module.status() == 0
