@@ -57,6 +57,9 @@ def parse_args() -> argparse.Namespace:
                    help="write: flush L2 with a 256 MiB write before each timed step, leaving it "
                         "full of dirty lines the next kernel writes back; clean: follow that write "
                         "with a 256 MiB read, so L2 holds clean unrelated lines")
+    p.add_argument("--ablation", action="store_true",
+                   help="instead of the benchmark: time the reference's shipped example kernels "
+                        "under each compiler flag (its published ablation tables), one JSON line")
     p.add_argument("--cpu-seconds", type=float, default=12.0,
                    help="target seconds of CPU work for the CPU baseline sample")
     return p.parse_args()
@@ -560,8 +563,71 @@ def run_reference(args: argparse.Namespace) -> None:
     print(json.dumps(line))
 
 
+GRAPH_LAUNCHES = 20
+ABLATION_FLAGS = {"default": {}, "no_loop_unroll": {"no_unroll": True},
+                  "no_fusion": {"no_fusion": True}, "no_cse": {"no_cse": True}}
+
+
+def run_ablation(args: argparse.Namespace) -> None:
+    """The reference's published numbers are flag ablations of its shipped example kernels
+    (median kernel time with and without loop unrolling, fusion and CSE). This times the same
+    kernels, compiled here for sm_100a. Two timings per kernel: the median of per-launch
+    CUDA-event times (``pg_kernel_time``, launches enqueued one by one from the host), and the
+    median over replays of a CUDA graph of ``GRAPH_LAUNCHES`` back-to-back launches divided by
+    that count -- for a kernel of a few microseconds the host enqueues slower than the GPU runs,
+    and only the graph keeps the GPU busy from one launch to the next."""
+    import torch
+
+    from ptxgen.build import build_library
+    from ptxgen.problems import seeded_input
+    from ptxgen.runtime import Problem, capture_launches, init
+
+    build_library()
+    init(0)
+    shipped = ROOT / "tests" / "golden" / "shipped"
+    table = []
+    for d in sorted(p for p in shipped.iterdir() if p.is_dir()):
+        graph = json.loads(next(d.glob("*.ir.json")).read_text())
+        meta = json.loads((d / "meta.json").read_text())
+        row: dict[str, Any] = {"problem": d.name}
+        for label, flags in ABLATION_FLAGS.items():
+            prob = Problem(graph, meta, flags=flags)
+            tensors = prob.allocate()
+            for i, a in enumerate(prob.launch_entry["args"]):
+                if a.get("output"):
+                    tensors[a["name"]].zero_()
+                    continue
+                arg = dict(a)
+                if "seed" in arg:
+                    arg["seed"] = meta["graph_inputs"].index(a["name"])
+                tensors[a["name"]].copy_(torch.from_numpy(seeded_input(arg).reshape(-1)))
+            ms = prob.time(tensors, warmup=10, reps=max(20, args.steps))
+            row[f"{label}_us"] = statistics.median(ms) * 1e3
+            replayed = capture_launches([prob] * GRAPH_LAUNCHES, tensors)
+            start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            per = []
+            for _ in range(max(10, args.steps // 2)):
+                start.record()
+                replayed.replay()
+                stop.record()
+                stop.synchronize()
+                per.append(start.elapsed_time(stop) / GRAPH_LAUNCHES)
+            row[f"{label}_graph_us"] = statistics.median(per) * 1e3
+            del replayed
+        table.append(row)
+        log(f"{d.name}: " + ", ".join(f"{k} {v:.2f}" for k, v in row.items() if k != "problem"))
+    print(json.dumps({"ablation": table, "unit": "us (median kernel time)",
+                      "timing": "*_us: pg_kernel_time, one event pair per host-enqueued launch; "
+                                f"*_graph_us: a CUDA graph of {GRAPH_LAUNCHES} back-to-back "
+                                "launches per replay, divided; L2 warm",
+                      "gpu": torch.cuda.get_device_name(0)}))
+
+
 def main() -> None:
     args = parse_args()
+    if args.ablation:
+        run_ablation(args)
+        return
     if args.impl == "reference":
         run_reference(args)
         return
