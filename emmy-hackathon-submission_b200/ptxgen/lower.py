@@ -34,7 +34,7 @@ from .ir import (Accum, Assign, BinaryExpr, CastExpr, Cond, CpAsyncCommit, CpAsy
                  Select, Smem, Stmt, StridedLoop, Sync, TernaryExpr, Tile, TreeHalve, Var,
                  WarpShuffle, Write, walk)
 from .ops import Val
-from .ptx import BUFFER_ALIGN, Kernel, pow2_part
+from .ptx import BUFFER_ALIGN, SM_COUNT, Kernel, pow2_part
 
 UNROLL_BUDGET = 6144  # instructions a loop may fully unroll to
 BODY_BUDGET = 768  # instructions the copies in one trip of a partly unrolled loop may hold
@@ -216,6 +216,11 @@ class Lowering:
         blocks = -(-n // self.block)
         k.ranges[self.ctaid] = (0, blocks - 1)
         k.header_notes.append(f"// @ptxgen launch grid={blocks} block={self.block}")
+        if blocks <= SM_COUNT:
+            # One wave: no SM ever holds a second CTA, so ptxas may spend the whole register file
+            # on one. Left to its occupancy heuristic, a long unrolled block can come out at 32
+            # registers and kilobytes of spills.
+            k.min_ctas = 1
         gid = Aff.of(self.ctaid) * self.block + Aff.of(self.tid)
         past = index.compare(k, ">=", gid, Aff.k(n))
         if past is True:

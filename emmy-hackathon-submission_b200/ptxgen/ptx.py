@@ -34,6 +34,7 @@ _REG = re.compile(r"%(?:rd|fd|[phrf])\d+")
 
 PTX_VERSION = "8.7"
 TARGET = "sm_100a"
+SM_COUNT = 148  # B200: SMs one wave of CTAs spreads over
 BUFFER_ALIGN = 16  # every kernel buffer pointer is at least this aligned (cudaMalloc gives 256)
 
 

@@ -51,13 +51,12 @@ from dataclasses import dataclass
 from ..ir import (Accum, Assign, BinaryExpr, CpAsyncCommit, CpAsyncCopy, Expr, Init, KernelOp,
                   Literal, Load, Loop, Smem, StridedLoop, Tile, Var, Write, walk)
 from ..lower import Buffer
-from ..ptx import PTX_VERSION, TARGET
+from ..ptx import PTX_VERSION, SM_COUNT, TARGET
 
 BM, BK = 128, 64  # tile rows (the MMA's M) and K per stage (64 bf16 = one 128-byte swizzle row)
 UMMA_K = 16
 MAX_STAGES = 6
 WAIT_NS = 2_000_000_000  # a bounded wait gives up after 2 s of %globaltimer
-SM_COUNT = 148  # B200: a split-K GEMM's split count is chosen for this many SMs
 MIN_SEGMENT = 8  # K blocks a split-K segment has at least
 SEGMENT_COST = 2  # a segment's epilogue, in K blocks of MMA time, when choosing the split count
 EPILOGUE_WARPS = (4, 5, 6, 7)
