@@ -470,9 +470,7 @@ class Lowering:
             k.emit(f"cvt.rn.{typ}.f32", (acc,), (ops.apply(k, name, f32, "f32").reg,))
         else:
             m = ops.ACCUM[name][0 if typ in ("f32", "f64", "f16") else 1]
-            if typ == "f16" and name in ("add", "subtract", "multiply"):
-                m = m  # add.rn.f16 and friends
-            k.emit(f"{m}.{typ}", (acc,), (base, value))
+            k.emit(f"{ops.arith(k, m)}.{typ}", (acc,), (base, value))
         k.forget(acc)
 
     # --- reduce -----------------------------------------------------------------------

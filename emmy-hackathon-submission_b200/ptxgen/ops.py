@@ -10,6 +10,12 @@ modifier explicitly, which stops ptxas from contracting a multiply and an add on
 only contraction is the one this backend makes, ``fma_operands``: an f32/f64 add whose operand is
 a still-reusable multiply of the same type becomes one ``fma.rn``. So every rounding in the
 emitted kernel is decided here, and the NumPy oracle can reproduce results bit for bit.
+
+``--no_fusion`` keeps the reference's meaning (``compile.py:8``, ``ptxgen/ops.py:56-71``): this
+backend fuses nothing, and writes ``add``, ``sub`` and ``mul`` without a rounding modifier, so
+ptxas may still contract a multiply and an add by itself. The flag then measures this backend's
+fusion against ptxas's, as the reference's op-fusion tables do, and each product rounds once or
+not at all, as ptxas chooses.
 """
 
 from __future__ import annotations
@@ -55,8 +61,18 @@ def const(k: Kernel, value: float, typ: str) -> str:
     return k.pure(f"mov.{move_type(typ)}", typ, literal(value, typ))
 
 
+# The forms ``--no_fusion`` writes: no rounding modifier, so ptxas may contract them.
+UNFUSED = {"add.rn": "add", "sub.rn": "sub", "mul.rn": "mul"}
+
+
+def arith(k: Kernel, m: str) -> str:
+    """Mnemonic ``m`` as this kernel writes it: ``add.rn``/``sub.rn``/``mul.rn`` lose their
+    rounding modifier with fusion off; everything else is unchanged."""
+    return UNFUSED.get(m, m) if k.no_fusion else m
+
+
 def _bin(m: str, t: str, k: Kernel, a: str, b: str) -> str:
-    return k.pure(f"{m}.{t}", t, a, b)
+    return k.pure(f"{arith(k, m)}.{t}", t, a, b)
 
 
 def _un(m: str, t: str, k: Kernel, x: str) -> str:

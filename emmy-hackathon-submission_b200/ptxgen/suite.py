@@ -312,6 +312,11 @@ POINTWISE: dict[str, Callable[[], SuiteCase]] = {
                                               _x(8192, name="c")], ("out", "f32", (8192,)),
                     [S("v0", "multiply", "a", "b"), S("v1", "add", "v0", "c")], "v1",
                     lambda a, b, c: a * b + c, 1e-6, 1e-6, EXACT),
+    # this backend fuses only an add of a product: a subtract of one stays a mul and a sub
+    "p09_fms": _pw("p09_fms", "a * b - c", [_x(8192, name="a"), _x(8192, name="b"),
+                                            _x(8192, name="c")], ("out", "f32", (8192,)),
+                   [S("v0", "multiply", "a", "b"), S("v1", "subtract", "v0", "c")], "v1",
+                   lambda a, b, c: a * b - c, 1e-6, 1e-6, EXACT),
     "p08_relu_affine_odd": _pw("p08_relu_affine_odd", "torch.relu(x * 0.5 - 0.25)",
                                [_x(3000)], ("out", "f32", (3000,)),
                                [S("v0", "multiply", "x", "mul_c1"),

@@ -47,6 +47,29 @@ def check(kind: str, got: np.ndarray, want: np.ndarray, dtype: str, bound: float
         np.testing.assert_allclose(g, w, rtol=bound, atol=bound * max(1.0, np.abs(w).max()))
 
 
+def check_flags(kind: str, got: np.ndarray, run, dtype: str, bound: float, flags: dict) -> None:
+    """The case's bar, against ``run(no_fusion)``, the oracle. With fusion off the kernel writes
+    a multiply and an add without a rounding modifier, as the reference's ``--no_fusion`` does,
+    and ptxas may contract any such pair: each product rounds once or not at all. The result
+    then meets the case's bar against the oracle with products rounded or with them fused, or,
+    where ptxas contracted only some pairs, lies within rel 1e-5 of the output's scale of the
+    rounded run (two bf16 ulp for bf16 outputs)."""
+    if not flags.get("no_fusion"):
+        check(kind, got, run(False), dtype, bound)
+        return
+    unfused = run(True)
+    for want in (unfused, run(False)):
+        try:
+            check(kind, got, want, dtype, bound)
+            return
+        except AssertionError:
+            pass
+    if dtype == "bf16":
+        check("ulp", got, unfused, dtype, max(bound, 2))
+    else:
+        check("rel", got, unfused, dtype, max(bound if kind == "rel" else 0, 1e-5))
+
+
 # Fast-math kernels: relative to the output's magnitude, since a softmax-weighted average of
 # signed values can sit near zero, where an ulp bound per element would mean nothing.
 SHIPPED_BAR = {"p02_scale_shift": ("exact", 0), "r02_big_sum": ("exact", 0),
@@ -62,10 +85,11 @@ def test_shipped_parity(cuda, name: str, flags: dict) -> None:
     graph, meta = shipped(name)
     ins = reference_inputs(meta)
     got = gpu_run(graph, meta, ins, guard=64, **flags)
-    want = oracle_run(graph, meta, ins, no_fusion=flags.get("no_fusion", False))
     kind, bound = SHIPPED_BAR[name]
     for out in got:
-        check(kind, got[out], want[out], "f32", bound)
+        check_flags(kind, got[out],
+                    lambda nf, out=out: oracle_run(graph, meta, ins, no_fusion=nf)[out],
+                    "f32", bound, flags)
 
 
 CASES = {

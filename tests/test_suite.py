@@ -43,14 +43,31 @@ def test_suite_oracle_meets_reference_formula(name: str) -> None:
     np.testing.assert_allclose(got, want, rtol=case.rtol, atol=case.atol)
 
 
-def test_packed_add_of_a_product_stays_scalar() -> None:
-    """With fusion off, a multiply feeding an add must stay two roundings: the SLP pass keeps
-    such an add scalar (its explicit .rn forbids ptxas to contract), since the packed f32x2
-    forms came out contracted on a B200."""
+def test_packed_sub_of_a_product_stays_scalar() -> None:
+    """A multiply this backend does not fuse must stay two roundings: the SLP pass keeps an
+    add or sub that reads a product scalar (its explicit .rn forbids ptxas to contract), since
+    the packed f32x2 forms came out contracted on a B200. ``a * b - c`` is such a case: only an
+    add of a product fuses."""
+    spec = SUITE["p09_fms"]().spec
+    ptx = to_ptx(Graph.from_dict(spec.graph), spec.meta)
+    assert ".f32x2" not in ptx and "fma.rn" not in ptx
+    assert ptx.count("mul.rn.f32 ") == ptx.count("sub.rn.f32 ") == 4
+
+
+def test_no_fusion_writes_the_reference_forms() -> None:
+    """``--no_fusion`` writes a multiply and an add without a rounding modifier, as the
+    reference does, so ptxas may contract them; with fusion on they are one ``fma.rn``."""
     spec = SUITE["p07_fma3"]().spec
-    ptx = to_ptx(Graph.from_dict(spec.graph), spec.meta, no_fusion=True)
-    assert "add.rn.f32x2" not in ptx and "fma.rn" not in ptx
-    assert ptx.count("add.rn.f32 ") == 4
+    plain = to_ptx(Graph.from_dict(spec.graph), spec.meta, no_fusion=True)
+    fused = to_ptx(Graph.from_dict(spec.graph), spec.meta)
+    def ops(ptx: str) -> list[str]:
+        return [ln.split()[0] for ln in ptx.splitlines() if ln.startswith("\t") and
+                not ln.startswith("\t.")]
+
+    assert ops(plain).count("mul.f32") == ops(plain).count("add.f32") == 4
+    assert not any(".rn" in o or o.startswith("fma") for o in ops(plain))
+    lanes = ops(fused).count("fma.rn.f32") + 2 * ops(fused).count("fma.rn.f32x2")
+    assert "mul.rn.f32" not in ops(fused) and lanes == 4
 
 
 # --- problems of several kernels ---------------------------------------------------------------
