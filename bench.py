@@ -53,13 +53,17 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--share", type=int, default=1,
                    help="on one GPU, run one share of a K-way strong split of the workload (a "
                         "smaller case of the same kernel, e.g. for a profiler capture)")
-    p.add_argument("--l2", choices=("write", "clean"), default="write",
+    p.add_argument("--l2", choices=("write", "clean", "none"), default="write",
                    help="write: flush L2 with a 256 MiB write before each timed step, leaving it "
                         "full of dirty lines the next kernel writes back; clean: follow that write "
-                        "with a 256 MiB read, so L2 holds clean unrelated lines")
+                        "with a 256 MiB read, so L2 holds clean unrelated lines; none: no flush, "
+                        "steps back to back over inputs larger than L2 (each step writes back "
+                        "the previous step's dirty lines, the steady state)")
     p.add_argument("--ablation", action="store_true",
                    help="instead of the benchmark: time the reference's shipped example kernels "
                         "under each compiler flag (its published ablation tables), one JSON line")
+    p.add_argument("--only", default=None,
+                   help="with --ablation: time only this shipped example (e.g. m01_matmul_512)")
     p.add_argument("--cpu-seconds", type=float, default=12.0,
                    help="target seconds of CPU work for the CPU baseline sample")
     return p.parse_args()
@@ -207,6 +211,13 @@ def device_tensors(prob: Any, seed: int) -> dict[str, Any]:
 # --- measurement ---------------------------------------------------------------------------------
 
 
+L2_MODES = {
+    "write": "flushed (256 MiB write) before every timed step",
+    "clean": "flushed (256 MiB write, then a 256 MiB read: clean) before every timed step",
+    "none": "not flushed: inputs larger than L2 (126 MB), steps back to back in steady state",
+}
+
+
 def measure_kernel(plan: Any, steps: int, warmup: int, world: int, l2: str = "write"
                    ) -> dict[str, Any]:
     """Mean kernel time over ``steps`` timed launches (each after an L2 flush), the slowest
@@ -225,6 +236,8 @@ def measure_kernel(plan: Any, steps: int, warmup: int, world: int, l2: str = "wr
     stream = torch.cuda.current_stream()
 
     def flush_l2() -> None:
+        if l2 == "none":
+            return
         flush.zero_()
         if l2 == "clean":
             torch.sum(reread.view(torch.int64), dim=(0,), out=sink)
@@ -513,9 +526,7 @@ def run_ours(args: argparse.Namespace) -> None:
         "config": {"workload": args.workload, "per_rank": plan.spec.meta["id"],
                    "parallelism": f"tile-axis x{world}" if world > 1 else "single GPU",
                    "share": f"1/{args.share} of the workload" if args.share > 1 else "whole",
-                   "l2": ("flushed (256 MiB write) before every timed step" if args.l2 == "write"
-                          else "flushed (256 MiB write, then a 256 MiB read: clean) before "
-                               "every timed step"),
+                   "l2": L2_MODES[args.l2],
                    "allreduce": list(plan.allreduce)},
         "roofline": head["roofline"], "e2e": head["e2e"], "clocks": head["clocks"],
         "gpu_launches": head["launches"],
@@ -587,6 +598,8 @@ def run_ablation(args: argparse.Namespace) -> None:
     shipped = ROOT / "tests" / "golden" / "shipped"
     table = []
     for d in sorted(p for p in shipped.iterdir() if p.is_dir()):
+        if args.only and d.name != args.only:
+            continue
         graph = json.loads(next(d.glob("*.ir.json")).read_text())
         meta = json.loads((d / "meta.json").read_text())
         row: dict[str, Any] = {"problem": d.name}
