@@ -242,16 +242,33 @@ def measure_kernel(plan: Any, steps: int, warmup: int, world: int, l2: str = "wr
         if l2 == "clean":
             torch.sum(reread.view(torch.int64), dim=(0,), out=sink)
 
-    def step() -> None:
+    collective = bool(plan.allreduce) and world > 1
+    mids: list[Any] = []
+
+    def step(mid: Any = None) -> None:
         prob.launch(tensors, stream=stream.cuda_stream)
-        if plan.allreduce and world > 1:
+        if collective:
             import torch.distributed as tdist
 
+            if mid is not None:
+                mid.record(stream)
             for name in plan.allreduce:
                 tdist.all_reduce(tensors[name])
 
+    align = torch.zeros(1, dtype=torch.float32, device="cuda")
+
+    def realign() -> None:
+        """Ranks leave one step's collective together; the L2 flush before the next (not part
+        of the workload) takes each rank a different time, so a one-element all-reduce after it,
+        outside the step's events, lines them up again as the previous collective would."""
+        if collective:
+            import torch.distributed as tdist
+
+            tdist.all_reduce(align)
+
     for _ in range(warmup):
         flush_l2()
+        realign()
         step()
     torch.cuda.synchronize()
     if world > 1:
@@ -262,11 +279,14 @@ def measure_kernel(plan: Any, steps: int, warmup: int, world: int, l2: str = "wr
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     stops = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     sampler = ClockSampler(torch.cuda.current_device())
+    if collective:
+        mids = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     with sampler:
         for i in range(steps):
             flush_l2()
+            realign()
             starts[i].record(stream)
-            step()
+            step(mids[i] if mids else None)
             stops[i].record(stream)
         torch.cuda.synchronize()
     if world > 1:
@@ -276,6 +296,10 @@ def measure_kernel(plan: Any, steps: int, warmup: int, world: int, l2: str = "wr
     torch.cuda.synchronize()
     times = [s.elapsed_time(e) for s, e in zip(starts, stops, strict=True)]
     mean_ms = statistics.fmean(times)
+    if mids:  # this rank's split of its step: its own kernel, then the collective's wait
+        kern = statistics.fmean(s.elapsed_time(m) for s, m in zip(starts, mids, strict=True))
+        log(f"{plan.name}: kernel {kern * 1e3:.1f} us, collective {(mean_ms - kern) * 1e3:.1f} us "
+            "(this rank)")
     status = prob.module.status()
     if status:
         raise RuntimeError(f"kernel status word 0x{status:08x}")
