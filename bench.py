@@ -62,6 +62,8 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--ablation", action="store_true",
                    help="instead of the benchmark: time the reference's shipped example kernels "
                         "under each compiler flag (its published ablation tables), one JSON line")
+    p.add_argument("--e2e-lanes", type=int, default=2,
+                   help="steps of the host-buffer (e2e) path in flight at once, one stream each")
     p.add_argument("--only", default=None,
                    help="with --ablation: time only this shipped example (e.g. m01_matmul_512)")
     p.add_argument("--cpu-seconds", type=float, default=12.0,
@@ -152,6 +154,19 @@ class ClockSampler:
         except Exception:  # noqa: BLE001 - no NVML: report no clocks
             self.nvml = None
 
+    # NVML's cumulative violation counters: time spent held below the requested clocks, by cause
+    POLICIES = {"power": 0, "thermal": 1, "sync_boost": 2, "board_limit": 3, "reliability": 5}
+
+    def _violations(self) -> dict[str, int]:
+        out = {}
+        for name, policy in self.POLICIES.items():
+            try:
+                out[name] = int(self.nvml.nvmlDeviceGetViolationStatus(self.h, policy)
+                                .violationTime)
+            except Exception:  # noqa: BLE001 - a policy this device does not report
+                pass
+        return out
+
     def _run(self) -> None:
         while not self._stop.is_set():
             try:
@@ -161,10 +176,12 @@ class ClockSampler:
                 self.reasons |= {n for b, n in self.REASONS.items() if bits & b}
             except Exception:  # noqa: BLE001
                 pass
-            self._stop.wait(0.001)
+            self._stop.wait(0.0002)
 
     def __enter__(self) -> ClockSampler:
+        self.violation_ns: dict[str, int] = {}
         if self.nvml is not None:
+            self._v0 = self._violations()
             self._thread = threading.Thread(target=self._run, daemon=True)
             self._thread.start()
         return self
@@ -173,11 +190,14 @@ class ClockSampler:
         self._stop.set()
         if self._thread is not None:
             self._thread.join()
+            v1 = self._violations()
+            self.violation_ns = {n: v1[n] - self._v0[n] for n in v1 if n in self._v0}
 
     def summary(self) -> dict[str, Any]:
         med = statistics.median(self.samples) if self.samples else None
         return {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
-                "samples": len(self.samples)}
+                "samples": len(self.samples),
+                "violation_us": {n: round(v / 1e3, 1) for n, v in self.violation_ns.items()}}
 
 
 # --- inputs ------------------------------------------------------------------------------------
@@ -346,12 +366,12 @@ def _host_lane(prob: Any, tensors: dict[str, Any], stream: int) -> dict[str, Any
             "h2d": h2d, "d2h": d2h}
 
 
-def measure_e2e(plan: Any, prob: Any, tensors: dict[str, Any], steps: int, world: int
-                ) -> dict[str, Any]:
+def measure_e2e(plan: Any, prob: Any, tensors: dict[str, Any], steps: int, world: int,
+                in_flight: int = 2) -> dict[str, Any]:
     """The same metric through ``pg_run_host``, the one-call host-buffer API: every step copies
     its page-locked inputs in, zeroes its zero_outputs, launches, copies its outputs back and
-    waits. Two steps are in flight at a time, each lane with its own module, buffers and
-    stream, so one step's upload overlaps the other's download on the full-duplex link (a
+    waits. ``in_flight`` steps run at a time, each lane with its own module, buffers and
+    stream, so one step's upload overlaps another's download on the full-duplex link (a
     workload with a collective keeps one lane). The value is all steps' work over the wall time
     from the first call to the last return."""
     import torch
@@ -359,10 +379,10 @@ def measure_e2e(plan: Any, prob: Any, tensors: dict[str, Any], steps: int, world
     from ptxgen.runtime import Problem
 
     lanes = [_host_lane(prob, tensors, torch.cuda.Stream().cuda_stream)]
-    if not (plan.allreduce and world > 1):
-        prob2 = Problem(plan.spec.graph, plan.spec.meta)
-        prob2.load()
-        lanes.append(_host_lane(prob2, {n: t.clone() for n, t in tensors.items()},
+    while len(lanes) < in_flight and not (plan.allreduce and world > 1):
+        other = Problem(plan.spec.graph, plan.spec.meta)
+        other.load()
+        lanes.append(_host_lane(other, {n: t.clone() for n, t in tensors.items()},
                                 torch.cuda.Stream().cuda_stream))
     for lane in lanes:  # warm each path once
         lane["kernel"].run_host(*lane["args"])
@@ -515,7 +535,8 @@ def run_ours(args: argparse.Namespace) -> None:
                            "algorithmic_per_launch": plan.work}
         log(f"{name}: {res['ms_per_step']:.4f} ms per step, {res['value']:.1f} {unit}")
         if with_e2e:
-            e = measure_e2e(plan, m["prob"], m["tensors"], max(3, min(steps, 20)), world)
+            e = measure_e2e(plan, m["prob"], m["tensors"], max(3, min(steps, 20)), world,
+                            args.e2e_lanes)
             res["e2e"] = {"value": plan.work * world / e["mean_s"] / scale, "unit": unit,
                           "h2d_bytes_per_step": e["h2d"], "d2h_bytes_per_step": e["d2h"],
                           "steps_in_flight": e["in_flight"]}
