@@ -7,7 +7,8 @@ the IR and the ``meta.json`` beside it (the contract for the parameter order, th
 the buffers' shapes, dtypes and outputs) and writes one PTX module to stdout. An IR it cannot
 lower raises (``NotImplementedError``/``ValueError``/``KeyError``) and exits non-zero.
 ``--no_loop_unroll`` turns every loop into a runtime loop with one copy of the body per trip.
-``--no_fusion`` never fuses a float multiply and add into one ``fma``.
+``--no_fusion`` never fuses a float multiply and add into one ``fma`` (ptxas still may: the
+multiply and the add are written without a rounding modifier, as the reference writes them).
 ``--no_cse`` turns off common subexpression elimination.
 Any of the three flags also turns off the hand-written kernel templates, so the generic lowering
 the flag describes is what runs.
