@@ -406,17 +406,26 @@ class _Vectorizer:
         return chunks
 
     def _loads(self, seg: list[Ins]) -> list[Ins]:
-        groups: dict[tuple[str, str, str, str], list[int]] = {}
+        """Read-only global loads merge anywhere in the segment. Shared loads merge within a
+        stretch that no shared store, reduction or opaque line splits (segments already end at
+        every barrier, ``cp.async`` and fence), so a merged load, issued at its first member's
+        place, reads what each member would have read."""
+        groups: dict[tuple[str, str, str, str, int], list[int]] = {}
+        epoch = 0
         for i, ins in enumerate(seg):
             m = ins.mem
+            if (m is not None and m.kind != "ld" and m.space == "shared") or \
+                    (ins.text is not None and not ins.pure):
+                epoch += 1
             if m is None or m.kind != "ld" or len(m.regs) != 1 or ins.pred or m.typ == "u8":
                 continue
-            if m.space != "global.nc":
-                continue  # loads of memory the kernel writes keep their order
-            groups.setdefault((m.space, m.typ, m.addr, m.hint), []).append(i)
+            if m.space not in ("global.nc", "shared"):
+                continue  # loads of global memory the kernel writes keep their order
+            groups.setdefault((m.space, m.typ, m.addr, m.hint,
+                               epoch if m.space == "shared" else 0), []).append(i)
         replace: dict[int, list[Ins]] = {}
         drop: set[int] = set()
-        for (space, typ, addr, hint), idxs in groups.items():
+        for (space, typ, addr, hint, _), idxs in groups.items():
             if len(idxs) < 2:
                 continue
             esize = size(typ)
