@@ -298,3 +298,41 @@ def test_fastmath_matches_reference_sequence(name: str) -> None:
     ours = _normalised([ins.render() for ins in k.body] + [f"result {out}"])
     want = _normalised(golden["body"] + [f"result {golden['out']}"])
     assert ours == want
+
+
+def _shared_loads(between: str | None) -> list[str]:
+    """Vectorize two f32 shared loads at [a+0] and [a+4] (a 16-byte aligned), with ``between``
+    ("st": a shared store, "ld": another shared load, None) placed between them."""
+    from ptxgen.ptx import Kernel
+
+    k = Kernel("t", [], 128)
+    a = k.reg("u32")
+    k.align[a] = 16
+    x, y, z = k.reg("f32"), k.reg("f32"), k.reg("f32")
+    k.mem("ld", "shared", "f32", a, 0, (x,))
+    if between == "st":
+        k.mem("st", "shared", "f32", a, 4, (z,))
+    elif between == "ld":
+        k.mem("ld", "shared", "f32", a, 8, (z,))
+    k.mem("ld", "shared", "f32", a, 4, (y,))
+    k.vectorize()
+    return [ins.render().strip() for ins in k.body]
+
+
+def test_shared_loads_merge_unless_a_shared_store_sits_between() -> None:
+    """Adjacent shared loads become one vector load; a shared store between them keeps them
+    apart, since the second load must read what the store wrote."""
+    assert any(line.startswith("ld.shared.v2.f32") for line in _shared_loads(None))
+    assert any(line.startswith("ld.shared.v2.f32") for line in _shared_loads("ld"))
+    kept = _shared_loads("st")
+    assert sum(line.startswith("ld.shared.f32") for line in kept) == 2
+    assert not any(".v2" in line or ".v4" in line for line in kept)
+
+
+def test_simt_matmul_reads_shared_memory_in_vectors() -> None:
+    """The shipped m01 nest: A's four consecutive k of one row in one v4 load, B's two columns
+    of one thread in one v2 load; no scalar shared loads remain."""
+    graph, meta = shipped("m01_matmul_512")
+    ptx = to_ptx(Graph.from_dict(graph), meta)
+    assert ptx.count("ld.shared.v4.f32") == 64 and ptx.count("ld.shared.v2.f32") == 128
+    assert "ld.shared.f32" not in ptx
