@@ -65,6 +65,10 @@ struct Driver {
   CUresult (*EventSynchronize)(CUevent);
   CUresult (*EventElapsedTime)(float *, CUevent, CUevent);
   CUresult (*EventDestroy)(CUevent);
+  CUresult (*MemGetAddressRange)(CUdeviceptr *, size_t *, CUdeviceptr);
+  CUresult (*IpcGetMemHandle)(CUipcMemHandle *, CUdeviceptr);
+  CUresult (*IpcOpenMemHandle)(CUdeviceptr *, CUipcMemHandle, unsigned);
+  CUresult (*IpcCloseMemHandle)(CUdeviceptr);
   CUresult (*GetErrorName)(CUresult, const char **);
   CUresult (*GetErrorString)(CUresult, const char **);
 };
@@ -111,6 +115,10 @@ int load_driver() {
   PG_SYM(EventSynchronize, "cuEventSynchronize")
   PG_SYM(EventElapsedTime, "cuEventElapsedTime")
   PG_SYM(EventDestroy, "cuEventDestroy_v2")
+  PG_SYM(MemGetAddressRange, "cuMemGetAddressRange_v2")
+  PG_SYM(IpcGetMemHandle, "cuIpcGetMemHandle")
+  PG_SYM(IpcOpenMemHandle, "cuIpcOpenMemHandle_v2")
+  PG_SYM(IpcCloseMemHandle, "cuIpcCloseMemHandle")
   PG_SYM(GetErrorName, "cuGetErrorName")
   PG_SYM(GetErrorString, "cuGetErrorString")
 #undef PG_SYM
@@ -396,6 +404,40 @@ int pg_status_take(pg_module *module, uint32_t *status) {
     uint32_t zero = 0;
     PG_CU(g_drv.MemcpyHtoD(module->status, &zero, sizeof zero), "cuMemcpyHtoD(status)");
   }
+  return PG_OK;
+}
+
+int pg_ipc_handle(uint64_t ptr, void *handle, uint64_t *offset) {
+  if (!ptr || !handle || !offset) return fail(PG_ERR_ARGUMENT, "pg_ipc_handle: null argument");
+  int rc = ensure_current();
+  if (rc) return rc;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  PG_CU(g_drv.MemGetAddressRange(&base, &size, ptr), "cuMemGetAddressRange");
+  CUipcMemHandle h;
+  PG_CU(g_drv.IpcGetMemHandle(&h, base), "cuIpcGetMemHandle");
+  std::memcpy(handle, h.reserved, sizeof h.reserved);
+  *offset = ptr - base;
+  return PG_OK;
+}
+
+int pg_ipc_open(const void *handle, uint64_t *base) {
+  if (!handle || !base) return fail(PG_ERR_ARGUMENT, "pg_ipc_open: null argument");
+  int rc = ensure_current();
+  if (rc) return rc;
+  CUipcMemHandle h;
+  std::memcpy(h.reserved, handle, sizeof h.reserved);
+  CUdeviceptr p = 0;
+  PG_CU(g_drv.IpcOpenMemHandle(&p, h, CU_IPC_MEM_LAZY_ENABLE_PEER_ACCESS), "cuIpcOpenMemHandle");
+  *base = p;
+  return PG_OK;
+}
+
+int pg_ipc_close(uint64_t base) {
+  if (!base) return fail(PG_ERR_ARGUMENT, "pg_ipc_close: null base");
+  int rc = ensure_current();
+  if (rc) return rc;
+  PG_CU(g_drv.IpcCloseMemHandle(base), "cuIpcCloseMemHandle");
   return PG_OK;
 }
 

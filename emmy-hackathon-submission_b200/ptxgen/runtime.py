@@ -73,6 +73,9 @@ def library() -> ctypes.CDLL:
                 "pg_stream_synchronize": [u64],
                 "pg_run_host": [vp, u32, u32, u32, u64, i32, pu64, ctypes.POINTER(vp), psz,
                                 pu32],
+                "pg_ipc_handle": [u64, vp, pu64],
+                "pg_ipc_open": [vp, pu64],
+                "pg_ipc_close": [u64],
             }
             for name, args in sig.items():
                 fn = getattr(lib, name)

@@ -21,12 +21,14 @@
  * pg_kernel_time is the timing the evaluator did around its launches (warm-up launches, then
  * one CUDA event pair per timed launch), for callers that have no other timer.
  *
- * Three entry points have no counterpart in the reference, because its kernels never needed
+ * Some entry points have no counterpart in the reference, because its kernels never needed
  * them: pg_tensormap_fill writes a TMA tensor map into a module's .global symbol (the tcgen05
  * templates read their operands through TMA, and a kernel's parameters must stay the plain
  * device pointers of meta.arg_order), pg_status_take reads the status word that kernels with
- * bounded waits set instead of hanging, and pg_kernel_max_clusters sizes the grid of a
- * persistent kernel whose CTAs run in pairs (the tcgen05 GEMM's 2-SM form).
+ * bounded waits set instead of hanging, pg_kernel_max_clusters sizes the grid of a
+ * persistent kernel whose CTAs run in pairs (the tcgen05 GEMM's 2-SM form), and
+ * pg_ipc_handle/pg_ipc_open/pg_ipc_close map the buffers through which ranks on other GPUs
+ * exchange partial results over NVLink (the reference runs on one GPU).
  *
  * Plain C types only: device pointers and CUDA streams travel as uint64_t. Every function
  * returns 0 on success, a positive CUresult from the driver, or a negative PG_ERR_* code;
@@ -109,6 +111,17 @@ int pg_tensormap_fill(pg_module *module, const char *symbol, int dtype, int rank
 /* Read the module's 32-bit status word (.global ptxgen_status) into *status and clear it;
  * *status is 0 when the module has none. Synchronous. */
 int pg_status_take(pg_module *module, uint32_t *status);
+
+/* CUDA IPC over one device allocation, for buffers that other processes' kernels reach through
+ * NVLink (ptxgen.peer's cross-rank sum). No counterpart in the reference, which runs on one
+ * GPU. pg_ipc_handle writes the PG_IPC_HANDLE_BYTES-byte handle of the allocation holding `ptr`
+ * and ptr's byte offset inside it; pg_ipc_open maps another process's allocation by its
+ * handle, *base being its first byte here (peer access enabled as needed); pg_ipc_close
+ * unmaps it. An allocation of this process cannot be opened here. */
+#define PG_IPC_HANDLE_BYTES 64
+int pg_ipc_handle(uint64_t ptr, void *handle, uint64_t *offset);
+int pg_ipc_open(const void *handle, uint64_t *base);
+int pg_ipc_close(uint64_t base);
 
 /* Stream-ordered helpers on device memory. */
 int pg_memset_async(uint64_t dptr, size_t bytes, uint64_t stream);
