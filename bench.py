@@ -62,6 +62,9 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--ablation", action="store_true",
                    help="instead of the benchmark: time the reference's shipped example kernels "
                         "under each compiler flag (its published ablation tables), one JSON line")
+    p.add_argument("--collective", choices=("peer", "nccl"), default="peer",
+                   help="how the sharded sum's partials are summed across ranks: this "
+                        "repository's one-warp kernel over NVLink peer memory, or NCCL")
     p.add_argument("--e2e-lanes", type=int, default=2,
                    help="steps of the host-buffer (e2e) path in flight at once, one stream each")
     p.add_argument("--only", default=None,
@@ -238,8 +241,8 @@ L2_MODES = {
 }
 
 
-def measure_kernel(plan: Any, steps: int, warmup: int, world: int, l2: str = "write"
-                   ) -> dict[str, Any]:
+def measure_kernel(plan: Any, steps: int, warmup: int, world: int, l2: str = "write",
+                   via: str = "peer") -> dict[str, Any]:
     """Mean kernel time over ``steps`` timed launches (each after an L2 flush), the slowest
     rank's, with the launch count and NVML clocks of the timed region."""
     import torch
@@ -264,16 +267,29 @@ def measure_kernel(plan: Any, steps: int, warmup: int, world: int, l2: str = "wr
 
     collective = bool(plan.allreduce) and world > 1
     mids: list[Any] = []
+    peer = None
+    if collective and via == "peer":
+        from ptxgen.peer import PeerSum
+
+        peer = PeerSum()
+
+    def combine(t: Any, s: Any) -> None:
+        """The path's collective: this rank's partial summed over the ranks, in place."""
+        if peer is not None:
+            peer(t.data_ptr(), stream=s.cuda_stream)
+        else:
+            import torch.distributed as tdist
+
+            with torch.cuda.stream(s):
+                tdist.all_reduce(t)
 
     def step(mid: Any = None) -> None:
         prob.launch(tensors, stream=stream.cuda_stream)
         if collective:
-            import torch.distributed as tdist
-
             if mid is not None:
                 mid.record(stream)
             for name in plan.allreduce:
-                tdist.all_reduce(tensors[name])
+                combine(tensors[name], stream)
 
     align = torch.zeros(1, dtype=torch.float32, device="cuda")
 
@@ -323,10 +339,12 @@ def measure_kernel(plan: Any, steps: int, warmup: int, world: int, l2: str = "wr
     status = prob.module.status()
     if status:
         raise RuntimeError(f"kernel status word 0x{status:08x}")
+    if peer is not None:
+        peer.check()
     out = {"mean_ms": max_over_ranks(mean_ms, world),
            "median_ms": max_over_ranks(statistics.median(times), world),
            "min_ms": max_over_ranks(min(times), world), "launches": steps,
-           "clocks": sampler.summary(), "tensors": tensors, "prob": prob}
+           "clocks": sampler.summary(), "tensors": tensors, "prob": prob, "peer": peer}
     return out
 
 
@@ -367,12 +385,13 @@ def _host_lane(prob: Any, tensors: dict[str, Any], stream: int) -> dict[str, Any
 
 
 def measure_e2e(plan: Any, prob: Any, tensors: dict[str, Any], steps: int, world: int,
-                in_flight: int = 2) -> dict[str, Any]:
+                in_flight: int = 2, peer: Any = None) -> dict[str, Any]:
     """The same metric through ``pg_run_host``, the one-call host-buffer API: every step copies
     its page-locked inputs in, zeroes its zero_outputs, launches, copies its outputs back and
     waits. ``in_flight`` steps run at a time, each lane with its own module, buffers and
     stream, so one step's upload overlaps another's download on the full-duplex link (a
-    workload with a collective keeps one lane). The value is all steps' work over the wall time
+    workload with a collective keeps one lane, its partial summed over the ranks after each
+    step by ``peer`` when given, else by NCCL). The value is all steps' work over the wall time
     from the first call to the last return."""
     import torch
 
@@ -395,7 +414,10 @@ def measure_e2e(plan: Any, prob: Any, tensors: dict[str, Any], steps: int, world
                 import torch.distributed as tdist
 
                 for name in plan.allreduce:
-                    tdist.all_reduce(lane["tensors"][name])
+                    if peer is not None:
+                        peer(lane["tensors"][name].data_ptr(), stream=lane["args"][3])
+                    else:
+                        tdist.all_reduce(lane["tensors"][name])
                 torch.cuda.synchronize()
 
     shares = [steps // len(lanes) + (i < steps % len(lanes)) for i in range(len(lanes))]
@@ -521,7 +543,7 @@ def run_ours(args: argparse.Namespace) -> None:
         log(f"{name}: compile and inputs")
         plan = plan_for(name)
         unit, bound, scale = unit_of(plan)
-        m = measure_kernel(plan, steps, warmup, world, args.l2)
+        m = measure_kernel(plan, steps, warmup, world, args.l2, args.collective)
         per_rank = plan.work / (m["mean_ms"] / 1e3) / scale
         res: dict[str, Any] = {"workload": name, "value": per_rank * world, "unit": unit,
                                "ms_per_step": m["mean_ms"], "median_ms": m["median_ms"],
@@ -536,10 +558,16 @@ def run_ours(args: argparse.Namespace) -> None:
         log(f"{name}: {res['ms_per_step']:.4f} ms per step, {res['value']:.1f} {unit}")
         if with_e2e:
             e = measure_e2e(plan, m["prob"], m["tensors"], max(3, min(steps, 20)), world,
-                            args.e2e_lanes)
+                            args.e2e_lanes, m["peer"])
             res["e2e"] = {"value": plan.work * world / e["mean_s"] / scale, "unit": unit,
                           "h2d_bytes_per_step": e["h2d"], "d2h_bytes_per_step": e["d2h"],
                           "steps_in_flight": e["in_flight"]}
+        if m["peer"] is not None:  # every rank is past its last call before any unmaps
+            import torch.distributed as tdist
+
+            m["peer"].check()
+            tdist.barrier()
+            m["peer"].close()
         del m
         torch.cuda.empty_cache()
         return res
@@ -572,7 +600,10 @@ def run_ours(args: argparse.Namespace) -> None:
                    "parallelism": f"tile-axis x{world}" if world > 1 else "single GPU",
                    "share": f"1/{args.share} of the workload" if args.share > 1 else "whole",
                    "l2": L2_MODES[args.l2],
-                   "allreduce": list(plan.allreduce)},
+                   "allreduce": list(plan.allreduce),
+                   "collective": (("peer memory: ptxgen.peer's one-warp kernel over NVLink"
+                                   if args.collective == "peer" else "NCCL all-reduce")
+                                  if plan.allreduce and world > 1 else None)},
         "roofline": head["roofline"], "e2e": head["e2e"], "clocks": head["clocks"],
         "gpu_launches": head["launches"],
         "cpu_baseline": cpu and {"value": cpu["value"] / unit_of(plan)[2], "unit": head["unit"],

@@ -1,7 +1,8 @@
 """The cross-rank sum over peer memory (``ptxgen.peer``, ``templates/exchange.py``).
 
-On the CPU: the kernel assembles for sm_100a, publishes and collects with release/acquire at
-system scope, bounds its wait by %globaltimer, and loads nothing with cluster multicast.
+On the CPU: the kernel assembles for sm_100a, publishes and collects with 64-bit stores and
+loads at system scope, bounds its wait by %globaltimer, and loads nothing with cluster
+multicast.
 
 On one GPU, three single-kernel cases, none of which waits on another kernel:
 1. one rank sums its own partial;
@@ -32,7 +33,7 @@ ROOT = Path(__file__).resolve().parents[1]
 
 def test_peer_sum_ptx_assembles(tmp_path) -> None:
     ptx = peer_sum_ptx()
-    assert "st.release.sys.global.u64" in ptx and "ld.acquire.sys.global.u64" in ptx
+    assert "st.relaxed.sys.global.u64" in ptx and "ld.relaxed.sys.global.u64" in ptx
     assert "%globaltimer" in ptx and "red.global.or.b32 [ptxgen_status]" in ptx
     assert "multicast" not in ptx and "multimem" not in ptx
     if shutil.which("ptxas") is None:
