@@ -40,3 +40,15 @@ def test_calls_before_init_fail_cleanly() -> None:
     assert isinstance(lib.pg_last_error(), bytes)
     lib.pg_module_load.argtypes = [ctypes.c_char_p, ctypes.c_void_p]
     assert lib.pg_module_load(None, None) == -2
+
+
+def test_python_binding_types_every_declared_symbol() -> None:
+    """``ptxgen.runtime.library()`` gives every header function its argument types, so no
+    call goes through ctypes' default int conversion of 64-bit pointers."""
+    from ptxgen.runtime import library
+
+    lib = library()
+    for name in declared():
+        if name == "pg_last_error":
+            continue
+        assert getattr(lib, name).argtypes is not None, name
