@@ -49,7 +49,7 @@ from collections.abc import Mapping, Sequence
 from dataclasses import dataclass
 
 from ..ir import (Accum, Assign, BinaryExpr, CpAsyncCommit, CpAsyncCopy, Expr, Init, KernelOp,
-                  Literal, Load, Loop, Smem, StridedLoop, Tile, Var, Write, walk)
+                  Load, Loop, Smem, StridedLoop, Tile, Var, Write, walk)
 from ..lower import Buffer
 from ..ptx import PTX_VERSION, SM_COUNT, TARGET
 

@@ -14,7 +14,6 @@ from datetime import timedelta
 from pathlib import Path
 
 import numpy as np
-import pytest
 
 ROOT = Path(__file__).resolve().parents[1]
 
