@@ -387,6 +387,21 @@ int pg_tensormap_fill(pg_module *module, const char *symbol, int dtype, int rank
   return PG_OK;
 }
 
+int pg_global_write(pg_module *module, const char *symbol, const void *data, size_t bytes) {
+  if (!module || !symbol || (bytes && !data))
+    return fail(PG_ERR_ARGUMENT, "pg_global_write: null argument");
+  int rc = ensure_current();
+  if (rc) return rc;
+  CUdeviceptr dst = 0;
+  size_t size = 0;
+  CUresult r = g_drv.ModuleGetGlobal(&dst, &size, module->mod, symbol);
+  if (r != CUDA_SUCCESS) return fail(PG_ERR_NOT_FOUND, "pg_global_write: no .global %s", symbol);
+  if (bytes > size)
+    return fail(PG_ERR_ARGUMENT, "pg_global_write: %zu bytes into %s of %zu", bytes, symbol, size);
+  if (bytes) PG_CU(g_drv.MemcpyHtoD(dst, data, bytes), "cuMemcpyHtoD(global)");
+  return PG_OK;
+}
+
 int pg_status_take(pg_module *module, uint32_t *status) {
   if (!module || !status) return fail(PG_ERR_ARGUMENT, "pg_status_take: null argument");
   int rc = ensure_current();

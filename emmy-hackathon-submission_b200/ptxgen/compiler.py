@@ -19,18 +19,20 @@ __all__ = ["Buffer", "compile_module", "to_ptx", "kernel_for_meta"]
 
 def compile_module(op: KernelOp, buffers: Mapping[str, Buffer], arg_order: Sequence[str],
                    block_threads: int, *, no_unroll: bool = False, no_fusion: bool = False,
-                   no_cse: bool = False, smem_bytes: int = 0, templates: bool = True) -> str:
+                   no_cse: bool = False, smem_bytes: int = 0, templates: bool = True,
+                   exchange: str | None = None) -> str:
     """The sm_100a PTX module for ``op``, launched with ``block_threads`` threads per block and
     ``smem_bytes`` of dynamic shared memory (meta.json's figure; templates size their pipelines
-    to it)."""
-    if templates:
+    to it). ``exchange`` names a one-element f32 output that the kernel, once every block has
+    added into it, sums across ranks over peer memory (``templates.exchange``)."""
+    if templates and exchange is None:
         from . import templates as tpl
 
         ptx = tpl.try_templates(op, buffers, arg_order, block_threads, smem_bytes)
         if ptx is not None:
             return ptx
     k = Lowering(op, buffers, arg_order, block_threads, no_unroll=no_unroll,
-                 no_fusion=no_fusion, no_cse=no_cse).run()
+                 no_fusion=no_fusion, no_cse=no_cse, exchange=exchange).run()
     return k.render()
 
 
@@ -68,7 +70,9 @@ def to_ptx(graph: Graph, meta: dict[str, Any], no_unroll: bool = False, no_fusio
                           bool(a.get("output")) or a["name"] in op.outputs)
         for a in launch["args"]
     }
+    exchange = launch.get("exchange", {}).get("output")  # a sharded plan's own meta only
     return compile_module(op, buffers, launch["arg_order"], launch["block"][0],
                           no_unroll=no_unroll, no_fusion=no_fusion, no_cse=no_cse,
                           smem_bytes=int(launch.get("smem_bytes", 0)),
-                          templates=templates and not (no_unroll or no_fusion or no_cse))
+                          templates=templates and not (no_unroll or no_fusion or no_cse),
+                          exchange=exchange)

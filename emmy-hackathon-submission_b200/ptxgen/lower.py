@@ -93,10 +93,16 @@ def pack_shared(decls: Sequence[Smem]) -> tuple[dict[str, int], int]:
 class Lowering:
     def __init__(self, op: KernelOp, buffers: Mapping[str, Buffer], arg_order: Sequence[str],
                  block: int, *, no_unroll: bool = False, no_fusion: bool = False,
-                 no_cse: bool = False):
+                 no_cse: bool = False, exchange: str | None = None):
         if not 1 <= block <= 1024:
             raise ValueError(f"block of {block} threads")
         self.op, self.block, self.buffers = op, block, dict(buffers)
+        # an f32 output whose blocks' atomic adds this kernel then sums across ranks itself
+        self.exchange = exchange
+        if exchange is not None:
+            buf = self.buffers.get(exchange)
+            if buf is None or buf.dtype != "f32" or math.prod(buf.shape) != 1:
+                raise ValueError(f"exchange: {exchange!r} is not a one-element f32 buffer")
         self.k = Kernel(op.name, list(arg_order), block, no_fusion=no_fusion, no_cse=no_cse)
         self.no_unroll = no_unroll
         self.env: dict[str, Value] = {}
@@ -230,6 +236,12 @@ class Lowering:
         with k.skip_if(past) if past else nullcontext(), self._block():
             self.env |= self._decode(t, gid, self._raster(t))
             self.body(t.body)
+        if self.exchange is not None:  # every thread reaches it, past the tail guard
+            from .templates.exchange import emit_epilogue
+
+            # whichever thread added the block's share, it happens before thread 0's release
+            k.emit("bar.sync", src=("0",), barrier=True)
+            emit_epilogue(k, self.tid, self.mem[self.exchange].ptr)
 
     def emit_Sync(self, s: Sync) -> None:
         if s.warp:

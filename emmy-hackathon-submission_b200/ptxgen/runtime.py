@@ -67,6 +67,7 @@ def library() -> ctypes.CDLL:
                                    ctypes.POINTER(ctypes.c_float)],
                 "pg_tensormap_fill": [vp, cp, i32, i32, u64, pu64, pu64, pu32, i32],
                 "pg_status_take": [vp, pu32],
+                "pg_global_write": [vp, cp, vp, ctypes.c_size_t],
                 "pg_memset_async": [u64, ctypes.c_size_t, u64],
                 "pg_memcpy_htod_async": [u64, vp, ctypes.c_size_t, u64],
                 "pg_memcpy_dtoh_async": [vp, u64, ctypes.c_size_t, u64],
@@ -168,6 +169,12 @@ class Module:
             _check(lib.pg_tensormap_fill(self.handle, t.symbol.encode(), _DTYPE_CODE[t.dtype],
                                          rank, pointers[t.buffer], dims, strides, box,
                                          t.swizzle), f"pg_tensormap_fill({t.symbol})")
+
+    def write_global(self, symbol: str, data: bytes) -> None:
+        """Copy ``data`` into the module's ``.global`` symbol (at most its size)."""
+        buf = ctypes.create_string_buffer(data, len(data))
+        _check(library().pg_global_write(self.handle, symbol.encode(), buf, len(data)),
+               f"pg_global_write({symbol})")
 
     def status(self) -> int:
         out = ctypes.c_uint32()

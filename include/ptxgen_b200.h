@@ -108,6 +108,12 @@ int pg_tensormap_fill(pg_module *module, const char *symbol, int dtype, int rank
                       const uint64_t *dims, const uint64_t *strides_bytes, const uint32_t *box,
                       int swizzle_bytes);
 
+/* Copy `bytes` bytes from host memory into the module's .global symbol `symbol` (at most its
+ * size). Synchronous. No counterpart in the reference: a kernel whose partial result is summed
+ * across ranks inside the kernel reads its exchange configuration (peer addresses, rank) from
+ * module globals, so its parameters stay the plain device pointers of meta.arg_order. */
+int pg_global_write(pg_module *module, const char *symbol, const void *data, size_t bytes);
+
 /* Read the module's 32-bit status word (.global ptxgen_status) into *status and clear it;
  * *status is 0 when the module has none. Synchronous. */
 int pg_status_take(pg_module *module, uint32_t *status);

@@ -18,6 +18,7 @@ must both hold the rank-order f32 sum bit for bit.
 from __future__ import annotations
 
 import os
+import re
 import shutil
 import subprocess
 import sys
@@ -150,3 +151,162 @@ def test_two_gpus_agree_on_the_rank_order_sum(cuda, tmp_path) -> None:
             want = np.float32(want + v)
         for r in range(world):
             assert np.float32(outs[r][i]) == want, (i, r, outs[r][i], want)
+
+
+# --- the exchange as the epilogue of the sum kernel itself ----------------------------------------
+
+
+def _fused_sum(n: int = 1 << 16, blocks: int = 8):
+    from ptxgen import problems
+    from ptxgen.peer import with_exchange
+
+    return with_exchange(problems.full_sum(n, blocks=blocks), "sum_1")
+
+
+def test_fused_sum_keeps_the_meta_parameters_and_assembles(tmp_path) -> None:
+    from ptxgen.compiler import to_ptx
+    from ptxgen.ir import Graph
+
+    spec = _fused_sum()
+    ptx = to_ptx(Graph.from_dict(spec.graph), spec.meta)
+    params = re.findall(r"\.param \.u64 (\w+)", ptx)
+    assert params == [f"k_sum_1_reduce_param_{a}" for a in spec.meta["kernels"][0]["arg_order"]]
+    assert ptx.count("atom.add.acq_rel.gpu.global.u32") == 1
+    assert ptx.count("st.relaxed.sys.global.u64") == 1 and "multicast" not in ptx
+    if shutil.which("ptxas") is None:
+        pytest.skip("no ptxas")
+    f = tmp_path / "fused.ptx"
+    f.write_text(ptx)
+    subprocess.run(["ptxas", "-arch=sm_100a", str(f), "-o", str(tmp_path / "fused.cubin")],
+                   check=True, capture_output=True)
+
+
+class _Slots:
+    """A stand-in for ``PeerSlots`` on one GPU: every rank's slot array is a local buffer."""
+
+    def __init__(self, world: int):
+        import torch
+
+        self.rank, self.world = 0, world
+        self.arrays = [torch.zeros(2 * world, dtype=torch.int64, device="cuda")
+                       for _ in range(world)]
+        self.slots = self.arrays[0]
+        self.peers = torch.tensor([a.data_ptr() for a in self.arrays], dtype=torch.int64,
+                                  device="cuda")
+
+
+def _fused_run(world: int, prefill: dict[int, float], limit_ns: int, launches: int = 1):
+    """``launches`` launches of the fused sum of 2^16 ones as rank 0 of ``world``; ``prefill``
+    maps rank -> partial already present in rank 0's slots for every launch's sequence number."""
+    import torch
+
+    from ptxgen.peer import bind_exchange
+    from ptxgen.runtime import Problem
+
+    spec = _fused_sum()
+    prob = Problem(spec.graph, spec.meta)
+    tensors = prob.allocate()
+    tensors["x"].fill_(1.0)
+    fake = _Slots(world)
+    bind_exchange(prob.module, fake, limit_ns)
+    out = []
+    for seq in range(1, launches + 1):
+        for p, v in prefill.items():
+            fake.slots[(seq & 1) * world + p] = int(_word(seq, np.float32(v)))
+        prob.launch(tensors)
+        torch.cuda.synchronize()
+        out.append(float(tensors["sum_1"].item()))
+    return prob.module.status(), out, [a.cpu().numpy() for a in fake.arrays]
+
+
+@pytest.mark.gpu
+def test_fused_sum_one_rank(cuda) -> None:
+    status, out, _ = _fused_run(1, {}, 1_000_000_000, launches=3)
+    assert status == 0 and out == [65536.0] * 3  # the block counter resets between launches
+
+
+@pytest.mark.gpu
+def test_fused_sum_emulated_peer(cuda) -> None:
+    status, out, arrays = _fused_run(2, {1: 0.5}, 1_000_000_000, launches=2)
+    assert status == 0 and out == [65536.5, 65536.5]
+    assert arrays[1][0] == _word(2, np.float32(65536.0))  # seq 2's word to "rank 1", slot 0
+
+
+@pytest.mark.gpu
+def test_fused_sum_missing_peer_gives_up(cuda) -> None:
+    status, out, _ = _fused_run(2, {}, 10_000_000)
+    assert status == 1 << STATUS_TIMEOUT
+    assert out == [65536.0]  # the rank's own partial, not a total
+
+
+_FUSED_WORKER = r"""
+import os, sys, torch, torch.distributed as dist
+sys.path[:0] = [sys.argv[1], os.path.join(sys.argv[1], "emmy-hackathon-submission_b200")]
+rank, world = int(sys.argv[2]), int(sys.argv[3])
+torch.cuda.set_device(rank)
+dist.init_process_group("gloo", init_method="tcp://127.0.0.1:" + sys.argv[4], rank=rank,
+                        world_size=world)
+from ptxgen import problems
+from ptxgen.peer import PeerSlots, bind_exchange, check_exchange, with_exchange
+from ptxgen.runtime import Problem, init
+init(rank)
+spec = with_exchange(problems.full_sum(1 << 20, blocks=64), "sum_1")
+prob = Problem(spec.graph, spec.meta, device=rank)
+t = prob.allocate()
+t["x"].fill_(float(rank + 1))
+slots = PeerSlots(device=rank)
+bind_exchange(prob.module, slots)
+out = []
+for i in range(20):
+    prob.launch(t)
+    torch.cuda.synchronize()
+    out.append(float(t["sum_1"].item()))
+check_exchange(prob.module)
+dist.barrier()
+slots.close()
+dist.destroy_process_group()
+print("RESULT", " ".join(repr(v) for v in out), flush=True)
+"""
+
+
+@pytest.mark.gpu
+def test_two_gpus_fused_sum(cuda, tmp_path) -> None:
+    """Rank r sums 2^20 copies of r + 1 (exact in f32): both ranks must hold 3 * 2^20."""
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world, port = 2, str(29900 + os.getpid() % 90)
+    script = tmp_path / "fused_worker.py"
+    script.write_text(_FUSED_WORKER)
+    procs = [subprocess.Popen([sys.executable, str(script), str(ROOT), str(r), str(world), port],
+                              stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)
+             for r in range(world)]
+    for p in procs:
+        try:
+            so, se = p.communicate(timeout=240)
+        except subprocess.TimeoutExpired:
+            for q in procs:
+                q.kill()
+            raise
+        assert p.returncode == 0, se[-2000:]
+        got = [float(v) for v in so.split("RESULT", 1)[1].split()]
+        assert got == [3.0 * (1 << 20)] * 20
+
+
+@pytest.mark.gpu
+def test_fused_sum_never_bound_exchanges_nothing(cuda) -> None:
+    """A fused kernel launched before ``bind_exchange`` leaves its partial and reports."""
+    import torch
+
+    from ptxgen.runtime import Problem
+    from ptxgen.templates.exchange import STATUS_UNBOUND
+
+    spec = _fused_sum()
+    prob = Problem(spec.graph, spec.meta)
+    tensors = prob.allocate()
+    tensors["x"].fill_(1.0)
+    prob.launch(tensors)
+    torch.cuda.synchronize()
+    assert prob.module.status() == 1 << STATUS_UNBOUND
+    assert float(tensors["sum_1"].item()) == 65536.0
