@@ -62,9 +62,10 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--ablation", action="store_true",
                    help="instead of the benchmark: time the reference's shipped example kernels "
                         "under each compiler flag (its published ablation tables), one JSON line")
-    p.add_argument("--collective", choices=("peer", "nccl"), default="peer",
-                   help="how the sharded sum's partials are summed across ranks: this "
-                        "repository's one-warp kernel over NVLink peer memory, or NCCL")
+    p.add_argument("--collective", choices=("fused", "peer", "nccl"), default="fused",
+                   help="how the sharded sum's partials are summed across ranks: inside the sum "
+                        "kernel (its last block exchanges over NVLink peer memory), by a "
+                        "separate one-warp kernel over peer memory, or by NCCL")
     p.add_argument("--e2e-lanes", type=int, default=2,
                    help="steps of the host-buffer (e2e) path in flight at once, one stream each")
     p.add_argument("--only", default=None,
@@ -266,12 +267,18 @@ def measure_kernel(plan: Any, steps: int, warmup: int, world: int, l2: str = "wr
             torch.sum(reread.view(torch.int64), dim=(0,), out=sink)
 
     collective = bool(plan.allreduce) and world > 1
+    fused = collective and via == "fused"  # the kernel sums its partial across ranks itself
     mids: list[Any] = []
-    peer = None
+    peer = slots = None
     if collective and via == "peer":
         from ptxgen.peer import PeerSum
 
         peer = PeerSum()
+    if fused:
+        from ptxgen.peer import PeerSlots, bind_exchange
+
+        slots = PeerSlots()
+        bind_exchange(prob.module, slots)
 
     def combine(t: Any, s: Any) -> None:
         """The path's collective: this rank's partial summed over the ranks, in place."""
@@ -285,7 +292,7 @@ def measure_kernel(plan: Any, steps: int, warmup: int, world: int, l2: str = "wr
 
     def step(mid: Any = None) -> None:
         prob.launch(tensors, stream=stream.cuda_stream)
-        if collective:
+        if collective and not fused:
             if mid is not None:
                 mid.record(stream)
             for name in plan.allreduce:
@@ -315,7 +322,7 @@ def measure_kernel(plan: Any, steps: int, warmup: int, world: int, l2: str = "wr
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     stops = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     sampler = ClockSampler(torch.cuda.current_device())
-    if collective:
+    if collective and not fused:
         mids = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     with sampler:
         for i in range(steps):
@@ -344,7 +351,8 @@ def measure_kernel(plan: Any, steps: int, warmup: int, world: int, l2: str = "wr
     out = {"mean_ms": max_over_ranks(mean_ms, world),
            "median_ms": max_over_ranks(statistics.median(times), world),
            "min_ms": max_over_ranks(min(times), world), "launches": steps,
-           "clocks": sampler.summary(), "tensors": tensors, "prob": prob, "peer": peer}
+           "clocks": sampler.summary(), "tensors": tensors, "prob": prob, "peer": peer,
+           "slots": slots}
     return out
 
 
@@ -385,14 +393,14 @@ def _host_lane(prob: Any, tensors: dict[str, Any], stream: int) -> dict[str, Any
 
 
 def measure_e2e(plan: Any, prob: Any, tensors: dict[str, Any], steps: int, world: int,
-                in_flight: int = 2, peer: Any = None) -> dict[str, Any]:
+                in_flight: int = 2, peer: Any = None, fused: bool = False) -> dict[str, Any]:
     """The same metric through ``pg_run_host``, the one-call host-buffer API: every step copies
     its page-locked inputs in, zeroes its zero_outputs, launches, copies its outputs back and
     waits. ``in_flight`` steps run at a time, each lane with its own module, buffers and
     stream, so one step's upload overlaps another's download on the full-duplex link (a
     workload with a collective keeps one lane, its partial summed over the ranks after each
-    step by ``peer`` when given, else by NCCL). The value is all steps' work over the wall time
-    from the first call to the last return."""
+    step by ``peer`` when given, else by NCCL, or inside the kernel when ``fused``). The value is
+    all steps' work over the wall time from the first call to the last return."""
     import torch
 
     from ptxgen.runtime import Problem
@@ -410,7 +418,7 @@ def measure_e2e(plan: Any, prob: Any, tensors: dict[str, Any], steps: int, world
     def run(lane: dict[str, Any], count: int) -> None:
         for _ in range(count):
             lane["kernel"].run_host(*lane["args"])
-            if plan.allreduce and world > 1:
+            if plan.allreduce and world > 1 and not fused:
                 import torch.distributed as tdist
 
                 for name in plan.allreduce:
@@ -537,7 +545,14 @@ def run_ours(args: argparse.Namespace) -> None:
     def plan_for(name: str) -> Any:
         if args.share > 1:
             return shard.local_problem(name, args.share)
-        return shard.local_problem(name, world, weak=args.scaling == "weak")
+        plan = shard.local_problem(name, world, weak=args.scaling == "weak")
+        if args.collective == "fused" and plan.allreduce and world > 1:
+            import dataclasses
+
+            from ptxgen.peer import with_exchange
+
+            plan = dataclasses.replace(plan, spec=with_exchange(plan.spec, plan.allreduce[0]))
+        return plan
 
     def one(name: str, steps: int, warmup: int, with_e2e: bool) -> dict[str, Any]:
         log(f"{name}: compile and inputs")
@@ -558,16 +573,17 @@ def run_ours(args: argparse.Namespace) -> None:
         log(f"{name}: {res['ms_per_step']:.4f} ms per step, {res['value']:.1f} {unit}")
         if with_e2e:
             e = measure_e2e(plan, m["prob"], m["tensors"], max(3, min(steps, 20)), world,
-                            args.e2e_lanes, m["peer"])
+                            args.e2e_lanes, m["peer"], fused=m["slots"] is not None)
             res["e2e"] = {"value": plan.work * world / e["mean_s"] / scale, "unit": unit,
                           "h2d_bytes_per_step": e["h2d"], "d2h_bytes_per_step": e["d2h"],
                           "steps_in_flight": e["in_flight"]}
-        if m["peer"] is not None:  # every rank is past its last call before any unmaps
+        if m["peer"] is not None or m["slots"] is not None:  # all ranks done before unmapping
             import torch.distributed as tdist
 
-            m["peer"].check()
+            if m["peer"] is not None:
+                m["peer"].check()
             tdist.barrier()
-            m["peer"].close()
+            (m["peer"] or m["slots"]).close()
         del m
         torch.cuda.empty_cache()
         return res
@@ -601,8 +617,10 @@ def run_ours(args: argparse.Namespace) -> None:
                    "share": f"1/{args.share} of the workload" if args.share > 1 else "whole",
                    "l2": L2_MODES[args.l2],
                    "allreduce": list(plan.allreduce),
-                   "collective": (("peer memory: ptxgen.peer's one-warp kernel over NVLink"
-                                   if args.collective == "peer" else "NCCL all-reduce")
+                   "collective": ({"fused": "inside the sum kernel: its last block exchanges "
+                                            "the partials over NVLink peer memory",
+                                   "peer": "a separate one-warp kernel over NVLink peer memory",
+                                   "nccl": "NCCL all-reduce"}[args.collective]
                                   if plan.allreduce and world > 1 else None)},
         "roofline": head["roofline"], "e2e": head["e2e"], "clocks": head["clocks"],
         "gpu_launches": head["launches"],
