@@ -316,9 +316,14 @@ class Lowering:
             addr, align = mem.ptr, BUFFER_ALIGN
             if not var.is_const:
                 g = math.gcd(var.var_mult(k.mult), var.const)
-                wide = k.pure("mul.wide.u32", "u64", index.reg_of(k, var), str(esz))
-                addr = k.pure("add.s64", "u64", mem.ptr, wide)
                 align = min(BUFFER_ALIGN, pow2_part(g * esz))
+                # in a runtime loop: a 64-bit pointer the latch steps, not index math per trip
+                iv = k.induction(mem.ptr, var, esz, align)
+                if iv is not None:
+                    addr = iv
+                else:
+                    wide = k.pure("mul.wide.u32", "u64", index.reg_of(k, var), str(esz))
+                    addr = k.pure("add.s64", "u64", mem.ptr, wide)
             k.align[addr] = max(k.align.get(addr, 1), align)
             return addr, flat.const * esz, "global" if mem.writable else "global.nc"
         addr, align = mem.base, mem.align
@@ -734,6 +739,20 @@ class Lowering:
         top, done = k.label("loop"), k.label("loop_end")
         return i, top, done, enters
 
+    def _iv_counter(self, s: Loop | StridedLoop, i: str) -> str | None:
+        """The counter through which this loop's global addresses become 64-bit induction
+        pointers (``Kernel.induction``), or None. A pointer takes two registers for the whole
+        loop where the index arithmetic it replaces keeps one 32-bit invariant. So only loops
+        with no loop inside them and no runtime loop around them get pointers: grid-stride and
+        other flat loops. Around inner loops, or inside a loop whose carried state is live
+        across them, ptxas answered with spills. The shipped a03 went from 144 to 524
+        spilled bytes, and with unrolling off from none to 992; its time grew from 236 to
+        304 µs. The shipped a01 with unrolling off ran faster all the same (108 to 76 µs),
+        but not by a rule that tells the two apart."""
+        if self.k._loops or any(isinstance(st, Loop | StridedLoop) for st in walk(s.body)):
+            return None
+        return i
+
     def _counted(self, s: Loop | StridedLoop, start: Aff, n: int, m: int, f: int,
                  written: list[str]) -> None:
         """A bottom-tested loop over the axis itself, from ``start`` while below
@@ -750,7 +769,7 @@ class Lowering:
             return
         if enters is not True:
             k.emit("bra", src=(done,), pred=f"!{enters}", barrier=True)
-        with k.loop(entered=enters is True):
+        with k.loop(entered=enters is True, counter=self._iv_counter(s, i), step=n * f) as mark:
             k.place(top)
             for reg in written:
                 k.forget(reg)
@@ -760,6 +779,8 @@ class Lowering:
                     self.body(s.body)
         k.ranges.pop(i, None)
         again = k.reg("pred")
+        for ptr, delta in mark.incs:
+            k.emit("add.s64", (ptr,), (ptr, str(delta)))
         k.emit("add.u32", (i,), (i, str(n * f)))
         k.emit("setp.lt.s32", (again,), (i, bound_op))
         k.emit("bra", src=(top,), pred=again, barrier=True)
@@ -779,7 +800,9 @@ class Lowering:
             return
         if enters is not True:
             k.emit("bra", src=(done,), pred=f"!{enters}", barrier=True)
-        with k.loop(entered=enters is True):
+        const_step = step.const if step.is_const else 0
+        with k.loop(entered=enters is True, counter=self._iv_counter(s, i),
+                    step=const_step) as mark:
             k.place(top)
             for reg in written:
                 k.forget(reg)
@@ -788,6 +811,8 @@ class Lowering:
                 self.body(s.body)
         k.ranges.pop(i, None)
         again = k.reg("pred")
+        for ptr, delta in mark.incs:
+            k.emit("add.s64", (ptr,), (ptr, str(delta)))
         k.emit("add.u32", (i,), (i, step_op))
         k.emit("setp.lt.s32", (again,), (i, end_op))
         k.emit("bra", src=(top,), pred=again, barrier=True)

@@ -25,7 +25,8 @@ import re
 from collections import Counter
 from collections.abc import Iterator
 from contextlib import contextmanager
-from dataclasses import dataclass
+from dataclasses import dataclass, field
+from typing import Any
 
 from .dtypes import REG_PREFIXES, move_type, reg_class, size
 
@@ -104,6 +105,11 @@ class _LoopMark:
     at: int  # body index in front of the loop, where hoisted instructions go
     born: int  # registers numbered from here on belong to the loop
     home: int  # the scope that keeps hoisted results
+    counter: str | None = None  # the loop's counter register, when it steps by a constant
+    step: int = 0  # what the latch adds to the counter each trip
+    # 64-bit induction pointers: key -> (register, alignment), and what the latch adds to each
+    ivs: dict = field(default_factory=dict)
+    incs: list = field(default_factory=list)
 
 
 class Kernel:
@@ -266,16 +272,61 @@ class Kernel:
                 self._defs.pop(out, None)
 
     @contextmanager
-    def loop(self, entered: bool) -> Iterator[None]:
+    def loop(self, entered: bool, counter: str | None = None, step: int = 0
+             ) -> Iterator[_LoopMark]:
         """The body of a runtime loop. ``entered``: every thread runs at least one trip, so code
-        in front of the loop dominates what follows it and hoisted results stay reusable."""
+        in front of the loop dominates what follows it and hoisted results stay reusable.
+        ``counter``/``step``: the counter register and its constant step, which lets addresses
+        become induction pointers (``induction``); the caller adds each ``incs`` entry to its
+        pointer at the latch."""
         home = len(self._scopes) - 1 if entered else len(self._scopes)
-        self._loops.append(_LoopMark(len(self.body), len(self._born), home))
+        mark = _LoopMark(len(self.body), len(self._born), home, counter, step)
+        self._loops.append(mark)
         try:
             with self.region():
-                yield
+                yield mark
         finally:
             self._loops.pop()
+
+    def induction(self, ptr: str, var: Any, esz: int, align: int) -> str | None:
+        """A 64-bit pointer register holding ``ptr + var * esz`` on every trip of the innermost
+        runtime loop, for ``var`` (an index ``Aff``) = ``coef * counter + sum(c_r * r)`` with
+        ``coef`` and every ``c_r`` positive and every ``r`` older than the loop or an enclosing
+        loop's counter. It is set in front of the loop, where the counter holds its start, by
+        the same u32 arithmetic and ``mul.wide`` the per-trip address would use, and the latch
+        adds ``coef * step * esz`` to it. None when ``var`` is not of that form (or with CSE
+        off, where every address is computed again)."""
+        if self.no_cse or not self._loops:
+            return None
+        loop = self._loops[-1]
+        if loop.counter is None or loop.step <= 0 or var.const:
+            return None
+        coef = var.terms.get(loop.counter, 0)
+        rest = {r: c for r, c in var.terms.items() if r != loop.counter}
+        outer = {m.counter for m in self._loops[:-1] if m.counter is not None}
+        if coef <= 0 or any(c <= 0 for c in rest.values()):
+            return None
+        if any(r not in outer and (r in self.variables or self._born[r] >= loop.born)
+               for r in rest):
+            return None
+        key = (ptr, coef, esz, tuple(sorted(rest.items())))
+        if key in loop.ivs:
+            return loop.ivs[key]
+        t = self.reg("u32")
+        pre = [Ins("mul.lo.u32", (t,), (loop.counter, str(coef)))]
+        for r, c in sorted(rest.items()):
+            t2 = self.reg("u32")
+            pre.append(Ins("mad.lo.u32", (t2,), (r, str(c), t)))
+            t = t2
+        w, p = self.reg("u64"), self.reg("u64")
+        pre += [Ins("mul.wide.u32", (w,), (t, str(esz))), Ins("add.s64", (p,), (ptr, w))]
+        self.body[loop.at:loop.at] = pre
+        loop.at += len(pre)
+        self.variables.add(p)
+        self.align[p] = align
+        loop.ivs[key] = p
+        loop.incs.append((p, coef * loop.step * esz))
+        return p
 
     @contextmanager
     def skip_if(self, pred: str) -> Iterator[None]:

@@ -336,3 +336,37 @@ def test_simt_matmul_reads_shared_memory_in_vectors() -> None:
     ptx = to_ptx(Graph.from_dict(graph), meta)
     assert ptx.count("ld.shared.v4.f32") == 64 and ptx.count("ld.shared.v2.f32") == 128
     assert "ld.shared.f32" not in ptx
+
+
+def _loop_bodies(ptx: str) -> list[list[str]]:
+    """The instruction mnemonics of each innermost runtime loop, in order."""
+    out = []
+    for m in re.finditer(r"(\$L_loop_\d+):\n(.*?)\n\$L_loop_end_\d+:", ptx, re.S):
+        lines = [ln.strip() for ln in m.group(2).splitlines()]
+        if any(ln.startswith("$L_loop_") for ln in lines):
+            continue
+        out.append([ln.split()[0] for ln in lines if ln and not ln.startswith(("$", "//"))])
+    return out
+
+
+def test_flat_runtime_loops_step_induction_pointers() -> None:
+    """A runtime loop with no loop inside or around it loads through a 64-bit pointer its latch
+    steps: r02's loop with unrolling off (128 threads x 4 bytes a trip) and config 4's
+    grid-stride sum (copies of 148 x 8 blocks x 256 threads x 4 bytes). A loop nested in another,
+    like
+    a01's dot products with unrolling off, keeps its index arithmetic: a pointer there stays
+    live beside the outer loop's state, and ptxas spilled."""
+    graph, meta = shipped("r02_big_sum")
+    body = _loop_bodies(to_ptx(Graph.from_dict(graph), meta, no_unroll=True))[0]
+    assert body.count("ld.global.nc.f32") == 1 and body.count("add.s64") == 1
+    assert not {"mul.wide.u32", "mad.lo.u32"} & set(body)
+    step = re.search(r"add\.s64 (%rd\d+), \1, (\d+);", compile_spec(problems.full_sum(1 << 30)))
+    assert step and int(step.group(2)) % (148 * 8 * 256 * 4) == 0
+    graph, meta = shipped("a01_attention")
+    body = next(b for b in _loop_bodies(to_ptx(Graph.from_dict(graph), meta, no_unroll=True))
+                if "fma.rn.f32" in b)
+    assert "mul.wide.u32" in body
+    # with CSE off every address is computed again on every trip
+    graph, meta = shipped("r02_big_sum")
+    body = _loop_bodies(to_ptx(Graph.from_dict(graph), meta, no_unroll=True, no_cse=True))[0]
+    assert "mul.wide.u32" in body
