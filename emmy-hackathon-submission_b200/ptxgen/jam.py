@@ -1,0 +1,67 @@
+"""Loop jamming: consecutive sibling loops over one axis become one loop.
+
+Emmy writes an attention nest's per-row inner products as sibling loops over the same axis: the
+shipped a01 has four per key, one per query row, and a03 six. Each is fully unrolled. Emitted one
+after another, every copy of the shared ``kt[d, key]`` loads stays live from the first row's
+loop to the last, and ptxas spills. Jammed, trip ``d`` of every row's loop is emitted together.
+Each row then uses ``kt[d]`` at once. On a B200, a01 went from 40.7 to 36.7 µs and a03 from 100.1
+to 93.8 µs.
+
+Each accumulator still takes exactly its own operations in its own order, so results are the same
+bit for bit. That holds because loops are jammed only when it cannot change what any statement
+sees:
+
+* both are ``Loop`` statements over the same axis, with the same ``seed`` and ``unroll``;
+* their bodies hold only loads, assignments and accumulations: no writes, copies, barriers,
+  shuffles or nested control flow;
+* neither reads or writes a name the other writes.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Sequence
+from dataclasses import fields, replace
+
+from .ir import Accum, Assign, Load, Loop, Stmt, walk
+
+_PLAIN = (Load, Assign, Accum)
+
+
+def _names(loop: Loop) -> tuple[set[str], set[str]] | None:
+    """(names read, names written) by the loop's body; None when it holds anything else."""
+    reads: set[str] = set()
+    writes: set[str] = set()
+    for st in walk(loop.body):
+        if not isinstance(st, _PLAIN):
+            return None
+        reads.update(st.deps())
+        writes.update(st.defines())
+    return reads, writes
+
+
+def can_jam(a: Stmt, b: Stmt) -> bool:
+    """Whether ``b`` may run trip by trip beside ``a`` instead of after it."""
+    if not (isinstance(a, Loop) and isinstance(b, Loop)):
+        return False
+    if a.axis != b.axis or a.seed != b.seed or a.unroll != b.unroll:
+        return False
+    na, nb = _names(a), _names(b)
+    if na is None or nb is None:
+        return False
+    (reads_a, writes_a), (reads_b, writes_b) = na, nb
+    return not (writes_a & (reads_b | writes_b)) and not (writes_b & reads_a)
+
+
+def jam(body: Sequence[Stmt]) -> tuple[Stmt, ...]:
+    """``body`` with every run of jammable sibling loops merged, at every depth."""
+    out: list[Stmt] = []
+    for st in body:
+        nested = {f.name: jam(getattr(st, f.name)) for f in fields(st)
+                  if f.name in ("body", "else_body") and isinstance(getattr(st, f.name), tuple)}
+        if nested:
+            st = replace(st, **nested)
+        if out and can_jam(out[-1], st):
+            out[-1] = replace(out[-1], body=out[-1].body + st.body)
+        else:
+            out.append(st)
+    return tuple(out)
