@@ -157,6 +157,12 @@ struct TmapKey {
 
 }  // namespace
 
+// Records `msg` as this thread's last error and returns `code`: the error channel of the entry
+// points defined in other translation units (noalloc_sum.cu). Not exported.
+__attribute__((visibility("hidden"))) int pg_detail_fail(int code, const char *msg) {
+  return fail(code, "%s", msg);
+}
+
 struct pg_module {
   CUmodule mod = nullptr;
   std::unordered_map<std::string, TmapKey> filled;

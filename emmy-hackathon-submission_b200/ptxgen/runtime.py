@@ -77,6 +77,7 @@ def library() -> ctypes.CDLL:
                 "pg_ipc_handle": [u64, vp, pu64],
                 "pg_ipc_open": [vp, pu64],
                 "pg_ipc_close": [u64],
+                "pg_grid_sum_f32_noalloc": [u64, u64, u64, u32, u64],
             }
             for name, args in sig.items():
                 fn = getattr(lib, name)
