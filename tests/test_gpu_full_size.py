@@ -1,0 +1,125 @@
+"""The benchmark configurations at their full sizes, through properties that do not depend on
+the size.
+
+* Configs 2 and 3: every output row depends only on its own input row (and config 2's per-row
+  scale), so the first, the last and random rows of the full-size GPU output are checked
+  against the oracle's run of the same kernel on just those rows, at the small cases' bars
+  (one bf16 ulp; rel 2e-5). Each of config 3's 16384 rows also sums to 1.
+* Config 4: the sum of all 2^30 elements against an f64 sum of the same data (rel 1e-5).
+* Configs 5 and 5b: sampled full rows of C against the f64 product of the same bf16 operands
+  (rel 1e-2 per element, floor 1e-3 of the largest |C| in those rows).
+
+The row-independence the first item rests on is itself checked on the CPU: the oracle's run on
+picked rows equals its run on the whole problem, row for row.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+from conftest import gpu_run, oracle_run, reference_inputs
+
+from ptxgen import problems
+
+
+def picked_rows(rows: int, count: int = 16, seed: int = 7) -> np.ndarray:
+    """The first and last rows and ``count`` others, sorted."""
+    rng = np.random.default_rng(seed)
+    return np.array(sorted({0, rows - 1, *rng.choice(rows, count, replace=False).tolist()}))
+
+
+def gelu_on_rows(spec: problems.ProblemSpec, ins: dict[str, np.ndarray], rows: np.ndarray
+                 ) -> tuple[problems.ProblemSpec, dict[str, np.ndarray]]:
+    """Config 2's kernel over only ``rows`` of ``ins`` (same constants a, b)."""
+    cols = int(ins["x"].shape[1])
+    a, b = float(ins["mul_c1"][0]), float(ins["add_c1"][0])
+    small = problems.gelu_chain(len(rows), cols, a=a, b=b)
+    return small, {"mul_c1": ins["mul_c1"], "add_c1": ins["add_c1"],
+                   "x": np.ascontiguousarray(ins["x"][rows]), "s": ins["s"][rows]}
+
+
+def test_oracle_rows_are_independent() -> None:
+    """The oracle's output rows of configs 2 and 3 on picked rows equal its rows of the whole
+    problem: the premise of the full-size row checks."""
+    spec = problems.gelu_chain(40, 256)
+    ins = reference_inputs(spec.meta)
+    whole = oracle_run(spec.graph, spec.meta, ins)["mul_1"]
+    rows = picked_rows(40, 6)
+    small, sub = gelu_on_rows(spec, ins, rows)
+    assert np.array_equal(oracle_run(small.graph, small.meta, sub)["mul_1"], whole[rows])
+
+    spec = problems.row_softmax(24, 1024)
+    ins = reference_inputs(spec.meta)
+    whole = oracle_run(spec.graph, spec.meta, ins)["softmax"]
+    rows = picked_rows(24, 5)
+    small = problems.row_softmax(len(rows), 1024)
+    got = oracle_run(small.graph, small.meta, {"x": np.ascontiguousarray(ins["x"][rows])})
+    assert np.array_equal(got["softmax"], whole[rows])
+
+
+@pytest.mark.gpu
+def test_c2_full_size_rows(cuda) -> None:
+    from test_gpu_parity import check
+
+    spec = problems.CONFIGS["c2_gelu_chain"]()
+    ins = reference_inputs(spec.meta)
+    got = gpu_run(spec.graph, spec.meta, ins)["mul_1"]
+    rows = picked_rows(got.shape[0])
+    small, sub = gelu_on_rows(spec, ins, rows)
+    want = oracle_run(small.graph, small.meta, sub)["mul_1"]
+    check("ulp", got[rows], want, "bf16", 1)
+
+
+@pytest.mark.gpu
+def test_c3_full_size_rows(cuda) -> None:
+    from test_gpu_parity import check
+
+    spec = problems.CONFIGS["c3_row_softmax"]()
+    ins = reference_inputs(spec.meta)
+    got = gpu_run(spec.graph, spec.meta, ins)["softmax"]
+    sums = got.astype(np.float64).sum(axis=1)
+    assert np.abs(sums - 1).max() < 1e-4, np.abs(sums - 1).max()
+    rows = picked_rows(got.shape[0])
+    cols = got.shape[1]
+    small = problems.row_softmax(len(rows), cols)
+    want = oracle_run(small.graph, small.meta,
+                      {"x": np.ascontiguousarray(ins["x"][rows])})["softmax"]
+    check("rel", got[rows], want, "f32", 2e-5)
+
+
+@pytest.mark.gpu
+def test_c4_full_size_against_f64(cuda) -> None:
+    """2^30 f32 elements ~ U(0,1) drawn on the device; the kernel's sum against torch's f64
+    sum of the same tensor (the checker only)."""
+    import torch
+
+    from ptxgen.runtime import Problem
+
+    spec = problems.CONFIGS["c4_full_sum"]()
+    prob = Problem(spec.graph, spec.meta)
+    tensors = prob.allocate()
+    gen = torch.Generator(device=cuda)
+    gen.manual_seed(0)
+    tensors["x"].uniform_(0.0, 1.0, generator=gen)
+    tensors["sum_1"].fill_(float("nan"))
+    prob.launch(tensors, check_status=True)
+    torch.cuda.synchronize()
+    got = float(tensors["sum_1"][0])
+    want = float(torch.sum(tensors["x"], dtype=torch.float64))
+    assert abs(got / want - 1) < 1e-5, (got, want)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("key", ["c5_matmul", "c5b_matmul_splitk"])
+def test_gemm_full_size_rows(cuda, key: str) -> None:
+    from test_gpu_gemm import assert_gemm_close
+
+    from oracle.fp import bf16_bits_to_f32
+
+    spec = problems.CONFIGS[key]()
+    ins = reference_inputs(spec.meta)
+    got = gpu_run(spec.graph, spec.meta, ins)["matmul"]
+    rows = picked_rows(got.shape[0])
+    a = bf16_bits_to_f32(ins["x0"][rows]).astype(np.float64)
+    b = bf16_bits_to_f32(ins["x1"]).astype(np.float64)
+    assert_gemm_close(got[rows], a @ b)
