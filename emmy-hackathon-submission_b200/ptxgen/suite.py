@@ -40,8 +40,8 @@ import numpy as np
 from .ir import (Accum, Assign, Axis, BinaryExpr, Cond, Dim, Init, Let, Literal, Load, Loop,
                  Stmt, StridedLoop, TensorSpec, Tile, Write, constant_node, dt, input_node,
                  kernel_node)
-from .problems import I, ProblemSpec, V, _arg, _block_reduce, _spec, add, div, matmul, mul, op, \
-    rem
+from .problems import GELU_C, GELU_K, I, ProblemSpec, V, _arg, _block_reduce, _spec, add, div, \
+    matmul, mul, op, rem
 
 # --- case container ----------------------------------------------------------------------------
 
@@ -153,11 +153,13 @@ class Rowwise:
     passes: list[tuple[Any, ...]]
     consts: dict[str, float] = field(default_factory=dict)
     block: int = 128
+    cols_in: tuple[str, ...] = ()  # f32 inputs of shape [cols], read by column in write sweeps
 
     def build(self) -> ProblemSpec:
         rows, cols = self.x.shape
         a0, t = V("a0"), V("a1_co")
         xdt = dt(self.x.dtype)
+        odt = dt(self.out[1])
         body: list[Stmt] = [Load((c,), c, (I(0),), dt("f32")) for c in self.consts]
         body.append(Let("n_cols", Literal(float(cols), "float"), dt("f32")))
         per_row = False
@@ -170,8 +172,10 @@ class Rowwise:
             # each sweep loads x under its own name
             xv = f"xv{k}"
 
-            def steps(ss: Sequence[Step], xv: str = xv) -> list[Stmt]:
-                return [Assign(s.name, op(s.fn), tuple(xv if a == "xv" else a for a in s.args),
+            names = {"xv": xv, **{c: f"{c}{k}" for c in self.cols_in}}
+
+            def steps(ss: Sequence[Step], names: dict[str, str] = names) -> list[Stmt]:
+                return [Assign(s.name, op(s.fn), tuple(names.get(a, a) for a in s.args),
                                dt(s.dtype) if s.dtype else None) for s in ss]
 
             def val(v: str, xv: str = xv) -> str:
@@ -187,23 +191,24 @@ class Rowwise:
                 body += steps([p[1]])
             elif p[0] == "write":
                 _, ss, value = p
-                body.append(sweep([load, *steps(ss),
-                                   Write(self.out[0], (a0, V("a1")), (val(value),),
-                                         dt("f32"))]))
+                col_loads = [Load((f"{c}{k}",), c, (V("a1"),), dt("f32")) for c in self.cols_in]
+                body.append(sweep([load, *col_loads, *steps(ss),
+                                   Write(self.out[0], (a0, V("a1")), (val(value),), odt)]))
             elif p[0] == "row":
                 per_row = True
                 body.append(Cond(BinaryExpr("==", t, I(0)),
-                                 (Write(self.out[0], (a0,), (p[1],), dt("f32")),), ()))
+                                 (Write(self.out[0], (a0,), (p[1],), odt),), ()))
             else:
                 raise ValueError(f"pass {k}: {p[0]!r}")
         tile = Tile((Axis("a0", Dim(rows)), Axis("a1_co", Dim(self.block))), tuple(body),
                     self.block)
         oshape = [rows] if per_row else [rows, cols]
         args = [_arg(c, "f32", [1], data=[v]) for c, v in self.consts.items()]
-        args += [_arg("x", self.x.dtype, self.x.shape, seed=0, dist=list(self.x.dist)),
-                 _arg(self.out[0], self.out[1], oshape, output=True)]
-        return _spec(self.pid, self.code, 0, 0, f"k_{self.pid}", tile, args, ["x"],
-                     [self.out[0]], dict(self.consts), self.block)
+        args += [_arg("x", self.x.dtype, self.x.shape, seed=0, dist=list(self.x.dist))]
+        args += [_arg(c, "f32", [cols], seed=k + 1) for k, c in enumerate(self.cols_in)]
+        args.append(_arg(self.out[0], self.out[1], oshape, output=True))
+        return _spec(self.pid, self.code, 0, 0, f"k_{self.pid}", tile, args,
+                     ["x", *self.cols_in], [self.out[0]], dict(self.consts), self.block)
 
 
 # --- reductions along other axes -------------------------------------------------------------
@@ -264,6 +269,10 @@ SQRT1_2 = 1.0 / math.sqrt(2.0)
 
 def _erf(x: np.ndarray) -> np.ndarray:
     return np.vectorize(math.erf, otypes=[np.float64])(x)
+
+
+def _d(x: np.ndarray) -> np.ndarray:
+    return x.astype(np.float64)
 
 
 def _softmax(x: np.ndarray) -> np.ndarray:
@@ -459,15 +468,166 @@ POINTWISE: dict[str, Callable[[], SuiteCase]] = {
                         [S("v0", "sigmoid", "x", dtype="f16"),
                          S("v1", "multiply", "x", "v0", dtype="f16")], "v1",
                         lambda x: x / (1 + np.exp(-x)), 1e-3, 1e-3, ("rel", 1e-3)),
+    "p00_scalar_add": _pw("p00_scalar_add", "torch.randn(128) + torch.randn(128)",
+                          [_x(128, name="a"), _x(128, name="b")], ("out", "f32", (128,)),
+                          [S("v0", "add", "a", "b")], "v0", lambda a, b: a + b, 0, 0, EXACT),
+    "p01_vector_add": _pw("p01_vector_add", "torch.randn(1024) + torch.randn(1024)",
+                          [_x(1024, name="a"), _x(1024, name="b")], ("out", "f32", (1024,)),
+                          [S("v0", "add", "a", "b")], "v0", lambda a, b: a + b, 0, 0, EXACT),
+    "p03_relu_mul": _pw("p03_relu_mul", "torch.relu(x) * y", [_x(2048), _x(2048, name="y")],
+                        ("out", "f32", (2048,)),
+                        [S("v0", "relu", "x"), S("v1", "multiply", "v0", "y")], "v1",
+                        lambda x, y: np.maximum(x, 0) * y, 0, 0, EXACT),
+    # --- the reference's remaining pointwise ids (formulas in f64 where its ``ref`` lifts
+    # to f64, cast back to f32) ---
+    "p05_add_2d": _pw("p05_add_2d", "torch.randn(64, 128) + torch.randn(64, 128)",
+                      [_x((64, 128), name="a"), _x((64, 128), name="b")],
+                      ("out", "f32", (64, 128)), [S("v0", "add", "a", "b")], "v0",
+                      lambda a, b: a + b, 0, 0, EXACT),
+    "p11_big_add": _pw("p11_big_add", "torch.randn(1 << 20) + torch.randn(1 << 20)",
+                       [_x(1 << 20, name="a"), _x(1 << 20, name="b")],
+                       ("out", "f32", (1 << 20,)), [S("v0", "add", "a", "b")], "v0",
+                       lambda a, b: a + b, 0, 0, EXACT),
+    "p22_gelu_tanh": _pw("p22_gelu_tanh", 'gelu(torch.randn(4096), approximate="tanh")',
+                         [_x(4096)], ("out", "f32", (4096,)),
+                         [S("v0", "multiply", "x", "x"), S("v1", "multiply", "v0", "x"),
+                          S("v2", "multiply", "c_cube", "v1"), S("v3", "add", "x", "v2"),
+                          S("v4", "multiply", "c_k", "v3"), S("v5", "tanh", "v4"),
+                          S("v6", "add", "v5", "c_one"), S("v7", "multiply", "c_half", "x"),
+                          S("v8", "multiply", "v7", "v6")], "v8",
+                         lambda x: (0.5 * x * (1.0 + np.tanh(GELU_K * (
+                             x + GELU_C * x.astype(np.float64) ** 3)))).astype(np.float32),
+                         1e-5, 1e-5, FAST_REL,
+                         {"c_cube": GELU_C, "c_k": GELU_K, "c_one": 1.0, "c_half": 0.5}),
+    "p33_sub_2d": _pw("p33_sub_2d", "x - y (x, y [64, 128])",
+                      [_x((64, 128)), _x((64, 128), name="y")], ("out", "f32", (64, 128)),
+                      [S("v0", "subtract", "x", "y")], "v0", lambda x, y: x - y, 0, 0, EXACT),
+    "p34_sigmoid": _pw("p34_sigmoid", "torch.sigmoid(torch.randn(2048))", [_x(2048)],
+                       ("out", "f32", (2048,)), [S("v0", "sigmoid", "x")], "v0",
+                       lambda x: (1 / (1 + np.exp(-_d(x)))).astype(np.float32), 1e-5, 1e-6,
+                       FAST),
+    "p35_tanh": _pw("p35_tanh", "torch.tanh(torch.randn(2048))", [_x(2048)],
+                    ("out", "f32", (2048,)), [S("v0", "tanh", "x")], "v0",
+                    lambda x: np.tanh(_d(x)).astype(np.float32), 1e-5, 1e-6, FAST_REL),
+    "p36_silu": _pw("p36_silu", "x * torch.sigmoid(x)", [_x(4096)], ("out", "f32", (4096,)),
+                    [S("v0", "sigmoid", "x"), S("v1", "multiply", "x", "v0")], "v1",
+                    lambda x: (_d(x) / (1 + np.exp(-_d(x)))).astype(np.float32), 1e-5, 1e-6,
+                    FAST),
+    "p38_bias_bcast": _pw("p38_bias_bcast", "x + b (x [32, 256], b [256])",
+                          [_x((32, 256)), In("b", "f32", (256,), bcast="cols")],
+                          ("out", "f32", (32, 256)), [S("v0", "add", "x", "b")], "v0",
+                          lambda x, b: x + b, 0, 0, EXACT),
+    "p39_odd_mul": _pw("p39_odd_mul", "torch.randn(1000) * torch.randn(1000)",
+                       [_x(1000, name="a"), _x(1000, name="b")], ("out", "f32", (1000,)),
+                       [S("v0", "multiply", "a", "b")], "v0", lambda a, b: a * b, 0, 0, EXACT),
+    "p40_odd_add_const": _pw("p40_odd_add_const", "torch.randn(999) + 1.5", [_x(999)],
+                             ("out", "f32", (999,)), [S("v0", "add", "x", "add_c1")], "v0",
+                             lambda x: x + np.float32(1.5), 0, 0, EXACT, {"add_c1": 1.5}),
+    "p41_maximum": _pw("p41_maximum", "torch.maximum(torch.randn(2048), torch.randn(2048))",
+                       [_x(2048, name="a"), _x(2048, name="b")], ("out", "f32", (2048,)),
+                       [S("v0", "maximum", "a", "b")], "v0", np.maximum, 0, 0, EXACT),
+    "p42_sqrt_abs": _pw("p42_sqrt_abs", "torch.sqrt(torch.randn(2048).abs())", [_x(2048)],
+                        ("out", "f32", (2048,)), [S("v0", "abs", "x"), S("v1", "sqrt", "v0")],
+                        "v1", lambda x: np.sqrt(np.abs(x)), 1e-6, 1e-6, EXACT),
+    "p43_square_shift": _pw("p43_square_shift", "(x - 0.5) * (x - 0.5)", [_x(4096)],
+                            ("out", "f32", (4096,)),
+                            [S("v0", "subtract", "x", "sub_c1"),
+                             S("v1", "multiply", "v0", "v0")], "v1",
+                            lambda x: (x - np.float32(0.5)) * (x - np.float32(0.5)), 1e-6,
+                            1e-6, EXACT, {"sub_c1": 0.5}),
+    "p45_rsqrt": _pw("p45_rsqrt", "torch.rsqrt(torch.randn(1024).abs() + 1.0)", [_x(1024)],
+                     ("out", "f32", (1024,)),
+                     [S("v0", "abs", "x"), S("v1", "add", "v0", "add_c1"),
+                      S("v2", "rsqrt", "v1")], "v2",
+                     lambda x: (1 / np.sqrt(np.abs(_d(x)) + 1.0)).astype(np.float32), 1e-5,
+                     1e-6, FAST, {"add_c1": 1.0}),
+    "p46_log": _pw("p46_log", "torch.log(torch.randn(1024).abs() + 1.0)", [_x(1024)],
+                   ("out", "f32", (1024,)),
+                   [S("v0", "abs", "x"), S("v1", "add", "v0", "add_c1"), S("v2", "log", "v1")],
+                   "v2", lambda x: np.log(np.abs(_d(x)) + 1.0).astype(np.float32), 1e-5, 1e-6,
+                   FAST_REL, {"add_c1": 1.0}),
+    "p47_gelu": _pw("p47_gelu", "torch.nn.functional.gelu(torch.randn(2048))", [_x(2048)],
+                    ("out", "f32", (2048,)),
+                    [S("v0", "multiply", "x", "c_rsqrt2"), S("v1", "erf", "v0"),
+                     S("v2", "add", "v1", "c_one"), S("v3", "multiply", "x", "c_half"),
+                     S("v4", "multiply", "v3", "v2")], "v4",
+                    lambda x: (0.5 * _d(x) * (1 + _erf(_d(x) / np.sqrt(2.0)))).astype(
+                        np.float32), 1e-4, 1e-5, FAST_REL,
+                    {"c_rsqrt2": SQRT1_2, "c_one": 1.0, "c_half": 0.5}),
+    "p48_3d_mul": _pw("p48_3d_mul", "torch.randn(4, 16, 64) * torch.randn(4, 16, 64)",
+                      [_x((4, 16, 64), name="a"), _x((4, 16, 64), name="b")],
+                      ("out", "f32", (4, 16, 64)), [S("v0", "multiply", "a", "b")], "v0",
+                      lambda a, b: a * b, 0, 0, EXACT),
+    "p49_fma3": _pw("p49_fma3", "a * b + c (512)", [_x(512, name="a"), _x(512, name="b"),
+                                                    _x(512, name="c")], ("out", "f32", (512,)),
+                    [S("v0", "multiply", "a", "b"), S("v1", "add", "v0", "c")], "v1",
+                    lambda a, b, c: a * b + c, 1e-6, 1e-6, EXACT),
+    "p51_neg_abs": _pw("p51_neg_abs", "-x.abs()", [_x(3000)], ("out", "f32", (3000,)),
+                       [S("v0", "abs", "x"), S("v1", "negative", "v0")], "v1",
+                       lambda x: -np.abs(x), 0, 0, EXACT),
+    "p53_sig_tanh": _pw("p53_sig_tanh", "torch.sigmoid(x) * torch.tanh(x) (x [4, 64])",
+                        [_x((4, 64))], ("out", "f32", (4, 64)),
+                        [S("v0", "sigmoid", "x"), S("v1", "tanh", "x"),
+                         S("v2", "multiply", "v0", "v1")], "v2",
+                        lambda x: (np.tanh(_d(x)) / (1 + np.exp(-_d(x)))).astype(np.float32),
+                        1e-5, 1e-6, FAST_REL),
+    "p55_f16_add": _pw("p55_f16_add", "f16 a + b (1024)", [_x(1024, f16x, name="a"),
+                                                          _x(1024, f16x, name="b")],
+                       ("out", "f16", (1024,)), [S("v0", "add", "a", "b", dtype="f16")], "v0",
+                       lambda a, b: (a + b).astype(np.float32), 1e-3, 1e-3, EXACT),
+    "p56_scalar_chain": _pw("p56_scalar_chain", "(x * 0.5 + 0.25) * 3.0 - 1.0", [_x(4096)],
+                            ("out", "f32", (4096,)),
+                            [S("v0", "multiply", "x", "mul_c1"), S("v1", "add", "v0", "add_c1"),
+                             S("v2", "multiply", "v1", "mul_c2"),
+                             S("v3", "subtract", "v2", "sub_c1")], "v3",
+                            lambda x: (x * np.float32(0.5) + np.float32(0.25)) * np.float32(3.0)
+                            - np.float32(1.0), 1e-6, 1e-6, EXACT,
+                            {"mul_c1": 0.5, "add_c1": 0.25, "mul_c2": 3.0, "sub_c1": 1.0}),
+    "p58_rsqrt_eps": _pw("p58_rsqrt_eps", "1.0 / torch.sqrt(torch.randn(1024).abs() + 1e-3)",
+                         [_x(1024)], ("out", "f32", (1024,)),
+                         [S("v0", "abs", "x"), S("v1", "add", "v0", "add_c1"),
+                          S("v2", "sqrt", "v1"), S("v3", "divide", "div_c1", "v2")], "v3",
+                         lambda x: (1 / np.sqrt(np.abs(_d(x)) + 1e-3)).astype(np.float32),
+                         1e-5, 1e-6, EXACT, {"add_c1": 1e-3, "div_c1": 1.0}),
+    "p59_large": _pw("p59_large", "torch.randn(1 << 20) * 2.0", [_x(1 << 20)],
+                     ("out", "f32", (1 << 20,)), [S("v0", "multiply", "x", "mul_c1")], "v0",
+                     lambda x: x * np.float32(2.0), 0, 0, EXACT, {"mul_c1": 2.0}),
+    "p60_tiny": _pw("p60_tiny", "torch.randn(7) + torch.randn(7)",
+                    [_x(7, name="a"), _x(7, name="b")], ("out", "f32", (7,)),
+                    [S("v0", "add", "a", "b")], "v0", lambda a, b: a + b, 0, 0, EXACT),
 }
 
 
 def _rw(pid: str, code: str, shape: tuple[int, int], out: tuple[str, str],
         passes: list[tuple[Any, ...]], ref: Callable[..., np.ndarray], rtol: float, atol: float,
         bar: tuple[str, float], block: int = 128, dtype: str = "f32",
-        consts: dict[str, float] | None = None) -> Callable[[], SuiteCase]:
+        consts: dict[str, float] | None = None,
+        cols_in: tuple[str, ...] = ()) -> Callable[[], SuiteCase]:
     return lambda: SuiteCase(Rowwise(pid, code, In("x", dtype, shape), out, passes,
-                                     consts or {}, block).build(), ref, rtol, atol, bar)
+                                     consts or {}, block, cols_in).build(), ref, rtol, atol, bar)
+
+
+def _softmax_passes(pre: Callable[[str, str], list[Step]] | None = None,
+                    out_cast: str | None = None) -> list[tuple[Any, ...]]:
+    """max, sum of exp(s - max), then exp(s - max) / sum, where s is x or ``pre``'s last step
+    (``pre(name, x)`` gives the steps making s under ``name``); ``out_cast`` casts the result."""
+    def s_of(tag: str) -> tuple[list[Step], str]:
+        if pre is None:
+            return [], "xv"
+        ss = pre(f"s{tag}", "xv")
+        return ss, ss[-1].name
+    s0, v0 = s_of("0")
+    s1, v1 = s_of("1")
+    s2, v2 = s_of("2")
+    write = [*s2, S("d2", "subtract", v2, "acc0"), S("e2", "exp", "d2"),
+             S("y", "multiply", "e2", "r")]
+    if out_cast:
+        write.append(S("yc", "cast", "y", dtype=out_cast))
+    return [("reduce", "acc0", "maximum", s0, v0),
+            ("reduce", "acc1", "add", [*s1, S("d", "subtract", v1, "acc0"), S("e", "exp", "d")],
+             "e"),
+            ("scalar", S("r", "reciprocal", "acc1")),
+            ("write", write, "yc" if out_cast else "y")]
 
 
 SUM = ("reduce", "acc0", "add", [], "xv")
@@ -539,6 +699,139 @@ ROWWISE: dict[str, Callable[[], SuiteCase]] = {
                             ("write", [S("d2", "subtract", "xv", "acc0"),
                                        S("y", "subtract", "d2", "lse")], "y")],
                            lambda x: np.log(_softmax(x)), 1e-4, 1e-5, FAST_REL),
+    # --- the reference's remaining row-wise, fused and whole-tensor ids; a whole-tensor
+    # reduction is one row of one block (the reference's single-block plans), and leading axes
+    # of a higher-rank input are flattened into rows ---
+    "r01_array_sum": _rw("r01_array_sum", "torch.randn(1024).sum()", (1, 1024), ("out", "f32"),
+                         [SUM, ("row", "acc0")], lambda x: _d(x).sum().astype(np.float32),
+                         1e-4, 1e-4, EXACT),
+    "r03_mean": _rw("r03_mean", "torch.randn(32768).mean()", (1, 32768), ("out", "f32"),
+                    [SUM, ("scalar", S("m", "divide", "acc0", "n_cols")), ("row", "m")],
+                    lambda x: _d(x).mean().astype(np.float32), 1e-4, 1e-4, EXACT),
+    "r04_row_sum": _rw("r04_row_sum", "torch.randn(64, 512).sum(-1)", (64, 512),
+                       ("out", "f32"), [SUM, ("row", "acc0")],
+                       lambda x: _d(x).sum(-1).astype(np.float32), 1e-4, 1e-4, EXACT),
+    "r00_sum_2048": _rw("r00_sum_2048", "torch.randn(2048).sum()", (1, 2048), ("out", "f32"),
+                        [SUM, ("row", "acc0")], lambda x: _d(x).sum().astype(np.float32),
+                        1e-4, 1e-4, EXACT),
+    "r01_sum_odd": _rw("r01_sum_odd", "torch.randn(1000).sum()", (1, 1000), ("out", "f32"),
+                       [SUM, ("row", "acc0")], lambda x: _d(x).sum().astype(np.float32),
+                       1e-4, 1e-4, EXACT),
+    "r07_sum_unpinned": _rw("r07_sum_unpinned", "torch.randn(65536).sum()", (1, 65536),
+                            ("out", "f32"), [SUM, ("row", "acc0")],
+                            lambda x: _d(x).sum().astype(np.float32), 1e-3, 1e-3, EXACT,
+                            block=256),
+    "r08_row_sum_short": _rw("r08_row_sum_short", "torch.randn(64, 32).sum(-1)", (64, 32),
+                             ("out", "f32"), [SUM, ("row", "acc0")],
+                             lambda x: _d(x).sum(-1).astype(np.float32), 1e-4, 1e-4, EXACT),
+    "r09_row_sum_unpinned": _rw("r09_row_sum_unpinned", "torch.randn(256, 512).sum(-1)",
+                                (256, 512), ("out", "f32"), [SUM, ("row", "acc0")],
+                                lambda x: _d(x).sum(-1).astype(np.float32), 1e-4, 1e-4,
+                                EXACT),
+    "r10_t256": _rw("r10_t256", "torch.randn(4096).sum(), 256 threads", (1, 4096),
+                    ("out", "f32"), [SUM, ("row", "acc0")],
+                    lambda x: _d(x).sum().astype(np.float32), 1e-4, 1e-4, EXACT, block=256),
+    "r13_t512_mean": _rw("r13_t512_mean", "torch.randn(65536).mean(), 512 threads",
+                         (1, 65536), ("out", "f32"),
+                         [SUM, ("scalar", S("m", "divide", "acc0", "n_cols")), ("row", "m")],
+                         lambda x: _d(x).mean().astype(np.float32), 1e-4, 1e-4, EXACT,
+                         block=512),
+    "r14_coop_t": _rw("r14_coop_t", "torch.randn(64, 512).sum(-1), cooperating threads",
+                      (64, 512), ("out", "f32"), [SUM, ("row", "acc0")],
+                      lambda x: _d(x).sum(-1).astype(np.float32), 1e-4, 1e-4, EXACT),
+    "r15_coop_r2": _rw("r15_coop_r2", "torch.randn(8192).sum(), cooperating threads",
+                       (1, 8192), ("out", "f32"), [SUM, ("row", "acc0")],
+                       lambda x: _d(x).sum().astype(np.float32), 1e-4, 1e-4, EXACT),
+    "r18_amax_4d": _rw("r18_amax_4d", "torch.randn(2, 4, 8, 256).amax(-1)", (64, 256),
+                       ("out", "f32"), [MAX, ("row", "acc0")], lambda x: x.max(-1), 0, 0,
+                       EXACT),
+    "r20_sig_tanh_sum": _rw("r20_sig_tanh_sum", "(sigmoid(x) * tanh(x)).sum(-1) (x [4, 64])",
+                            (4, 64), ("out", "f32"),
+                            [("reduce", "acc0", "add",
+                              [S("sg", "sigmoid", "xv"), S("th", "tanh", "xv"),
+                               S("pr", "multiply", "sg", "th")], "pr"), ("row", "acc0")],
+                            lambda x: (np.tanh(_d(x)) / (1 + np.exp(-_d(x)))).sum(-1).astype(
+                                np.float32), 1e-4, 1e-4, FAST_REL, block=64),
+    "f01_rmsnorm": _rw("f01_rmsnorm", "x / sqrt((x * x).mean(-1) + 1e-5) * w (x [64, 1024])",
+                       (64, 1024), ("out", "f32"),
+                       [SUMSQ, ("scalar", S("ms", "divide", "acc0", "n_cols")),
+                        ("scalar", S("mse", "add", "ms", "c_eps")),
+                        ("scalar", S("den", "sqrt", "mse")),
+                        ("write", [S("q", "divide", "xv", "den"), S("y", "multiply", "q", "w")],
+                         "y")],
+                       lambda x, w: (x / np.sqrt((_d(x) ** 2).mean(-1, keepdims=True) + 1e-5)
+                                     * w).astype(np.float32), 1e-3, 1e-4, EXACT,
+                       consts={"c_eps": 1e-5}, cols_in=("w",)),
+    "f02_row_softmax": _rw("f02_row_softmax", "torch.softmax(torch.randn(64, 256), dim=-1)",
+                           (64, 256), ("out", "f32"), _softmax_passes(),
+                           lambda x: _softmax(_d(x)).astype(np.float32), 1e-3, 1e-5, FAST_REL),
+    "f03_l2norm": _rw("f03_l2norm", "x / sqrt((x * x).sum(-1)) (x [64, 512])", (64, 512),
+                      ("out", "f32"),
+                      [SUMSQ, ("scalar", S("nrm", "sqrt", "acc0")),
+                       ("write", [S("y", "divide", "xv", "nrm")], "y")],
+                      lambda x: (x / np.sqrt((_d(x) ** 2).sum(-1, keepdims=True))).astype(
+                          np.float32), 1e-3, 1e-4, EXACT),
+    "f02_center": _rw("f02_center", "x - x.mean(-1, keepdim=True) (x [64, 256])", (64, 256),
+                      ("out", "f32"),
+                      [SUM, ("scalar", S("mu", "divide", "acc0", "n_cols")),
+                       ("write", [S("y", "subtract", "xv", "mu")], "y")],
+                      lambda x: (_d(x) - _d(x).mean(-1, keepdims=True)).astype(np.float32),
+                      1e-3, 1e-5, EXACT),
+    "f03_softmax_narrow": _rw("f03_softmax_narrow", "torch.softmax(torch.randn(128, 64), -1)",
+                              (128, 64), ("out", "f32"), _softmax_passes(),
+                              lambda x: _softmax(_d(x)).astype(np.float32), 1e-3, 1e-5,
+                              FAST_REL, block=64),
+    "f05_softmax_temp": _rw("f05_softmax_temp", "torch.softmax(x * 0.5, dim=-1) (x [64, 512])",
+                            (64, 512), ("out", "f32"),
+                            _softmax_passes(lambda nm, x: [S(nm, "multiply", x, "c_t")]),
+                            lambda x: _softmax(_d(x) * 0.5).astype(np.float32), 1e-3, 1e-5,
+                            FAST_REL, consts={"c_t": 0.5}),
+    "f06_rmsnorm_pow": _rw("f06_rmsnorm_pow", "x * pow(mean(pow(x, 2), -1) + 1e-6, -0.5) "
+                           "(x [2, 64, 256])", (128, 256), ("out", "f32"),
+                           [SUMSQ, ("scalar", S("ms", "divide", "acc0", "n_cols")),
+                            ("scalar", S("mse", "add", "ms", "c_eps")),
+                            ("scalar", S("inv", "pow", "mse", "c_p")),
+                            ("write", [S("y", "multiply", "xv", "inv")], "y")],
+                           lambda x: (_d(x) / np.sqrt((_d(x) ** 2).mean(-1, keepdims=True)
+                                                      + 1e-6)).astype(np.float32),
+                           1e-3, 1e-4, FAST_REL, consts={"c_eps": 1e-6, "c_p": -0.5}),
+    "f07_softmax_4d": _rw("f07_softmax_4d", "torch.softmax(torch.randn(2, 4, 16, 128), -1)",
+                          (128, 128), ("out", "f32"), _softmax_passes(),
+                          lambda x: _softmax(_d(x)).astype(np.float32), 1e-3, 1e-5, FAST_REL),
+    "f08_layernorm_affine": _rw("f08_layernorm_affine",
+                                "d / sqrt((d * d).mean(-1) + 1e-5) * w + b, d = x - x.mean(-1) "
+                                "(x [32, 256])", (32, 256), ("out", "f32"),
+                                [SUM, ("scalar", S("mu", "divide", "acc0", "n_cols")),
+                                 ("reduce", "acc1", "add", [S("c", "subtract", "xv", "mu"),
+                                                            S("c2", "multiply", "c", "c")],
+                                  "c2"),
+                                 ("scalar", S("var", "divide", "acc1", "n_cols")),
+                                 ("scalar", S("vare", "add", "var", "c_eps")),
+                                 ("scalar", S("den", "sqrt", "vare")),
+                                 ("write", [S("cc", "subtract", "xv", "mu"),
+                                            S("q", "divide", "cc", "den"),
+                                            S("qw", "multiply", "q", "w"),
+                                            S("y", "add", "qw", "b")], "y")],
+                                lambda x, w, b: ((_d(x) - _d(x).mean(-1, keepdims=True))
+                                                 / np.sqrt(_d(x).var(-1, keepdims=True) + 1e-5)
+                                                 * w + b).astype(np.float32),
+                                1e-3, 1e-4, EXACT, consts={"c_eps": 1e-5}, cols_in=("w", "b")),
+    "f09_softmax_wide": _rw("f09_softmax_wide", "torch.softmax(torch.randn(8, 4096), dim=-1)",
+                            (8, 4096), ("out", "f32"), _softmax_passes(),
+                            lambda x: _softmax(_d(x)).astype(np.float32), 1e-3, 1e-6, FAST_REL,
+                            block=256),
+    "f10_normalize_sum": _rw("f10_normalize_sum", "a / a.sum(-1, keepdim=True), a = x.abs() "
+                             "(x [64, 128])", (64, 128), ("out", "f32"),
+                             [("reduce", "acc0", "add", [S("a", "abs", "xv")], "a"),
+                              ("write", [S("a2", "abs", "xv"), S("y", "divide", "a2", "acc0")],
+                               "y")],
+                             lambda x: (np.abs(_d(x)) / np.abs(_d(x)).sum(-1, keepdims=True)
+                                        ).astype(np.float32), 1e-3, 1e-5, EXACT),
+    "f11_softmax_f16": _rw("f11_softmax_f16", "torch.softmax(f16 x [64, 256], dim=-1)",
+                           (64, 256), ("out", "f16"),
+                           _softmax_passes(lambda nm, x: [S(nm, "cast", x)], out_cast="f16"),
+                           lambda x: _softmax(_d(x)).astype(np.float16).astype(np.float32),
+                           5e-3, 1e-4, ("rel", 1e-3), dtype="f16"),
 }
 
 AXES: dict[str, Callable[[], SuiteCase]] = {
@@ -561,12 +854,69 @@ AXES: dict[str, Callable[[], SuiteCase]] = {
 }
 
 
+def dot_nest(pid: str, code: str, m: int, n: int, k: int, batch: int = 1,
+             linear: bool = False, bias: bool = False, relu: bool = False,
+             block: int = 128) -> ProblemSpec:
+    """out[(b,) i, j] = sum over k of a[(b,) i, k] * B[(b,) k, j], with B = w[j, k] for
+    ``F.linear`` (``linear``), then + bias[j] and relu: one thread per output element and a Loop
+    over k into an Init'ed accumulator, the plan for matmuls too small or too ragged for block
+    tiles (matrix-vector products, odd shapes, few rows)."""
+    a0, a1 = V("a0"), V("a1")
+    j = rem(a0, I(n))
+    i = rem(div(a0, I(n)), I(m)) if batch > 1 else div(a0, I(n))
+    bi: tuple[Any, ...] = (div(a0, I(m * n)),) if batch > 1 else ()
+    lead = [batch] if batch > 1 else []
+    bname = "w" if linear else "b"
+    body: list[Stmt] = [
+        Init("acc0", 0.0, dt("f32")),
+        Loop(Axis("a1", Dim(k)), (
+            Load(("av",), "a", (*bi, i, a1), dt("f32")),
+            Load(("bv",), bname, (j, a1) if linear else (*bi, a1, j), dt("f32")),
+            Assign("pr", op("multiply"), ("av", "bv"), dt("f32")),
+            Accum("acc0", "pr", op("add"), dt("f32"), ("a1",), None))),
+    ]
+    value = "acc0"
+    if bias:
+        body += [Load(("bb",), "bias", (j,), dt("f32")),
+                 Assign("yb", op("add"), (value, "bb"), dt("f32"))]
+        value = "yb"
+    if relu:
+        body.append(Assign("yr", op("relu"), (value,), dt("f32")))
+        value = "yr"
+    body.append(Write("out", (*bi, i, j), (value,), dt("f32")))
+    tile = Tile((Axis("a0", Dim(batch * m * n)),), tuple(body), None)
+    args = [_arg("a", "f32", lead + [m, k], seed=0),
+            _arg(bname, "f32", [n, k] if linear else lead + [k, n], seed=1)]
+    if bias:
+        args.append(_arg("bias", "f32", [n], seed=2))
+    args.append(_arg("out", "f32", lead + [m, n], output=True))
+    return _spec(pid, code, 0, 0, f"k_{pid}", tile, args, [a["name"] for a in args[:-1]],
+                 ["out"], {}, block)
+
+
+def _dn(pid: str, code: str, m: int, n: int, k: int, ref: Callable[..., np.ndarray],
+        atol: float = 1e-3, **kw: Any) -> Callable[[], SuiteCase]:
+    return lambda: SuiteCase(dot_nest(pid, code, m, n, k, **kw), ref, 1e-3, atol, EXACT)
+
+
 def _mm(pid: str, m: int, n: int, k: int, **kw: Any) -> Callable[[], SuiteCase]:
     def make() -> SuiteCase:
         spec = matmul(m, n, k, dtype="f32", raster_group=None, **kw)
         spec.meta["id"] = pid
-        return SuiteCase(spec, lambda x0, x1: x0 @ x1, 1e-3, 1e-3, EXACT)
+        return SuiteCase(spec, lambda x0, x1: (_d(x0) @ _d(x1)).astype(np.float32), 1e-3,
+                         1e-3, EXACT)
     return make
+
+
+def m06_1024sq(m: int = 1024, n: int = 1024) -> ProblemSpec:
+    """The reference's ``m06_1024sq`` (f32 [1024, 1024] @ [1024, 1024]) in the m01 nest with
+    128 x 128 block tiles; ``m``, ``n`` smaller give the same nest over fewer tiles (a tile of C
+    depends only on its rows of A and columns of B, so a one-tile problem reproduces any tile of
+    the full one bit for bit)."""
+    spec = matmul(m, n, 1024, dtype="f32", raster_group=None, bm=128, bn=128, bk=16,
+                  block=256, b_std=1.0)
+    spec.meta["id"] = "m06_1024sq"
+    return spec
 
 
 MATMUL: dict[str, Callable[[], SuiteCase]] = {
@@ -574,6 +924,33 @@ MATMUL: dict[str, Callable[[], SuiteCase]] = {
     "m01_64sq": _mm("m01_64sq", 64, 64, 64, bm=64, bn=64, bk=16, block=256),
     "m03_tall": _mm("m03_tall", 1024, 32, 64, bm=64, bn=32, bk=16, block=128),
     "m04_deep_k": _mm("m04_deep_k", 32, 128, 1024, bm=32, bn=64, bk=32, block=128),
+    # the reference's remaining matmul ids; square and rectangular shapes that divide into
+    # block tiles take the m01 nest, the rest one thread per output element
+    "m02_matmul_rect": _mm("m02_matmul_rect", 128, 64, 256, bm=64, bn=64, bk=16, block=256,
+                           b_std=1.0),
+    "m02_odd": _dn("m02_odd", "torch.randn(96, 80) @ torch.randn(80, 48)", 96, 48, 80,
+                   lambda a, b: (_d(a) @ _d(b)).astype(np.float32)),
+    "m05_bias": _dn("m05_bias", "a @ b + c (a, b [128, 128], c [128])", 128, 128, 128,
+                    lambda a, b, c: (_d(a) @ _d(b) + _d(c)).astype(np.float32), bias=True),
+    "m07_linear_b1": _dn("m07_linear_b1", "F.linear(x [1, 64], w [32, 64])", 1, 32, 64,
+                         lambda x, w: (_d(x) @ _d(w).T).astype(np.float32), linear=True),
+    "m08_linear_b5": _dn("m08_linear_b5", "F.linear(x [5, 96], w [72, 96])", 5, 72, 96,
+                         lambda x, w: (_d(x) @ _d(w).T).astype(np.float32), linear=True),
+    "m09_matvec_wide": _dn("m09_matvec_wide", "torch.randn(1, 1024) @ torch.randn(1024, 3072)",
+                           1, 3072, 1024, lambda a, b: (_d(a) @ _d(b)).astype(np.float32)),
+    "m10_bmm": _dn("m10_bmm", "torch.bmm(torch.randn(4, 64, 32), torch.randn(4, 32, 48))",
+                   64, 48, 32, lambda a, b: (_d(a) @ _d(b)).astype(np.float32), batch=4),
+    "m11_linear_deep": _dn("m11_linear_deep", "F.linear(x [1, 4096], w [512, 4096])", 1, 512,
+                           4096, lambda x, w: (_d(x) @ _d(w).T).astype(np.float32), atol=2e-3,
+                           linear=True),
+    "m12_linear_bias": _dn("m12_linear_bias", "F.linear(x [16, 128], w [64, 128], b [64])",
+                           16, 64, 128,
+                           lambda x, w, b: (_d(x) @ _d(w).T + _d(b)).astype(np.float32),
+                           linear=True, bias=True),
+    "m13_matmul_relu": _dn("m13_matmul_relu",
+                           "torch.relu(torch.randn(128, 64) @ torch.randn(64, 128))", 128, 128,
+                           64, lambda a, b: np.maximum(_d(a) @ _d(b), 0).astype(np.float32),
+                           relu=True),
 }
 
 
@@ -695,6 +1072,8 @@ ATTENTION: dict[str, Callable[[], SuiteCase]] = {
     "a05_heads": _at("a05_heads", (4, 32, 48, 16, 16), "mul", 0.25, (32, 4, 16, 2)),
     "a06_long_kv": _at("a06_long_kv", (1, 16, 512, 64, 64), "div", 8.0, (16, 2, 64, 2)),
     "a07_tall_q": _at("a07_tall_q", (1, 256, 64, 16, 16), "div", 4.0, (64, 4, 16, 2)),
+    "a02_attention_128": _at("a02_attention_128", (1, 128, 128, 32, 32), "div", 5.656854,
+                             (32, 4, 32, 2)),
 }
 
 

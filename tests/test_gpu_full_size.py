@@ -8,9 +8,13 @@ the size.
 * Config 4: the sum of all 2^30 elements against an f64 sum of the same data (rel 1e-5).
 * Configs 5 and 5b: sampled full rows of C against the f64 product of the same bf16 operands
   (rel 1e-2 per element, floor 1e-3 of the largest |C| in those rows).
+* The reference's ``m06_1024sq`` (an f32 1024^3 matmul on the SIMT nest, whose oracle run at
+  full size takes most of a minute): a tile of C depends only on its rows of A and columns of B,
+  so three 128 x 128 tiles of the full-size GPU result are checked bit for bit against the
+  oracle's run of the one-tile problem on those rows and columns.
 
-The row-independence the first item rests on is itself checked on the CPU: the oracle's run on
-picked rows equals its run on the whole problem, row for row.
+The independence these checks rest on is itself checked on the CPU: the oracle's run on picked
+rows (or one tile) equals its run on the whole problem.
 """
 
 from __future__ import annotations
@@ -55,6 +59,15 @@ def test_oracle_rows_are_independent() -> None:
     small = problems.row_softmax(len(rows), 1024)
     got = oracle_run(small.graph, small.meta, {"x": np.ascontiguousarray(ins["x"][rows])})
     assert np.array_equal(got["softmax"], whole[rows])
+
+    from ptxgen.suite import m06_1024sq
+
+    spec = m06_1024sq(256, 256)
+    ins = reference_inputs(spec.meta)
+    whole = oracle_run(spec.graph, spec.meta, ins)["matmul"]
+    tile = oracle_run(m06_1024sq(128, 128).graph, m06_1024sq(128, 128).meta,
+                      m06_tile_inputs(ins, 1, 1))["matmul"]
+    assert np.array_equal(tile, whole[128:, 128:])
 
 
 @pytest.mark.gpu
@@ -123,3 +136,38 @@ def test_gemm_full_size_rows(cuda, key: str) -> None:
     a = bf16_bits_to_f32(ins["x0"][rows]).astype(np.float64)
     b = bf16_bits_to_f32(ins["x1"]).astype(np.float64)
     assert_gemm_close(got[rows], a @ b)
+
+
+def m06_tile_inputs(ins: dict[str, np.ndarray], r: int, c: int) -> dict[str, np.ndarray]:
+    """The operands of the one-tile problem for tile (r, c) of the 128 x 128 tiling."""
+    return {"x0": np.ascontiguousarray(ins["x0"][128 * r:128 * (r + 1)]),
+            "x1": np.ascontiguousarray(ins["x1"][:, 128 * c:128 * (c + 1)])}
+
+
+def test_m06_tile_oracle_meets_reference_formula() -> None:
+    """The reference's m06_1024sq formula (f64 product, rtol/atol 1e-3) on one tile, through
+    the oracle's run of the one-tile problem."""
+    from ptxgen.suite import m06_1024sq
+
+    ins = reference_inputs(m06_1024sq().meta)
+    small = m06_1024sq(128, 128)
+    got = oracle_run(small.graph, small.meta, m06_tile_inputs(ins, 7, 7))["matmul"]
+    want = ins["x0"][896:].astype(np.float64) @ ins["x1"][:, 896:].astype(np.float64)
+    np.testing.assert_allclose(got, want, rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.gpu
+def test_m06_1024sq_tiles(cuda) -> None:
+    """m06_1024sq at its full size on the GPU: its first and last 128 x 128 tiles equal, bit for
+    bit, the oracle's run of the one-tile problem on those rows and columns."""
+    from test_gpu_parity import check
+
+    from ptxgen.suite import m06_1024sq
+
+    spec = m06_1024sq()
+    ins = reference_inputs(spec.meta)
+    got = gpu_run(spec.graph, spec.meta, ins, guard=64)["matmul"]
+    small = m06_1024sq(128, 128)
+    for r, c in [(0, 0), (7, 7), (3, 5)]:
+        want = oracle_run(small.graph, small.meta, m06_tile_inputs(ins, r, c))["matmul"]
+        check("exact", got[128 * r:128 * (r + 1), 128 * c:128 * (c + 1)], want, "f32")
