@@ -1,12 +1,14 @@
-"""Seeded random pointwise chains through the generic lowering: a differential test of the
-compiler against the oracle on Kernel IR nobody wrote by hand.
+"""Seeded random pointwise chains and row reductions through the generic lowering: a
+differential test of the compiler against the oracle on Kernel IR nobody wrote by hand.
 
 Each seed draws a chain of 2 to 9 IEEE round-to-nearest operations (add, subtract, multiply,
 divide, maximum, minimum, abs, negative, relu, square, sqrt of an abs) over f32 or f64 inputs
 of a random shape: flat sizes from 1 to 5000 or [rows, cols] with row and column broadcasts,
 ConstantOp scalars, 1- to 8-wide unrolled bodies and blocks of 64 to 512 threads. Products
 that feed adds meet the lowering's fma rule, packed f32x2 pairs, vector loads and stores and
-tail guards wherever the shape leads them.
+tail guards wherever the shape leads them. Row reductions draw the rows, the row length (up to
+3000, mostly ragged against the block) and the block (32 to 1024 threads), and reduce by sum, max
+or sum of squares of x or |x|, then write the row's value or x divided by it plus one.
 
 On the CPU every chain compiles under each flag set and assembles for sm_100a. On the GPU the
 kernel's output equals the oracle's bit for bit (IEEE operations only, so nothing is
@@ -23,7 +25,7 @@ from test_compile import FLAG_SETS, ptxas
 from ptxgen.compiler import to_ptx
 from ptxgen.ir import Graph
 from ptxgen.problems import ProblemSpec
-from ptxgen.suite import In, Pointwise, S
+from ptxgen.suite import In, Pointwise, Rowwise, S
 
 SEEDS = list(range(32))
 BINARY = ["add", "subtract", "multiply", "divide", "maximum", "minimum"]
@@ -70,9 +72,41 @@ def random_chain(seed: int) -> ProblemSpec:
     return pw.build()
 
 
+def random_rows(seed: int) -> ProblemSpec:
+    """One block per row of x [rows, cols]: a sum, max or sum of squares (of x or |x|) through
+    the block reduction, then either the row's value or a sweep writing x normalised by it."""
+    rng = np.random.default_rng(5000 + seed)
+    block = int(rng.choice([32, 64, 128, 256, 512, 1024]))
+    rows, cols = int(rng.integers(1, 48)), int(rng.integers(1, 3000))
+    pre = [S("ax", "abs", "xv")] if rng.random() < 0.3 else []
+    val = pre[-1].name if pre else "xv"
+    kind = str(rng.choice(["add", "maximum", "sumsq"]))
+    if kind == "sumsq":
+        pre = [*pre, S("sq", "multiply", val, val)]
+        val, kind = "sq", "add"
+    passes: list[tuple] = [("reduce", "acc0", kind, pre, val)]
+    consts = {"c_one": 1.0}
+    if rng.random() < 0.5:
+        passes.append(("row", "acc0"))
+    else:
+        passes += [("scalar", S("den", "add", "acc0", "c_one")),
+                   ("write", [S("y", "divide", "xv", "den")], "y")]
+    return Rowwise(f"z{seed:02d}_random_rows", "random row reduction", In("x", "f32", (rows, cols)),
+                   ("out", "f32"), passes, consts, block).build()
+
+
 @pytest.mark.parametrize("seed", SEEDS)
 def test_random_chain_compiles_and_assembles(seed: int, tmp_path) -> None:
     spec = random_chain(seed)
+    for flags in FLAG_SETS:
+        ptx = to_ptx(Graph.from_dict(spec.graph), spec.meta, **flags)
+        assert ".target sm_100a" in ptx
+        ptxas(ptx, tmp_path)
+
+
+@pytest.mark.parametrize("seed", SEEDS[:16])
+def test_random_rows_compile_and_assemble(seed: int, tmp_path) -> None:
+    spec = random_rows(seed)
     for flags in FLAG_SETS:
         ptx = to_ptx(Graph.from_dict(spec.graph), spec.meta, **flags)
         assert ".target sm_100a" in ptx
@@ -106,3 +140,21 @@ def test_random_chain_matches_oracle(cuda, seed: int, flags: dict) -> None:
 
     dtype = next(a["dtype"] for a in spec.kernel["args"] if a["name"] == "out")
     check_flags("exact", got, run, dtype, 0, flags)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("seed", SEEDS[:16])
+@pytest.mark.parametrize("flags", FLAG_SETS, ids=["default", "no_unroll", "no_fusion", "no_cse"])
+def test_random_rows_match_oracle(cuda, seed: int, flags: dict) -> None:
+    """Single-block reductions add in one fixed order (a warp's shuffle ladder, then the
+    halving tree over warps), so the GPU equals the oracle bit for bit."""
+    from test_gpu_parity import check_flags
+
+    spec = random_rows(seed)
+    ins = reference_inputs(spec.meta)
+    got = gpu_run(spec.graph, spec.meta, ins, guard=64, **flags)["out"]
+
+    def run(nf: bool) -> np.ndarray:
+        return oracle_run(spec.graph, spec.meta, ins, no_fusion=nf)["out"]
+
+    check_flags("exact", got, run, "f32", 0, flags)
