@@ -8,7 +8,9 @@ ConstantOp scalars, 1- to 8-wide unrolled bodies and blocks of 64 to 512 threads
 that feed adds meet the lowering's fma rule, packed f32x2 pairs, vector loads and stores and
 tail guards wherever the shape leads them. Row reductions draw the rows, the row length (up to
 3000, mostly ragged against the block) and the block (32 to 1024 threads), and reduce by sum, max
-or sum of squares of x or |x|, then write the row's value or x divided by it plus one.
+or sum of squares of x or |x|, then write the row's value or x divided by it plus one. Nests
+draw matmuls with one thread per output element (random shapes, batch, ``F.linear`` layout, bias,
+relu) and sums, maxima, minima and means over the middle axis of a 3-D input.
 
 On the CPU every chain compiles under each flag set and assembles for sm_100a. On the GPU the
 kernel's output equals the oracle's bit for bit (IEEE operations only, so nothing is
@@ -25,7 +27,7 @@ from test_compile import FLAG_SETS, ptxas
 from ptxgen.compiler import to_ptx
 from ptxgen.ir import Graph
 from ptxgen.problems import ProblemSpec
-from ptxgen.suite import In, Pointwise, Rowwise, S
+from ptxgen.suite import In, Pointwise, Rowwise, S, axis_reduce, dot_nest
 
 SEEDS = list(range(32))
 BINARY = ["add", "subtract", "multiply", "divide", "maximum", "minimum"]
@@ -95,6 +97,31 @@ def random_rows(seed: int) -> ProblemSpec:
                    ("out", "f32"), passes, consts, block).build()
 
 
+def random_dot(seed: int) -> ProblemSpec:
+    """A matmul with one thread per output element (``suite.dot_nest``): random m, n, k,
+    batch, ``F.linear`` layout, bias, relu and block."""
+    rng = np.random.default_rng(9000 + seed)
+    m, n, k = (int(rng.integers(1, hi)) for hi in (70, 70, 300))
+    return dot_nest(f"z{seed:02d}_random_dot", "random matmul", m, n, k,
+                    batch=int(rng.choice([1, 1, 2, 3])), linear=bool(rng.random() < 0.4),
+                    bias=bool(rng.random() < 0.4), relu=bool(rng.random() < 0.3),
+                    block=int(rng.choice([32, 64, 128, 256])))
+
+
+def random_axis(seed: int) -> ProblemSpec:
+    """A reduction over the middle axis of x [a, b, c] (``suite.axis_reduce``): sum, max or min,
+    or a mean, over random extents."""
+    rng = np.random.default_rng(13000 + seed)
+    shape = tuple(int(rng.integers(1, hi)) for hi in (9, 200, 97))
+    fn = str(rng.choice(["add", "maximum", "minimum"]))
+    return axis_reduce(f"z{seed:02d}_random_axis", "random axis reduction", shape, fn,
+                       mean=fn == "add" and bool(rng.random() < 0.5),
+                       block=int(rng.choice([32, 64, 128, 256])))
+
+
+EXTRA = {"dot": random_dot, "axis": random_axis}
+
+
 @pytest.mark.parametrize("seed", SEEDS)
 def test_random_chain_compiles_and_assembles(seed: int, tmp_path) -> None:
     spec = random_chain(seed)
@@ -107,6 +134,16 @@ def test_random_chain_compiles_and_assembles(seed: int, tmp_path) -> None:
 @pytest.mark.parametrize("seed", SEEDS[:16])
 def test_random_rows_compile_and_assemble(seed: int, tmp_path) -> None:
     spec = random_rows(seed)
+    for flags in FLAG_SETS:
+        ptx = to_ptx(Graph.from_dict(spec.graph), spec.meta, **flags)
+        assert ".target sm_100a" in ptx
+        ptxas(ptx, tmp_path)
+
+
+@pytest.mark.parametrize("kind", sorted(EXTRA))
+@pytest.mark.parametrize("seed", SEEDS[:12])
+def test_random_nests_compile_and_assemble(kind: str, seed: int, tmp_path) -> None:
+    spec = EXTRA[kind](seed)
     for flags in FLAG_SETS:
         ptx = to_ptx(Graph.from_dict(spec.graph), spec.meta, **flags)
         assert ".target sm_100a" in ptx
@@ -151,6 +188,25 @@ def test_random_rows_match_oracle(cuda, seed: int, flags: dict) -> None:
     from test_gpu_parity import check_flags
 
     spec = random_rows(seed)
+    ins = reference_inputs(spec.meta)
+    got = gpu_run(spec.graph, spec.meta, ins, guard=64, **flags)["out"]
+
+    def run(nf: bool) -> np.ndarray:
+        return oracle_run(spec.graph, spec.meta, ins, no_fusion=nf)["out"]
+
+    check_flags("exact", got, run, "f32", 0, flags)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("kind", sorted(EXTRA))
+@pytest.mark.parametrize("seed", SEEDS[:12])
+@pytest.mark.parametrize("flags", FLAG_SETS, ids=["default", "no_unroll", "no_fusion", "no_cse"])
+def test_random_nests_match_oracle(cuda, kind: str, seed: int, flags: dict) -> None:
+    """Each output element's loop adds in index order, so the GPU equals the oracle bit for
+    bit."""
+    from test_gpu_parity import check_flags
+
+    spec = EXTRA[kind](seed)
     ins = reference_inputs(spec.meta)
     got = gpu_run(spec.graph, spec.meta, ins, guard=64, **flags)["out"]
 
