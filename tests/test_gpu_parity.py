@@ -13,7 +13,7 @@ from __future__ import annotations
 
 import numpy as np
 import pytest
-from conftest import SHIPPED, gpu_run, oracle_run, reference_inputs, shipped
+from conftest import SHIPPED, gpu_run, oracle_once, oracle_run, reference_inputs, shipped
 
 from ptxgen import problems
 
@@ -88,7 +88,7 @@ def test_shipped_parity(cuda, name: str, flags: dict) -> None:
     kind, bound = SHIPPED_BAR[name]
     for out in got:
         check_flags(kind, got[out],
-                    lambda nf, out=out: oracle_run(graph, meta, ins, no_fusion=nf)[out],
+                    lambda nf, out=out: oracle_once(name, graph, meta, ins, nf)[out],
                     "f32", bound, flags)
 
 

@@ -12,7 +12,7 @@ from __future__ import annotations
 
 import numpy as np
 import pytest
-from conftest import gpu_run, oracle_run, reference_inputs
+from conftest import gpu_run, oracle_once, reference_inputs
 from test_gpu_parity import check, check_flags
 
 from ptxgen.suite import MULTI, SUITE
@@ -30,7 +30,7 @@ def test_suite_parity(cuda, name: str, flags: dict) -> None:
     got = gpu_run(case.spec.graph, case.spec.meta, ins, guard=64, **flags)[case.out]
 
     def run(nf: bool) -> np.ndarray:
-        return oracle_run(case.spec.graph, case.spec.meta, ins, no_fusion=nf)[case.out]
+        return oracle_once(name, case.spec.graph, case.spec.meta, ins, nf)[case.out]
 
     kind, bound = case.bar
     want = run(False)
