@@ -108,7 +108,8 @@ def oracle_once(key: str, graph: dict[str, Any], meta: dict[str, Any],
                 inputs: dict[str, np.ndarray], no_fusion: bool = False) -> dict[str, np.ndarray]:
     """``oracle_run`` remembered under ``key`` for the session: a case checked under several
     compiler flag sets meets the same oracle result each time (the inputs are seeded), and the
-    attention cases take many seconds to interpret."""
+    attention cases take many seconds to interpret. ``key`` must name the IR uniquely across
+    test files (a shipped IR and a generated case can share a problem id)."""
     k = (key, no_fusion)
     if k not in _ORACLE_RUNS:
         _ORACLE_RUNS[k] = oracle_run(graph, meta, inputs, no_fusion=no_fusion)

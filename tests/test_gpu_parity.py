@@ -88,7 +88,8 @@ def test_shipped_parity(cuda, name: str, flags: dict) -> None:
     kind, bound = SHIPPED_BAR[name]
     for out in got:
         check_flags(kind, got[out],
-                    lambda nf, out=out: oracle_once(name, graph, meta, ins, nf)[out],
+                    lambda nf, out=out: oracle_once(f"shipped/{name}", graph, meta, ins,
+                                                    nf)[out],
                     "f32", bound, flags)
 
 

@@ -30,7 +30,7 @@ def test_suite_parity(cuda, name: str, flags: dict) -> None:
     got = gpu_run(case.spec.graph, case.spec.meta, ins, guard=64, **flags)[case.out]
 
     def run(nf: bool) -> np.ndarray:
-        return oracle_once(name, case.spec.graph, case.spec.meta, ins, nf)[case.out]
+        return oracle_once(f"suite/{name}", case.spec.graph, case.spec.meta, ins, nf)[case.out]
 
     kind, bound = case.bar
     want = run(False)
