@@ -1,7 +1,7 @@
 """Regenerates the golden fixtures in this directory from the reference checkout.
 
-Run in a container that has the reference at REFERENCE (default /root/reference); the fixtures
-it writes are committed, so tests never read the reference at run time.
+Run with the environment variable REFERENCE set to a checkout of the reference; the fixtures it
+writes are committed, so tests never read the reference at run time.
 
 * ``shipped/<problem>/`` -- the five distinct Kernel IR kernels the reference ships as examples
   (``examples/*/<problem>/<kernel>.ir.json`` + ``meta.json``), byte for byte: they are the
@@ -27,7 +27,7 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REFERENCE = Path(os.environ.get("REFERENCE", "/root/reference"))
+REFERENCE = Path(os.environ.get("REFERENCE", "reference"))
 SHIPPED = {
     "p02_scale_shift": "examples/op_fusion/p02_scale_shift",
     "r02_big_sum": "examples/cse/r02_big_sum",
