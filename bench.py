@@ -47,9 +47,11 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--workload", default=DEFAULT_WORKLOAD)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--no-extras", action="store_true", help="skip the other configurations")
-    p.add_argument("--scaling", choices=("weak", "strong"), default="weak",
-                   help="weak: each GPU keeps a full benchmark-sized share of an N-times larger "
-                        "problem; strong: the GPUs split the benchmark size")
+    p.add_argument("--scaling", choices=("strong", "weak"), default="strong",
+                   help="strong (default): the N GPUs split the configuration's fixed size "
+                        "(BASELINE's problem at every N); weak: each GPU keeps a full "
+                        "benchmark-sized share of an N-times larger problem (a different, larger "
+                        "configuration at N > 1)")
     p.add_argument("--share", type=int, default=1,
                    help="on one GPU, run one share of a K-way strong split of the workload (a "
                         "smaller case of the same kernel, e.g. for a profiler capture)")
@@ -128,11 +130,31 @@ def peaks() -> tuple[dict[str, float], str]:
     return {"hbm": 6650.0, "tensor": 1590.0, "tensor_sustained": 1400.0}, "fallback"
 
 
-def traffic_of(workload: str) -> float | None:
+def ptx_sha16(ptx: str) -> str:
+    import hashlib
+
+    return hashlib.sha256(ptx.encode()).hexdigest()[:16]
+
+
+def traffic_of(workload: str, ptx: str) -> tuple[float | None, dict[str, Any]]:
+    """DRAM bytes (read + write) of one launch of the workload's kernel from the committed ncu
+    summary ``profiles/traffic.json``, and where the figure comes from. Each entry names the
+    sha-256 (first 16 hex digits) of the PTX module it was captured on; if the kernel compiled
+    now differs, the figure no longer describes it and no traffic is reported."""
     f = ROOT / "profiles" / "traffic.json"
     if not f.exists():
-        return None
-    return json.loads(f.read_text()).get(workload)
+        return None, {"file": None}
+    entry = json.loads(f.read_text()).get(workload)
+    if not isinstance(entry, dict):
+        return None, {"file": "profiles/traffic.json", "entry": None}
+    now = ptx_sha16(ptx)
+    src = {"file": "profiles/traffic.json", "profile": entry.get("profile"),
+           "captured_on_ptx_sha16": entry.get("ptx_sha16"), "kernel_ptx_sha16": now,
+           "how": entry.get("how")}
+    if entry.get("ptx_sha16") != now:
+        src["stale"] = True
+        return None, src
+    return float(entry["bytes"]), src
 
 
 class ClockSampler:
@@ -230,6 +252,95 @@ def device_tensors(prob: Any, seed: int) -> dict[str, Any]:
         t.copy_(f.to(t.dtype))
         del f
     return tensors
+
+
+# --- result checks -------------------------------------------------------------------------------
+
+CHECK_ROWS = 16  # sampled rows of C per rank for the full-K GEMM (all rows for split-K)
+
+CHECK_BARS = {
+    "c1_vector_add": "bit-exact against torch x + y",
+    "c2_gelu_chain": "|y - ref| <= 2^-7 |ref| + 1e-5 against torch's f32 gelu(a*x+b, tanh) * s",
+    "c3_row_softmax": "|y - ref| <= 1e-4 |ref| + 1e-9 against torch.softmax, and every row sums "
+                      "to 1 within 1e-4",
+    "c4_full_sum": "the total within rel 1e-5 of the f64 sum of every rank's data",
+    "c5_matmul": f"{CHECK_ROWS} rows of C (first, last, seeded picks) of every rank: "
+                 "|C - ref| <= 1e-2 |ref| + 1e-4 max|ref| against the f64 product",
+    "c5b_matmul_splitk": "every row of C of every rank: |C - ref| <= 1e-2 |ref| + 1e-4 max|ref| "
+                         "against the f64 product",
+}
+
+
+def check_output(name: str, plan: Any, tensors: dict[str, Any], world: int) -> dict[str, Any]:
+    """Check one rank's result after the timed steps against a torch evaluation of the same
+    configuration on the same device data (the rank's own shard; the sum's total against the
+    f64 sum over every rank's data), and agree on the outcome across ranks: the check passes
+    only if it passes on every rank. Works on CPU tensors too (a gloo group)."""
+    import torch
+
+    args = {a["name"]: a for a in plan.spec.kernel["args"]}
+
+    def view(n: str) -> Any:
+        return tensors[n][: int(np.prod(args[n]["shape"]))].view(*args[n]["shape"])
+
+    dev = tensors[next(iter(tensors))].device
+    total = None
+    if name == "c1_vector_add":
+        ok = bool(torch.equal(view("add"), view("x") + view("y")))
+        err = 0.0 if ok else float((view("add") - (view("x") + view("y"))).abs().max())
+    elif name == "c2_gelu_chain":
+        a, b = view("mul_c1").float()[0], view("add_c1").float()[0]
+        u = view("x").float() * a + b
+        ref = torch.nn.functional.gelu(u, approximate="tanh") * view("s").float()[:, None]
+        diff = (view("mul_1").float() - ref).abs()
+        ok = bool((diff <= 2.0 ** -7 * ref.abs() + 1e-5).all())
+        err = float(diff.max())
+    elif name == "c3_row_softmax":
+        got = view("softmax")
+        ref = torch.softmax(view("x"), dim=-1)
+        diff = (got - ref).abs()
+        rows = (got.sum(dim=-1, dtype=torch.float64) - 1.0).abs()
+        ok = bool((diff <= 1e-4 * ref.abs() + 1e-9).all()) and bool((rows <= 1e-4).all())
+        err = float(diff.max())
+    elif name == "c4_full_sum":
+        part = torch.sum(view("x"), dtype=torch.float64).reshape(1)
+        if world > 1:
+            import torch.distributed as tdist
+
+            tdist.all_reduce(part)
+        total = float(part.item())
+        got = float(view("sum_1").double()[0])
+        err = abs(got - total) / max(abs(total), 1e-30)
+        ok = err <= 1e-5
+    elif name in ("c5_matmul", "c5b_matmul_splitk"):
+        a, b, c = view("x0"), view("x1"), view("matmul")
+        m = a.shape[0]
+        if name == "c5_matmul" and m > CHECK_ROWS:
+            g = torch.Generator().manual_seed(7)
+            picks = torch.randperm(m - 2, generator=g)[: CHECK_ROWS - 2] + 1
+            rows = torch.cat([torch.tensor([0, m - 1]), picks]).to(dev)
+        else:
+            rows = torch.arange(m, device=dev)
+        bd = b.double()
+        ref = a.index_select(0, rows).double() @ bd
+        del bd
+        diff = (c.index_select(0, rows).double() - ref).abs()
+        ok = bool((diff <= 1e-2 * ref.abs() + 1e-4 * ref.abs().max()).all())
+        err = float(diff.max() / ref.abs().max())
+    else:
+        raise KeyError(name)
+    flag = torch.tensor([1.0 if ok else 0.0], dtype=torch.float64, device=dev)
+    worst = torch.tensor([err], dtype=torch.float64, device=dev)
+    if world > 1:
+        import torch.distributed as tdist
+
+        tdist.all_reduce(flag, op=tdist.ReduceOp.MIN)
+        tdist.all_reduce(worst, op=tdist.ReduceOp.MAX)
+    res = {"result": "pass" if flag.item() == 1.0 else "fail", "bar": CHECK_BARS[name],
+           "max_err": float(worst.item()), "ranks": world}
+    if total is not None:
+        res["f64_total"] = total
+    return res
 
 
 # --- measurement ---------------------------------------------------------------------------------
@@ -441,6 +552,51 @@ def measure_e2e(plan: Any, prob: Any, tensors: dict[str, Any], steps: int, world
             "in_flight": len(lanes)}
 
 
+def pcie_bandwidth(nbytes: int = 256 << 20, reps: int = 3) -> dict[str, float]:
+    """Measured page-locked copy bandwidth of this GPU's host link, the bound of the e2e path:
+    host-to-device alone, device-to-host alone, and both at once on two streams (total bytes of
+    both directions over the time both take). Best of ``reps``, CUDA events, GB/s."""
+    import torch
+
+    host_in = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    host_out = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    dev_in = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    dev_out = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    up, down = torch.cuda.Stream(), torch.cuda.Stream()
+
+    def timed(h2d: bool, d2h: bool) -> float:
+        best = float("inf")
+        for _ in range(reps):
+            torch.cuda.synchronize()
+            start = torch.cuda.Event(enable_timing=True)
+            ends = []
+            start.record(up)
+            down.wait_event(start)
+            for on, go, stream in ((h2d, lambda: dev_in.copy_(host_in, non_blocking=True), up),
+                                   (d2h, lambda: host_out.copy_(dev_out, non_blocking=True),
+                                    down)):
+                if on:
+                    with torch.cuda.stream(stream):
+                        go()
+                        ev = torch.cuda.Event(enable_timing=True)
+                        ev.record(stream)
+                        ends.append(ev)
+            torch.cuda.synchronize()
+            best = min(best, max(start.elapsed_time(e) for e in ends) / 1e3)
+        return best
+
+    h2d, d2h, both = timed(True, False), timed(False, True), timed(True, True)
+    return {"h2d_gbs": nbytes / h2d / 1e9, "d2h_gbs": nbytes / d2h / 1e9,
+            "bidirectional_gbs": 2 * nbytes / both / 1e9, "bytes": nbytes}
+
+
+def e2e_floor_s(h2d_bytes: int, d2h_bytes: int, pcie: dict[str, float]) -> float:
+    """The shortest time a step's copies can take on the measured link: each direction at its
+    own rate, and both together at the measured two-way rate."""
+    return max(h2d_bytes / (pcie["h2d_gbs"] * 1e9), d2h_bytes / (pcie["d2h_gbs"] * 1e9),
+               (h2d_bytes + d2h_bytes) / (pcie["bidirectional_gbs"] * 1e9))
+
+
 # inputs the CPU path splits across threads: contiguous rows / elements of each
 _SPLIT = {"c1_vector_add": ("x", "y"), "c2_gelu_chain": ("x", "s"), "c3_row_softmax": ("x",),
           "c4_full_sum": ("x",)}
@@ -453,56 +609,110 @@ def host_threads() -> int:
         return os.cpu_count() or 1
 
 
+class CpuPath:
+    """The NumPy path of one configuration (the oracle's direct formulas of its semantics) on
+    this host's cores. The inputs are made once; ``run`` times repetitions. The elementwise and
+    reduction configurations cut their rows (elements) into one contiguous chunk per thread,
+    each evaluated by one thread (NumPy releases the GIL in its array loops); the GEMMs use the
+    BLAS's own threads.
+
+    The size is the configuration's full size whenever ``reps`` full-size repetitions are
+    estimated (from a small first sample) to fit in ``budget_s`` seconds; otherwise it is the
+    largest sample (a whole number of rows) that fits, and ``fraction`` says which share of the
+    full size that is. ``value`` figures are scaled by that fraction to the full size's work."""
+
+    def __init__(self, name: str, budget_s: float, reps: int, threads: int = 1):
+        from ptxgen import shard
+
+        self.name = name
+        split = _SPLIT.get(name)
+        self.threads = max(1, threads) if split else 1
+        self.work = shard.local_problem(name, 1).work
+        self._prepare(min(1 / 4, self.threads / 64))
+        probe = min(self.run_once() for _ in range(2))
+        want = budget_s / max(1, reps)
+        frac = 1.0 if probe / self.fraction <= want else max(self.fraction,
+                                                               want / probe * self.fraction)
+        if frac != self.fraction:
+            self._prepare(frac)
+        self.cores = host_threads() if name.startswith("c5") else self.threads
+
+    def _prepare(self, frac: float) -> None:
+        from oracle.semantics import FORMULAS
+        from ptxgen import problems
+
+        samples = {
+            "c1_vector_add": lambda f: problems.pointwise_add(
+                max(1 << 12, int((1 << 24) * f) // 256 * 256)),
+            "c2_gelu_chain": lambda f: problems.gelu_chain(max(8, int(8192 * f)), 8192),
+            "c3_row_softmax": lambda f: problems.row_softmax(max(8, int(16384 * f)), 4096),
+            "c4_full_sum": lambda f: problems.full_sum(
+                max(1 << 16, int((1 << 30) * f) // 256 * 256)),
+            "c5_matmul": lambda f: problems.matmul(max(128, int(8192 * f) // 128 * 128), 8192,
+                                                   8192),
+            "c5b_matmul_splitk": lambda f: problems.matmul(
+                max(128, int(1024 * f) // 128 * 128), 1024, 65536, split_k=4,
+                raster_group=None),
+        }
+        self.fn = FORMULAS[self.name]
+        self.parts = []  # free the previous sample's arrays first
+        spec = samples[self.name](frac)
+        ins = {a["name"]: problems.seeded_input(a) for a in spec.kernel["args"]
+               if not a.get("output")}
+        split = _SPLIT.get(self.name)
+        self.parts = [[ins]]
+        if split:
+            # each thread's contiguous share, cut again into blocks of about 2^20 elements so a
+            # block's temporaries stay in cache and are reused instead of freshly faulted in
+            first = ins[split[0]]
+            per_row = int(np.prod(first.shape[1:])) if first.ndim > 1 else 1
+            rows = first.shape[0]
+            nblocks = max(self.threads, -(-rows * per_row // (1 << 20)))
+            nblocks = min(rows, -(-nblocks // self.threads) * self.threads)
+            cut = {n: np.array_split(ins[n], nblocks) for n in split}
+            blocks = [{**ins, **{n: cut[n][i] for n in split}} for i in range(nblocks)]
+            share = nblocks // self.threads
+            self.parts = [blocks[i * share:(i + 1) * share] for i in range(self.threads)]
+        self.spec = spec
+        full = problems.CONFIGS[self.name]().kernel["args"]
+        self.elements = _elements(spec.kernel["args"])
+        self.fraction = self.elements / _elements(full)
+
+    def run_once(self) -> float:
+        """Seconds of one repetition over the whole sample."""
+        from concurrent.futures import ThreadPoolExecutor
+
+        with ThreadPoolExecutor(self.threads) as pool:
+            t0 = time.perf_counter()
+            list(pool.map(lambda part: [self.fn(b, self.spec.meta) for b in part], self.parts))
+            return time.perf_counter() - t0
+
+    def value(self, seconds: float) -> float:
+        """The metric's work per second (bytes or flops, not yet in the unit's scale) for one
+        repetition that took ``seconds``."""
+        return self.work * self.fraction / seconds
+
+    def sample(self, reps: int) -> str:
+        size = ("the full size" if self.fraction == 1.0
+                else f"{self.fraction:.4f} of the full size")
+        return (f"{self.spec.meta['id']} at {size} ({self.elements} input elements), "
+                f"{reps} repetitions"
+                + (f", split over {self.threads} threads" if self.threads > 1 else ""))
+
+
 def cpu_baseline(name: str, plan: Any, seconds: float, threads: int = 1) -> dict[str, Any]:
-    """The NumPy path of the same configuration on a bounded sample, timed on this host. With
-    ``threads`` > 1 the sample's rows (elements) are cut into that many contiguous chunks, each
-    evaluated by one thread (NumPy releases the GIL in its array loops); the GEMMs use the
-    BLAS's own threads."""
-    from concurrent.futures import ThreadPoolExecutor
-
-    from oracle.semantics import FORMULAS
-    from ptxgen import problems, shard
-
-    fn = FORMULAS[name]
-    # a sample of the workload: the same kernel shape on fewer rows / elements
-    samples = {
-        "c1_vector_add": lambda f: problems.pointwise_add(max(1 << 12, int((1 << 24) * f))),
-        "c2_gelu_chain": lambda f: problems.gelu_chain(max(8, int(8192 * f)), 8192),
-        "c3_row_softmax": lambda f: problems.row_softmax(max(8, int(16384 * f)), 4096),
-        "c4_full_sum": lambda f: problems.full_sum(max(1 << 16, int((1 << 30) * f) // 256 * 256)),
-        "c5_matmul": lambda f: problems.matmul(max(128, int(8192 * f) // 128 * 128), 8192, 8192),
-        "c5b_matmul_splitk": lambda f: problems.matmul(128, 1024, 65536, split_k=4,
-                                                        raster_group=None),
-    }
-    split = _SPLIT.get(name)
-    threads = max(1, threads) if split else 1
-    frac = min(1 / 4, threads / 64)
-    spec = samples[name](frac)
-    ins = {a["name"]: problems.seeded_input(a) for a in spec.kernel["args"]
-           if not a.get("output")}
-    parts = [ins]
-    if threads > 1:
-        cut = {n: np.array_split(ins[n], threads) for n in split}
-        parts = [{**ins, **{n: cut[n][i] for n in split}} for i in range(threads)]
-    work = shard.local_problem(name, 1).work
-    full = problems.CONFIGS[name]().kernel["args"]
-    scale = _elements(spec.kernel["args"]) / _elements(full)
-    with ThreadPoolExecutor(threads) as pool:
-        t0 = time.perf_counter()
-        reps = 0
-        while True:
-            list(pool.map(lambda part: fn(part, spec.meta), parts))
-            reps += 1
-            el = time.perf_counter() - t0
-            if el >= seconds or reps >= 1000:
-                break
+    """The NumPy path of the same configuration timed on this host for about ``seconds``
+    (``CpuPath``): the mean over repetitions, at the full size where two repetitions fit."""
+    path = CpuPath(name, seconds, 2, threads)
+    reps, el = 0, 0.0
+    while True:
+        el += path.run_once()
+        reps += 1
+        if el >= seconds or reps >= 1000:
+            break
     per_rep = el / reps
-    value = work * scale / per_rep
-    cores = host_threads() if name.startswith("c5") else threads
-    return {"value": value, "per_rep_s": per_rep, "reps": reps, "cores": cores,
-            "sample": f"{spec.meta['id']} at {scale:.4f} of the full size "
-                      f"({_elements(spec.kernel['args'])} elements), {reps} repetitions"
-                      + (f", split over {threads} threads" if threads > 1 else "")}
+    return {"value": path.value(per_rep), "per_rep_s": per_rep, "reps": reps,
+            "cores": path.cores, "fraction": path.fraction, "sample": path.sample(reps)}
 
 
 def _elements(args: list[dict[str, Any]]) -> int:
@@ -554,7 +764,10 @@ def run_ours(args: argparse.Namespace) -> None:
             plan = dataclasses.replace(plan, spec=with_exchange(plan.spec, plan.allreduce[0]))
         return plan
 
+    pcie = None
+
     def one(name: str, steps: int, warmup: int, with_e2e: bool) -> dict[str, Any]:
+        nonlocal pcie
         log(f"{name}: compile and inputs")
         plan = plan_for(name)
         unit, bound, scale = unit_of(plan)
@@ -565,18 +778,27 @@ def run_ours(args: argparse.Namespace) -> None:
                                "min_ms": m["min_ms"], "clocks": m["clocks"],
                                "launches": m["launches"]}
         peak = pk[bound]
-        traffic = traffic_of(name)
+        traffic, traffic_src = traffic_of(name, m["prob"].compile())
         res["roofline"] = {"bound": bound, "achieved": per_rank, "peak": peak,
                            "unit": unit, "frac": per_rank / peak,
-                           "traffic": traffic, "peak_source": pk_kind,
-                           "algorithmic_per_launch": plan.work}
+                           "traffic": traffic, "traffic_source": traffic_src,
+                           "peak_source": pk_kind, "algorithmic_per_launch": plan.work}
         log(f"{name}: {res['ms_per_step']:.4f} ms per step, {res['value']:.1f} {unit}")
+        res["check"] = check_output(name, plan, m["tensors"], world)
+        log(f"{name}: check {res['check']['result']} (max err {res['check']['max_err']:.3g})")
         if with_e2e:
             e = measure_e2e(plan, m["prob"], m["tensors"], max(3, min(steps, 20)), world,
                             args.e2e_lanes, m["peer"], fused=m["slots"] is not None)
-            res["e2e"] = {"value": plan.work * world / e["mean_s"] / scale, "unit": unit,
+            value = plan.work * world / e["mean_s"] / scale
+            if pcie is None:
+                pcie = pcie_bandwidth()
+            floor = e2e_floor_s(e["h2d"], e["d2h"], pcie)
+            bound_value = plan.work * world / floor / scale
+            res["e2e"] = {"value": value, "unit": unit,
                           "h2d_bytes_per_step": e["h2d"], "d2h_bytes_per_step": e["d2h"],
-                          "steps_in_flight": e["in_flight"]}
+                          "steps_in_flight": e["in_flight"],
+                          "pcie": {k: round(v, 2) for k, v in pcie.items() if k != "bytes"},
+                          "pcie_bound": bound_value, "frac_of_pcie": value / bound_value}
         if m["peer"] is not None or m["slots"] is not None:  # all ranks done before unmapping
             import torch.distributed as tdist
 
@@ -597,38 +819,67 @@ def run_ours(args: argparse.Namespace) -> None:
             try:
                 r = one(name, min(args.steps, 20), min(args.warmup, 3), with_e2e=False)
                 extras.append({k: r[k] for k in ("workload", "value", "unit", "ms_per_step",
-                                                 "roofline")})
+                                                 "roofline", "check")})
             except Exception as e:  # noqa: BLE001 - report and continue
                 extras.append({"workload": name, "error": f"{type(e).__name__}: {e}"[:300]})
     log("measurements done")
+    failed = [head["workload"]] if head["check"]["result"] != "pass" else []
+    failed += [x["workload"] for x in extras
+               if "error" in x or x.get("check", {}).get("result") != "pass"]
     if rank != 0:
+        if failed:
+            raise SystemExit(f"result check failed: {', '.join(failed)}")
         return
     plan = plan_for(args.workload)
-    cpu = (cpu_baseline(args.workload, plan, args.cpu_seconds, host_threads()) if world == 1
-           else None)
+    cpu = None
+    if world == 1:
+        cpu = cpu_baseline(args.workload, plan, args.cpu_seconds, host_threads())
     line = {
-        "metric": "Kernel time: HBM GB/s (% of ~8 TB/s), GEMM TFLOPS (% peak) at 1/2/4/8 B200",
+        "metric": METRIC,
         "value": head["value"], "unit": head["unit"], "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
         "scaling": args.scaling, "vs_baseline": None, "dtype": _dtype(args.workload),
         "data": "synthetic (seeded, the configuration's distributions, generated on the GPU)",
-        "config": {"workload": args.workload, "per_rank": plan.spec.meta["id"],
-                   "parallelism": f"tile-axis x{world}" if world > 1 else "single GPU",
-                   "share": f"1/{args.share} of the workload" if args.share > 1 else "whole",
-                   "l2": L2_MODES[args.l2],
-                   "allreduce": list(plan.allreduce),
-                   "collective": ({"fused": "inside the sum kernel: its last block exchanges "
-                                            "the partials over NVLink peer memory",
-                                   "peer": "a separate one-warp kernel over NVLink peer memory",
-                                   "nccl": "NCCL all-reduce"}[args.collective]
-                                  if plan.allreduce and world > 1 else None)},
+        "config": config_of(args.workload, world, args.scaling, args.share),
+        "setup": {"per_rank": plan.spec.meta["id"],
+                  "parallelism": f"tile-axis x{world}" if world > 1 else "single GPU",
+                  "l2": L2_MODES[args.l2],
+                  "allreduce": list(plan.allreduce),
+                  "collective": ({"fused": "inside the sum kernel: its last block exchanges "
+                                           "the partials over NVLink peer memory",
+                                  "peer": "a separate one-warp kernel over NVLink peer memory",
+                                  "nccl": "NCCL all-reduce"}[args.collective]
+                                 if plan.allreduce and world > 1 else None)},
+        "check": head["check"]["result"] if not failed else "fail",
+        "checks": {head["workload"]: head["check"],
+                   **{x["workload"]: x.get("check", {"result": "error"}) for x in extras}},
         "roofline": head["roofline"], "e2e": head["e2e"], "clocks": head["clocks"],
         "gpu_launches": head["launches"],
         "cpu_baseline": cpu and {"value": cpu["value"] / unit_of(plan)[2], "unit": head["unit"],
                                  "cores": cpu["cores"], "kind": "port", "sample": cpu["sample"]},
         "workloads": extras,
     }
-    print(json.dumps(line))
+    print(json.dumps(line), flush=True)
+    if failed:
+        raise SystemExit(f"result check failed: {', '.join(failed)}")
+
+
+METRIC = "Kernel time: HBM GB/s (% of ~8 TB/s), GEMM TFLOPS (% peak) at 1/2/4/8 B200"
+
+
+def config_of(name: str, world: int, scaling: str, share: int = 1) -> dict[str, Any]:
+    """The workload both arms report: the configuration, the whole problem's size, and how
+    many ranks share it. The reference arm prints the same dictionary for the same flags."""
+    from ptxgen import shard
+
+    size = list(shard.SIZES[name])
+    if scaling == "weak":
+        size[0] *= world
+    cfg = {"workload": name, "size": size, "scaling": scaling, "ranks": world,
+           "split": shard.SPLIT_AXIS[name]}
+    if share > 1:
+        cfg["share"] = f"1/{share} of the workload on one GPU"
+    return cfg
 
 
 def _dtype(name: str) -> str:
@@ -639,7 +890,9 @@ def _dtype(name: str) -> str:
 
 def run_reference(args: argparse.Namespace) -> None:
     """The CPU path of the same configuration (the NumPy port of its semantics, the oracle's
-    formulas), timed per step on a bounded sample on this host's cores."""
+    formulas) on this host's cores, one repetition per step: the full problem at every N (the
+    strong-scaling configuration's whole size), or a stated fraction of it when the steps would
+    not fit in a few minutes. Under torchrun rank 0 alone runs it; the others exit."""
     from ptxgen import shard
 
     rank, world, _ = dist_env()
@@ -647,22 +900,21 @@ def run_reference(args: argparse.Namespace) -> None:
         return
     plan = shard.local_problem(args.workload, 1)
     unit, _, scale = unit_of(plan)
-    per_step = max(1.0, args.cpu_seconds / max(1, args.steps + args.warmup))
-    vals = []
-    for i in range(args.warmup + args.steps):
-        r = cpu_baseline(args.workload, plan, per_step, host_threads())
-        if i >= args.warmup:
-            vals.append(r["value"])
-    value = statistics.fmean(vals) / scale
+    reps = args.steps + args.warmup
+    path = CpuPath(args.workload, max(args.cpu_seconds, 120.0), reps, host_threads())
+    times = [path.run_once() for _ in range(reps)][args.warmup:]
+    mean_s = statistics.fmean(times)
+    value = path.value(mean_s) / scale
     line = {
-        "metric": "Kernel time: HBM GB/s (% of ~8 TB/s), GEMM TFLOPS (% peak) at 1/2/4/8 B200",
+        "metric": METRIC,
         "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": r["per_rep_s"] * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": _dtype(args.workload),
+        "warmup": args.warmup, "ms_per_step": mean_s * 1e3, "higher_is_better": True,
+        "scaling": args.scaling, "vs_baseline": None, "dtype": _dtype(args.workload),
         "data": "synthetic (seeded NumPy inputs)", "impl": "reference",
-        "config": {"workload": args.workload, "parallelism": "host CPU"},
-        "cpu_baseline": {"value": value, "unit": unit, "cores": r["cores"], "kind": "port",
-                         "sample": r["sample"]},
+        "config": config_of(args.workload, world, args.scaling, args.share),
+        "setup": {"parallelism": "host CPU", "sample_fraction": path.fraction},
+        "cpu_baseline": {"value": value, "unit": unit, "cores": path.cores, "kind": "port",
+                         "sample": path.sample(len(times))},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))

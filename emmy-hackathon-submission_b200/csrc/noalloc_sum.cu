@@ -2,12 +2,13 @@
 // for callers that cannot allocate device memory.
 //
 // The two-kernel sum ptxgen emits for the grid-kernel reduce plan keeps its per-block partials
-// in an intermediate buffer that the caller allocates. Some callers cannot do that: code that
-// runs where cudaMalloc is off limits (inside a host callback or a driver-level plug-in, under
-// an allocator that owns the whole device, or in a process whose memory is reserved up front),
-// and code that must not pay an allocation's synchronisation on a latency-critical path. This
-// entry point runs the same plan with the partials in one file-scope device array instead, so
-// the caller passes only the input and the output.
+// in an intermediate buffer that the caller allocates. Some callers cannot do that: a plug-in
+// loaded into an application whose allocator owns the whole device and grants it nothing, a
+// process whose device memory is reserved up front, and code that must not pay an allocation's
+// synchronisation on a latency-critical path. This entry point runs the same plan with the
+// partials in one file-scope device array instead, so the caller passes only the input and the
+// output. It still launches kernels, so it is no use inside a stream's host function, where CUDA
+// forbids every CUDA call.
 //
 // The array holds PG_GRID_SUM_MAX_BLOCKS floats (16 KiB). It belongs to this library's device
 // module: every GPU on which the module is loaded holds it until the process exits. Every call
@@ -19,7 +20,9 @@
 // Host code cannot use the array's name as a device address (there it names a host-side stand-in
 // for the symbol). The first call on each device, with that device current, asks the runtime for
 // the array's device address (cudaGetSymbolAddress) and keeps it; that set-up may load this
-// library's module, so the first call on a device should come before any stream capture.
+// library's module, so the first call on a device should come before any stream capture. The
+// kept address belongs to the device's primary context: after cudaDeviceReset on a device the
+// module is loaded again elsewhere, and the library must not be called on that device again.
 //
 // The summation order is the emitted kernels': each thread adds its grid-stride share in index
 // order, a warp combines its lanes by the xor butterfly of strides 16..1 (v = v + other), the
@@ -42,6 +45,10 @@ namespace {
 constexpr int kBlock = PG_GRID_SUM_BLOCK;
 constexpr int kWarps = kBlock / 32;
 constexpr int kMaxDevices = 64;
+// block_sum's second stage is an xor butterfly over one warp's lanes from kWarps / 2 down: it
+// needs whole warps, at most 32 of them, a power of two
+static_assert(kBlock % 32 == 0 && kWarps >= 1 && kWarps <= 32 && (kWarps & (kWarps - 1)) == 0,
+              "PG_GRID_SUM_BLOCK must be 32 times a power of two, at most 1024");
 
 static __device__ __align__(256) float g_partials[PG_GRID_SUM_MAX_BLOCKS];
 

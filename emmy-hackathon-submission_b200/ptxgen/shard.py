@@ -11,8 +11,9 @@ contiguous share of it, with no collective on the data path:
 * full sum: the element axis splits; each rank reduces its share to one partial, and the only
   collective of the whole path, one all-reduce of those partials, combines them.
 
-The benchmark scales weakly: each rank keeps a benchmark-sized share of a problem ``world``
-times larger along the split axis (``weak=True``); strong scaling splits the benchmark size.
+By default the ranks split the configuration's fixed size (strong scaling: the same problem at
+every rank count); ``weak=True`` instead gives each rank a benchmark-sized share of a problem
+``world`` times larger along the split axis.
 
 ``local_problem`` returns the rank's Plan: its Kernel IR problem (every rank's has the same
 shape, so each rank compiles the same module), which arguments are split along their first axis
@@ -74,6 +75,14 @@ SIZES: dict[str, tuple[int, ...]] = {
     "c1_vector_add": (1 << 24,), "c2_gelu_chain": (8192, 8192), "c3_row_softmax": (16384, 4096),
     "c4_full_sum": (1 << 30,), "c5_matmul": (8192, 8192, 8192),
     "c5b_matmul_splitk": (1024, 1024, 65536),
+}
+
+
+SPLIT_AXIS: dict[str, str] = {
+    "c1_vector_add": "elements", "c2_gelu_chain": "rows", "c3_row_softmax": "rows",
+    "c4_full_sum": "elements (per-rank partials summed across ranks)",
+    "c5_matmul": "rows of A and C (B replicated)",
+    "c5b_matmul_splitk": "rows of A and C (B replicated)",
 }
 
 

@@ -338,39 +338,71 @@ class _Text:
 
 
 def bounded_wait(x: _Text, bar_addr: str, parity: str, code: int, fail: str,
-                 limit_ns: int = WAIT_NS, sem: str = "") -> None:
+                 limit_ns: int = WAIT_NS, sem: str = "", warp: bool = False) -> None:
     """An mbarrier wait that gives up: it polls ``try_wait.parity`` until the phase of
     ``parity`` completes or ``limit_ns`` of %globaltimer pass; then it sets bit ``code`` of the
     module's ``ptxgen_status`` word and branches to ``fail``. ``sem`` is the wait's memory
-    order (``.acquire.cluster`` for a barrier another CTA of the cluster arrives at)."""
+    order (``.acquire.cluster`` for a barrier another CTA of the cluster arrives at).
+
+    ``warp=False`` is for one thread (the TMA producer, the MMA issuer): it leaves the poll the
+    moment it sees the phase or runs out of time. ``warp=True`` is for a whole converged warp
+    that goes on to warp-collective ``.sync.aligned`` instructions (the epilogue's
+    ``tcgen05.ld``): every lane keeps polling until all 32 have seen the phase
+    (``vote.sync.all``) or none has time left (``vote.sync.any`` on the time check), so the
+    warp takes exactly one of the two exits, together. Polling again after seeing the phase is
+    safe because the barriers this waits on cannot complete their next phase before this warp
+    arrives on its partner barrier."""
     top, ok = x.label("wait"), x.label("waited")
     x(f"mov.u64 {x.reg('w_t0', 'u64')}, %globaltimer;")
     x(f"{top}:")
     x(f"mbarrier.try_wait.parity{sem}.shared::cta.b64 {x.reg('pw', 'pred')}, [{bar_addr}], "
       f"{parity};")
-    x(f"@%pw bra {ok};")
+    if warp:
+        x("vote.sync.all.pred %pw, %pw, -1;")
+        x(f"@%pw bra.uni {ok};")
+    else:
+        x(f"@%pw bra {ok};")
     x(f"mov.u64 {x.reg('w_t1', 'u64')}, %globaltimer;")
     x("sub.u64 %w_t1, %w_t1, %w_t0;")
     x(f"setp.lt.u64 {x.reg('pw2', 'pred')}, %w_t1, {limit_ns};")
-    x(f"@%pw2 bra {top};")
-    x(f"red.global.or.b32 [ptxgen_status], {1 << code};")
+    if warp:
+        x("vote.sync.any.pred %pw2, %pw2, -1;")
+        x(f"@%pw2 bra.uni {top};")
+        x(f"mov.u32 {x.reg('w_lane', 'u32')}, %laneid;")
+        x("setp.eq.u32 %pw, %w_lane, 0;")
+        x(f"@%pw red.global.or.b32 [ptxgen_status], {1 << code};")
+    else:
+        x(f"@%pw2 bra {top};")
+        x(f"red.global.or.b32 [ptxgen_status], {1 << code};")
     x(f"bra.uni {fail};")
     x(f"{ok}:")
 
 
-def wait_probe_ptx(limit_ns: int, code: int = 7) -> str:
-    """A one-warp kernel that waits on an mbarrier nothing ever arrives at, through
-    ``bounded_wait``: it must give up after ``limit_ns`` and set status bit ``code``. Used to
-    test the give-up path without hanging a GPU."""
+def wait_probe_ptx(limit_ns: int, code: int = 7, warp: bool = False,
+                   arrive: bool = False) -> str:
+    """A one-warp kernel that waits on an mbarrier through ``bounded_wait``, to test both of
+    its exits without hanging a GPU. Without ``arrive`` nothing ever arrives at the barrier, so
+    the wait must give up after ``limit_ns`` and set status bit ``code``; with ``arrive`` lane 0
+    arrives first, so the wait must succeed and leave the status word alone. With ``warp`` all
+    32 lanes wait in the warp-uniform form and then meet at a ``bar.warp.sync`` (which needs the
+    whole warp, as the epilogue's ``tcgen05.ld`` does); otherwise lane 0 alone waits."""
     x = _Text()
     x(f"mov.u32 {x.reg('smem', 'u32')}, probe_bar;")
     x(f"mov.u32 {x.reg('tid', 'u32')}, %tid.x;")
     x(f"setp.ne.u32 {x.reg('p', 'pred')}, %tid, 0;")
-    x("@%p bra $P_done;")
+    x("@%p bra $P_inited;")
     x("mbarrier.init.shared::cta.b64 [%smem], 1;")
     x("fence.mbarrier_init.release.cluster;")
-    bounded_wait(x, "%smem", "0", code, "$P_done", limit_ns)
+    if arrive:
+        x("mbarrier.arrive.shared::cta.b64 _, [%smem];")
+    x("$P_inited:")
+    x("bar.warp.sync -1;")
+    if not warp:
+        x("@%p bra $P_done;")
+    bounded_wait(x, "%smem", "0", code, "$P_done", limit_ns, warp=warp)
     x("$P_done:")
+    if warp:
+        x("bar.warp.sync -1;")
     x("ret;")
     decls = "\n".join(f"\t.reg .{t} %m_{n};" for n, t in x.regs.items())
     return "\n".join([
@@ -433,8 +465,9 @@ def emit(p: MatmulPlan) -> str:
     u32, u64, pred = "u32", "u64", "pred"
     r = lambda n, t=u32: x.reg(n, t)  # noqa: E731
 
-    def wait(bar_addr: str, parity: str, code: int, fail: str, sem: str = "") -> None:
-        bounded_wait(x, bar_addr, parity, code, fail, sem=sem)
+    def wait(bar_addr: str, parity: str, code: int, fail: str, sem: str = "",
+             warp: bool = False) -> None:
+        bounded_wait(x, bar_addr, parity, code, fail, sem=sem, warp=warp)
 
     def sched_lookup(skip: str) -> None:
         """Entry %t of the table into %mt, %nt, %kb0, %cnt; an empty entry branches to skip."""
@@ -697,7 +730,7 @@ def emit(p: MatmulPlan) -> str:
     sched_lookup(e_next)
     x("mad.lo.u32 %tfbar, %ab, 8, %bars;")
     x(f"add.u32 %tfbar, %tfbar, {tfull};")
-    wait("%tfbar", "%aph", 4, teardown)
+    wait("%tfbar", "%aph", 4, teardown, warp=True)  # the whole warp goes on to tcgen05.ld
     x("tcgen05.fence::after_thread_sync;")
     # this thread's row of C and the accumulator's columns in TMEM (a pair's CTA holds rows
     # rank*128 of the 256-row tile, all BN columns)

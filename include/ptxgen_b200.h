@@ -149,18 +149,21 @@ int pg_run_host(pg_kernel *kernel, uint32_t grid, uint32_t block, uint32_t smem_
  * block adds the partials. Asynchronous on `stream`; x and out are device pointers (4-byte
  * aligned), n may be 0.
  *
- * No counterpart in the reference. It is for callers that cannot allocate device memory: a host
- * function enqueued on a stream (cudaLaunchHostFunc), which CUDA forbids from making CUDA calls;
- * a plug-in loaded into an application that owns the device's allocator and grants it none; a
- * process whose device memory is all reserved up front by another allocator. ptxgen's own
- * two-kernel sum needs a caller-allocated buffer for its per-block partials. This entry point
- * keeps them in a fixed device array inside the library instead (PG_GRID_SUM_MAX_BLOCKS floats,
- * 16 KiB, held on every GPU where the library's module is loaded until the process exits) and
- * allocates nothing. blocks must be 1..PG_GRID_SUM_MAX_BLOCKS, else PG_ERR_ARGUMENT. The first
- * call on a device looks up the array's device address with that device current (it may load
- * the module): make it before any stream capture. All calls share the array, so calls that
- * overlap on the GPU (other streams, other threads) race and must not be made. Runtime failures
- * return PG_ERR_RUNTIME. */
+ * No counterpart in the reference. It is for callers that cannot allocate device memory: a
+ * plug-in loaded into an application that owns the device's allocator and grants it none; a
+ * process whose device memory is all reserved up front by another allocator; a latency-critical
+ * path that must not wait on an allocation. ptxgen's own two-kernel sum needs a caller-allocated
+ * buffer for its per-block partials. This entry point keeps them in a fixed device array inside
+ * the library instead (PG_GRID_SUM_MAX_BLOCKS floats, 16 KiB, held on every GPU where the
+ * library's module is loaded until the process exits) and allocates nothing. It does make CUDA
+ * calls itself (it launches two kernels), so it must not be called from a host function
+ * enqueued on a stream (cudaLaunchHostFunc), where CUDA forbids CUDA calls. blocks must be
+ * 1..PG_GRID_SUM_MAX_BLOCKS, else PG_ERR_ARGUMENT. The first call on a device looks up the
+ * array's device address with that device current (it may load the module) and keeps it for
+ * the process: make that first call before any stream capture, and make no call on a device
+ * after cudaDeviceReset there (the kept address belongs to the context that the reset
+ * destroyed). All calls share the array, so calls that overlap on the GPU (other streams, other
+ * threads) race and must not be made. Runtime failures return PG_ERR_RUNTIME. */
 #define PG_GRID_SUM_BLOCK 256
 #define PG_GRID_SUM_MAX_BLOCKS 4096
 int pg_grid_sum_f32_noalloc(uint64_t x, uint64_t n, uint64_t out, uint32_t blocks,

@@ -29,7 +29,9 @@ def test_reference_arm_prints_one_contract_line(workload: str | None) -> None:
     line = json.loads(lines[0])
     assert KEYS <= set(line), KEYS - set(line)
     assert line["impl"] == "reference" and line["n_gpus"] == 1 and line["value"] > 0
-    assert line["config"]["workload"] == (workload or "c2_gelu_chain")
+    import bench
+
+    assert line["config"] == bench.config_of(workload or "c2_gelu_chain", 1, "strong")
     assert line["unit"] == ("TFLOP/s" if workload else "GB/s")
     assert line["e2e"]["h2d_bytes_per_step"] == line["e2e"]["d2h_bytes_per_step"] == 0
     cpu = line["cpu_baseline"]

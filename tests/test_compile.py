@@ -206,6 +206,31 @@ def test_gemm_uses_the_tcgen05_template() -> None:
     assert "tcgen05" not in generic and "cp.async.cg.shared.global" in generic
 
 
+def test_gemm_epilogue_wait_is_warp_uniform(tmp_path) -> None:
+    """The epilogue's warps go from their accumulator wait to warp-collective ``tcgen05.ld``:
+    that wait leaves only through warp votes (all lanes saw the phase, or no lane has time
+    left) and uniform branches, so no lane reaches ``tcgen05.ld.sync.aligned`` alone. The
+    single-thread waits (producer, MMA issuer) keep their per-lane form. The probe kernels of
+    both forms assemble."""
+    import re
+
+    from ptxgen.templates.matmul import wait_probe_ptx
+
+    for spec in (problems.CONFIGS["c5_matmul"](), problems.matmul(384, 512, 512)):
+        ptx = compile_spec(spec)
+        epi = ptx[ptx.index("$M_epilogue:"):ptx.index("tcgen05.ld.sync.aligned")]
+        waits = re.findall(r"mbarrier\.try_wait[^\n]*\n\s*(\S+)[^\n]*\n\s*([^\n]*)", epi)
+        assert len(waits) == 1, waits
+        assert waits[0][0] == "vote.sync.all.pred" and "bra.uni" in waits[0][1]
+        assert "vote.sync.any.pred" in epi and "%laneid" in epi
+        assert not re.search(r"@%m_pw2 bra \$", epi)  # no per-lane retry branch
+        head = ptx[:ptx.index("$M_epilogue:")]
+        assert "vote.sync" not in head  # one-thread waits stay per lane
+    for warp in (False, True):
+        for arrive in (False, True):
+            ptxas(wait_probe_ptx(1000, warp=warp, arrive=arrive), tmp_path)
+
+
 def gemm_plan(spec: problems.ProblemSpec):
     from ptxgen.compiler import kernel_for_meta
     from ptxgen.lower import Buffer

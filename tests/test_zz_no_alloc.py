@@ -1,15 +1,18 @@
 """``pg_grid_sum_f32_noalloc``: the grid-kernel sum for callers that cannot allocate device
-memory (code run from a host callback or a plug-in without an allocator of its own, or a process
-whose device memory is reserved up front). ptxgen's two-kernel sum (the ``r17_grid_kernel``
-problem) keeps its per-block partials in a buffer the caller allocates; this entry point keeps
-them in a fixed 16 KiB device array inside the library and allocates nothing.
+memory (a plug-in without an allocator of its own, or a process whose device memory is reserved
+up front). ptxgen's two-kernel sum (the ``r17_grid_kernel`` problem) keeps its per-block partials
+in a buffer the caller allocates; this entry point keeps them in a fixed 16 KiB device array
+inside the library and allocates nothing.
 
 The GPU test calls it through the C ABI twice in a row and checks each result against the
 two-kernel sum launched through the existing entry points (``pg_module_load`` /
-``pg_kernel_launch`` via ``ProblemSet``) on the same input, within rel 1e-5, the bar of the
-problem's own formula. The second call uses fewer blocks on other data, so partials the first
-call left in the shared array must not leak into it. The argument checks run before any CUDA
-call, so they are tested on the CPU.
+``pg_kernel_launch`` via ``ProblemSet``) on the same input. The two add in the same order (each
+thread's grid-stride share in index order, the warp butterfly of strides 16..1, the halving tree
+over the block's warp slots, then the same over the partials), so the results must be equal bit
+for bit; each must also be within rel 1e-5 of the f64 sum of the data, the bar of the problem's
+own formula. The second call uses fewer blocks on other data, so partials the first call left in
+the shared array must not leak into it. The argument checks run before any CUDA call, so they
+are tested on the CPU.
 
 This file is named to be collected last: it passes alone in a fresh process and after every
 other test."""
@@ -67,6 +70,8 @@ def test_noalloc_sum_matches_the_two_kernel_sum(cuda) -> None:
         assert rc == 0, lib.pg_last_error().decode(errors="replace")
         torch.cuda.synchronize()
         got = float(out.cpu()[0])
-        assert abs(got - want) <= RTOL * abs(want), (call, got, want)
-        results.append((got, want, float(x.astype(np.float64).sum())))
+        exact = float(x.astype(np.float64).sum())
+        assert got == want, (call, got, want)  # same summation order, same bits
+        assert abs(got - exact) <= RTOL * abs(exact), (call, got, exact)
+        results.append((got, want, exact))
     print("noalloc sum (got, two-kernel, f64):", results)
