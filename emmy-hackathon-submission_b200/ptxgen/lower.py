@@ -113,113 +113,130 @@ class Lowering:
 
     # --- walking ----------------------------------------------------------------------
     def run(self) -> Kernel:
+        """The whole kernel: parameter pointers, thread registers, shared buffers, then the
+        body's statements in order."""
+        self._bind_parameters()
         k = self.k
-        for name in k.params:
-            if name not in self.buffers:
-                raise ValueError(f"parameter {name!r} has no buffer")
-            raw = k.reg("u64")
-            k.emit("ld.param.u64", (raw,), (f"[{k.name}_param_{name}]",))
-            buf = self.buffers[name]
-            ptr = k.pure("cvta.to.global.u64", "u64", raw)
-            k.align[ptr] = BUFFER_ALIGN
-            self.mem[name] = GlobalBuf(tuple(buf.shape), buf.dtype, ptr, buf.is_output)
         self.tid = k.pure("mov.u32", "u32", "%tid.x", rng=(0, self.block - 1))
         self.ctaid = k.pure("mov.u32", "u32", "%ctaid.x")
-        if any(isinstance(st, WarpShuffle | TreeHalve) for st in self._stmts) or any(
-                isinstance(e, Var) and e.name in ("lane", "warp") for e in self._all_exprs()):
-            lane = k.pure("and.b32", "u32", self.tid, "31", rng=(0, min(31, self.block - 1)))
-            warp = k.pure("shr.u32", "u32", self.tid, "5", rng=(0, (self.block - 1) >> 5))
-            self.env |= {"lane": Aff.of(lane), "warp": Aff.of(warp)}
-        self.mem |= self._declare_shared(list(self.op.smem_buffers.values()))
+        if self._uses_lanes():
+            last = self.block - 1
+            lane = k.pure("and.b32", "u32", self.tid, "31", rng=(0, min(31, last)))
+            warp = k.pure("shr.u32", "u32", self.tid, "5", rng=(0, last >> 5))
+            self.env["lane"], self.env["warp"] = Aff.of(lane), Aff.of(warp)
+        self.mem.update(self._declare_shared(list(self.op.smem_buffers.values())))
         self.body([self.op.body])
         return k
 
-    def _all_exprs(self) -> Iterator[Expr]:
-        def sub(e: object) -> Iterator[Expr]:
-            if isinstance(e, Expr):
-                yield e
-                for f in getattr(e, "__dataclass_fields__", {}):
-                    yield from sub(getattr(e, f))
-            elif isinstance(e, tuple):
-                for x in e:
-                    yield from sub(x)
+    def _bind_parameters(self) -> None:
+        """Each parameter's global pointer, in ``arg_order`` (the entry's .param list)."""
+        k = self.k
+        missing = [name for name in k.params if name not in self.buffers]
+        if missing:
+            raise ValueError(f"parameter {missing[0]!r} has no buffer")
+        for name in k.params:
+            buf = self.buffers[name]
+            param = k.reg("u64")
+            k.emit("ld.param.u64", (param,), (f"[{k.name}_param_{name}]",))
+            ptr = k.pure("cvta.to.global.u64", "u64", param)
+            k.align[ptr] = BUFFER_ALIGN
+            self.mem[name] = GlobalBuf(tuple(buf.shape), buf.dtype, ptr, buf.is_output)
 
-        for st in self._stmts:
-            for f in getattr(st, "__dataclass_fields__", {}):
-                if f not in ("body", "else_body"):
-                    yield from sub(getattr(st, f))
+    def _uses_lanes(self) -> bool:
+        """Whether the body needs the lane and warp registers: it reduces across lanes, or an
+        expression names ``lane`` or ``warp``."""
+        if any(isinstance(st, WarpShuffle | TreeHalve) for st in self._stmts):
+            return True
+        return any(isinstance(e, Var) and e.name in ("lane", "warp")
+                   for st in self._stmts for e in _expressions_of(st))
 
     def body(self, stmts: Sequence[Stmt]) -> None:
         for st in stmts:
-            fn = getattr(self, f"emit_{type(st).__name__}", None)
-            if fn is None:
+            method = _HANDLERS.get(type(st))
+            if method is None:
                 raise NotImplementedError(f"no PTX lowering for Kernel IR node {type(st).__name__}")
-            fn(st)
+            getattr(self, method)(st)
 
     @contextmanager
     def _block(self) -> Iterator[None]:
-        """Names first bound inside end with it (rebinding an outer name persists)."""
-        before = set(self.env)
-        yield
-        for name in set(self.env) - before:
-            del self.env[name]
+        """A lexical scope: a name first bound inside it is unbound when it ends, while a new
+        value given to a name bound outside it stays."""
+        outer = frozenset(self.env)
+        try:
+            yield
+        finally:
+            for name in [n for n in self.env if n not in outer]:
+                self.env.pop(name)
 
     def _where(self, p: str | bool) -> AbstractContextManager[None]:
         """A block that runs only where predicate ``p`` holds (always when ``p`` is True)."""
-        return nullcontext() if p is True else self.k.skip_if(f"!{p}")
+        if p is True:
+            return nullcontext()
+        return self.k.skip_if(f"!{p}")
 
     # --- names ------------------------------------------------------------------------
+    # ``env`` maps each Kernel IR name to its value. A *variable* is a register that is written
+    # in place (an accumulator, a loop-carried state, a reduction's state); every other data
+    # register is written once. A name bound to data never shares a variable's register, or it
+    # would see the variable's later writes.
+
     def _lookup(self, name: str) -> Value:
-        if name not in self.env:
-            raise KeyError(f"{name!r} is used before it is defined")
-        return self.env[name]
+        try:
+            return self.env[name]
+        except KeyError:
+            raise KeyError(f"{name!r} is used before it is defined") from None
 
     def _data(self, name: str) -> Val:
         return self._as_val(self._lookup(name))
 
+    def _snapshot(self, v: Val) -> Val:
+        """A write-once copy of a variable's current value."""
+        typ = reg_type(v.dtype)
+        copy = self.k.reg(typ)
+        self.k.emit(f"mov.{move_type(typ)}", (copy,), (v.reg,))
+        return Val(copy, v.dtype)
+
     def _define(self, name: str, v: Val) -> None:
-        """Bind ``name`` to ``v``; a name never aliases a variable, so one is copied first."""
-        if v.reg in self.k.variables:
-            typ = reg_type(v.dtype)
-            copy = self.k.reg(typ)
-            self.k.emit(f"mov.{move_type(typ)}", (copy,), (v.reg,))
-            v = Val(copy, v.dtype)
-        self.env[name] = v
+        """Bind ``name`` to ``v`` (a snapshot, when ``v`` is a variable)."""
+        self.env[name] = self._snapshot(v) if v.reg in self.k.variables else v
 
     def _init(self, name: str, identity: float | None, dtype: str) -> None:
+        """Bind ``name`` to a new variable of ``dtype`` that starts at ``identity``."""
         if identity is None:
             raise ValueError(f"{name!r} has no identity to start from")
         typ = reg_type(dtype)
         self.env[name] = Val(self.k.variable(typ, literal(identity, typ)), dtype)
 
     def _variable(self, name: str, dtype: str | None = None) -> Val:
-        """Make ``name``'s value a variable (of ``dtype``) so it can be written in place."""
-        v = self._data(name)
-        if dtype is not None and v.dtype != dtype:
-            v = ops.convert(self.k, v, dtype)
-        if v.reg not in self.k.variables:
-            v = Val(self.k.variable(reg_type(v.dtype), v.reg), v.dtype)
-            self.env[name] = v
-        return v
+        """``name``'s value as a variable (of ``dtype``, when given) that can be written in
+        place; a write-once value is moved into a new variable, which ``name`` then names."""
+        current = self._data(name)
+        if dtype is not None and dtype != current.dtype:
+            current = ops.convert(self.k, current, dtype)
+        if current.reg in self.k.variables:
+            return current
+        var = Val(self.k.variable(reg_type(current.dtype), current.reg), current.dtype)
+        self.env[name] = var
+        return var
 
     def _write(self, name: str, v: Val) -> None:
-        """Write ``v`` into variable ``name`` in place."""
+        """Write ``v`` into variable ``name`` in place (converted to the variable's dtype)."""
         var = self._variable(name)
-        src = ops.convert(self.k, v, var.dtype).reg
-        if src != var.reg:
-            self.k.emit(f"mov.{move_type(reg_type(var.dtype))}", (var.reg,), (src,))
-            self.k.forget(var.reg)
+        self._move_into(var, ops.convert(self.k, v, var.dtype).reg)
+
+    def _move_into(self, var: Val, src: str) -> None:
+        if src == var.reg:
+            return
+        self.k.emit(f"mov.{move_type(reg_type(var.dtype))}", (var.reg,), (src,))
+        self.k.forget(var.reg)  # results computed from its old value are stale now
 
     # --- launch -----------------------------------------------------------------------
     def emit_Tile(self, t: Tile) -> None:
-        if not t.is_static_grid or t.aux_threads:
-            raise NotImplementedError("Tile: only static grids without an aux thread band")
-        n, k = t.n_elements, self.k
-        if n > 2**31 - 1:
-            raise NotImplementedError("Tile: more than 2^31 - 1 cells")
-        if t.block_threads is not None and t.block_threads != self.block:
-            raise ValueError(f"Tile block_threads {t.block_threads} != launch block {self.block}")
-        blocks = -(-n // self.block)
+        """The grid: one thread per Tile cell, cell ``ctaid * block + tid``; the axes decoded
+        from it; the tail guard only when the last block is partial."""
+        k = self.k
+        cells = self._check_grid(t)
+        blocks = -(-cells // self.block)
         k.ranges[self.ctaid] = (0, blocks - 1)
         k.header_notes.append(f"// @ptxgen launch grid={blocks} block={self.block}")
         if blocks <= SM_COUNT:
@@ -227,14 +244,15 @@ class Lowering:
             # on one. Left to its occupancy heuristic, a long unrolled block can come out at 32
             # registers and kilobytes of spills.
             k.min_ctas = 1
-        gid = Aff.of(self.ctaid) * self.block + Aff.of(self.tid)
-        past = index.compare(k, ">=", gid, Aff.k(n))
-        if past is True:
+        cell = Aff.combine((Aff.of(self.ctaid), self.block), (Aff.of(self.tid), 1))
+        beyond = index.compare(k, ">=", cell, Aff.k(cells))
+        if beyond is True:
             return
-        if past is not False and any(isinstance(st, BARRIERS) for st in walk(t.body)):
+        guarded = beyond is not False
+        if guarded and any(isinstance(st, BARRIERS) for st in walk(t.body)):
             raise NotImplementedError("Tile: a partial last block around a barrier")
-        with k.skip_if(past) if past else nullcontext(), self._block():
-            self.env |= self._decode(t, gid, self._raster(t))
+        with (k.skip_if(beyond) if guarded else nullcontext()), self._block():
+            self.env.update(self._decode(t, cell, _raster_pair(t)))
             self.body(t.body)
         if self.exchange is not None:  # every thread reaches it, past the tail guard
             from .templates.exchange import emit_epilogue
@@ -243,63 +261,73 @@ class Lowering:
             k.emit("bar.sync", src=("0",), barrier=True)
             emit_epilogue(k, self.tid, self.mem[self.exchange].ptr)
 
+    def _check_grid(self, t: Tile) -> int:
+        """The Tile's cell count, after the checks this lowering needs of its grid."""
+        if not t.is_static_grid or t.aux_threads:
+            raise NotImplementedError("Tile: only static grids without an aux thread band")
+        if t.n_elements > 2**31 - 1:
+            raise NotImplementedError("Tile: more than 2^31 - 1 cells")
+        if t.block_threads is not None and t.block_threads != self.block:
+            raise ValueError(f"Tile block_threads {t.block_threads} != launch block {self.block}")
+        return t.n_elements
+
     def emit_Sync(self, s: Sync) -> None:
         if s.warp:
             if s.barrier_id:
                 raise ValueError("Sync(warp=True) cannot carry a named barrier_id")
             self.k.emit("bar.warp.sync", src=("-1",), barrier=True)
-        elif s.barrier_id == 0 and s.count is None:
-            self.k.emit("bar.sync", src=("0",), barrier=True)
-        elif s.count is None:
-            raise ValueError(f"Sync(barrier_id={s.barrier_id}) requires count")
+            return
+        if s.count is None:
+            if s.barrier_id:
+                raise ValueError(f"Sync(barrier_id={s.barrier_id}) requires count")
+            operands: tuple[str, ...] = ("0",)
         else:
-            self.k.emit("bar.sync", src=(str(s.barrier_id), str(s.count)), barrier=True)
+            operands = (str(s.barrier_id), str(s.count))
+        self.k.emit("bar.sync", src=operands, barrier=True)
 
-    @staticmethod
-    def _raster(t: Tile) -> tuple[int, int, int] | None:
-        """(grouped axis, other axis, group) when the Tile orders its block axes in groups."""
-        names = [a.name for a in t.axes]
-        if not (t.raster_group and t.raster_axes and all(n in names for n in t.raster_axes)):
-            return None
-        mi, ni = (names.index(n) for n in t.raster_axes)
-        if ni != mi + 1:
-            return None
-        gi, oi = (mi, ni) if t.raster_orient == "m" else (ni, mi)
-        g = min(t.raster_group, t.extents[gi])
-        return (gi, oi, g) if t.extents[gi] > 1 and g > 1 else None
-
-    def _decode(self, t: Tile, gid: Aff, raster: tuple[int, int, int] | None) -> dict[str, Aff]:
-        """Each axis from the global id, row-major (the outermost axis takes no %). A raster
-        pair, grouped axis a (extent Ea, group G) beside axis b (Eb), is decoded in grouped
-        order: a = grp*G + (s % (G*Eb)) % gsz and b = (s % (G*Eb)) / gsz, where gsz is G except
-        in a ragged last group (Ea - grp*G)."""
+    def _decode(self, t: Tile, cell: Aff, raster: tuple[int, int, int] | None
+                ) -> dict[str, Aff]:
+        """Each Tile axis as an index of the cell number, in Emmy's block order: row-major
+        (axis i is ``cell / stride_i % extent_i``; the outermost axis needs no ``%``), except a
+        raster pair, which ``_grouped`` decodes."""
         k = self.k
-        extents = list(t.extents)
+        extents = [int(e) for e in t.extents]
         strides = [math.prod(extents[i + 1:]) for i in range(len(extents))]
-        axes: dict[str, Aff] = {}
-        for i, (axis, e) in enumerate(zip(t.axes, extents, strict=True)):
-            if raster is not None and i in raster[:2]:
+        paired = set(raster[:2]) if raster is not None else set()
+        out: dict[str, Aff] = {}
+        for i, axis in enumerate(t.axes):
+            if i in paired:
                 continue
-            v = Aff() if e == 1 else index.div(k, gid, strides[i])
-            axes[axis.name] = index.mod(k, v, e) if i and e > 1 else v
-        if raster is None:
-            return axes
-        gi, oi, g = raster
-        ea, eb = extents[gi], extents[oi]
-        sub = index.div(k, gid, strides[max(gi, oi)])
-        if min(gi, oi):
-            sub = index.mod(k, sub, ea * eb)
+            if extents[i] == 1:
+                out[axis.name] = Aff()
+                continue
+            value = index.div(k, cell, strides[i])
+            out[axis.name] = value if i == 0 else index.mod(k, value, extents[i])
+        if raster is not None:
+            grouped, other, group = raster
+            inner = max(grouped, other)
+            pair_cell = index.div(k, cell, strides[inner])
+            if min(grouped, other) > 0:  # axes outside the pair: keep the pair's own part
+                pair_cell = index.mod(k, pair_cell, extents[grouped] * extents[other])
+            a, b = self._grouped(pair_cell, extents[grouped], extents[other], group)
+            out[t.axes[grouped].name], out[t.axes[other].name] = a, b
+        return out
+
+    def _grouped(self, c: Aff, ea: int, eb: int, g: int) -> tuple[Aff, Aff]:
+        """The grouped decode of a raster pair's cell ``c``: the grouped axis (extent ``ea``)
+        advances in groups of ``g``; within a group the cells run down the group first, then
+        across the other axis (extent ``eb``). A ragged last group is ``ea mod g`` wide."""
+        k = self.k
         if eb == 1:
-            a, b = sub, Aff()
-        else:
-            grp, r = index.div(k, sub, g * eb), index.mod(k, sub, g * eb)
-            gsz: Aff = Aff.k(g)
-            if ea % g:
-                gsz = index.minimum(k, Aff.k(ea) - grp * g, gsz)
-            a = grp * g + index.mod(k, r, gsz)
-            b = index.div(k, r, gsz)
-        axes[t.axes[gi].name], axes[t.axes[oi].name] = a, b
-        return axes
+            return c, Aff()
+        span = g * eb  # cells of one whole group
+        group_no = index.div(k, c, span)
+        within = index.mod(k, c, span)
+        width: Aff = Aff.k(g)
+        if ea % g:
+            width = index.minimum(k, Aff.k(ea) - group_no * g, width)
+        a = group_no * g + index.mod(k, within, width)
+        return a, index.div(k, within, width)
 
     # --- memory -----------------------------------------------------------------------
     def emit_Smem(self, s: Smem) -> None:
@@ -359,51 +387,60 @@ class Lowering:
             r = ops.convert(self.k, v, mem.dtype).reg
             self.k.mem("st", space, typ, addr, off + j * esz, (r,))
 
+    def _element(self, name: str, exprs: Sequence[Expr]) -> tuple[Memory, Aff]:
+        """Buffer ``name`` and the flat element offset its index expressions select."""
+        mem = self.mem[name]
+        return mem, _row_major(name, mem.shape, [self._int(e) for e in exprs])
+
     def emit_Load(self, s: Load) -> None:
-        mem = self.mem[s.input]
-        dtype = s.dtype.name if s.dtype is not None else mem.dtype
-        flat = self._flat(s.input, mem.shape, [self._int(e) for e in s.index])
-        vals = self._load(mem, flat, dtype, len(s.names))
-        for name, v in zip(s.names, vals, strict=True):
-            self.env[name] = v
+        mem, flat = self._element(s.input, s.index)
+        dtype = mem.dtype if s.dtype is None else s.dtype.name
+        values = self._load(mem, flat, dtype, len(s.names))
+        self.env.update(zip(s.names, values, strict=True))
 
     def emit_Write(self, s: Write) -> None:
         if s.swizzle != "NONE":
             raise NotImplementedError(f"Write: swizzle {s.swizzle}")
-        k, mem = self.k, self.mem[s.output]
-        flat = self._flat(s.output, mem.shape, [self._int(e) for e in s.index])
+        mem, flat = self._element(s.output, s.index)
         values = [self._data(v) for v in s.values]
-        if not s.atomic:
+        if s.atomic:
+            self._add_into(mem, flat, values)
+        else:
             self._store(mem, flat, values)
-            return
+
+    def _add_into(self, mem: Memory, flat: Aff, values: Sequence[Val]) -> None:
+        """``red.global.add`` of each value into consecutive elements from ``flat`` (the
+        split-K finalize: blocks add their partials into a zeroed output)."""
         if isinstance(mem, SharedBuf):
             raise NotImplementedError("Write: atomic to shared memory")
-        forms = {"f32": "f32", "f64": "f64", "f16": "noftz.f16", "bf16": "noftz.bf16",
-                 "i32": "s32", "u32": "u32", "u64": "u64", "i64": "u64"}
-        if mem.dtype not in forms:
+        form = _RED_ADD.get(mem.dtype)
+        if form is None:
             raise NotImplementedError(f"Write: atomic add of {mem.dtype}")
-        addr, off, space = self._address(mem, flat, mem.dtype)
-        esz = size(mem_type(mem.dtype))
+        k = self.k
+        addr, off, _ = self._address(mem, flat, mem.dtype)
+        step = size(mem_type(mem.dtype))
         for j, v in enumerate(values):
-            r = ops.convert(k, v, mem.dtype).reg
-            k.mem("red", "global", forms[mem.dtype], addr, off + j * esz, (r,))
+            k.mem("red", "global", form, addr, off + j * step,
+                  (ops.convert(k, v, mem.dtype).reg,))
 
     def emit_CpAsyncCopy(self, s: CpAsyncCopy) -> None:
+        """One asynchronous copy of ``nbytes`` (4, 8 or 16) from global to shared memory; a
+        ``lane_index`` offsets the shared destination per lane. 16-byte copies bypass L1."""
         if s.swizzle != "NONE":
             raise NotImplementedError(f"CpAsyncCopy: swizzle {s.swizzle}")
         if s.nbytes not in (4, 8, 16):
             raise ValueError(f"CpAsyncCopy: nbytes {s.nbytes} is not 4, 8 or 16")
-        k, dst, src = self.k, self.mem[s.smem], self.mem[s.src]
-        idx: tuple[Expr, ...] = s.smem_index
+        dst_index: tuple[Expr, ...] = tuple(s.smem_index)
         if s.lane_index is not None:
-            idx = tuple(BinaryExpr("+", b, ln) for b, ln in zip(idx, s.lane_index, strict=True))
-        flat = self._flat(s.smem, dst.shape, [self._int(e) for e in idx])
-        d_addr, d_off, _ = self._address(dst, flat, dst.dtype)
-        flat = self._flat(s.src, src.shape, [self._int(e) for e in s.src_index])
-        s_addr, s_off, _ = self._address(src, flat, src.dtype)
-        cache = "cg" if s.nbytes == 16 else "ca"
-        k.raw(f"cp.async.{cache}.shared.global [{d_addr}+{d_off}], [{s_addr}+{s_off}], "
-              f"{s.nbytes};")
+            dst_index = tuple(BinaryExpr("+", at, lane)
+                              for at, lane in zip(dst_index, s.lane_index, strict=True))
+        operands = []
+        for name, exprs in ((s.smem, dst_index), (s.src, s.src_index)):
+            mem, flat = self._element(name, exprs)
+            addr, off, _ = self._address(mem, flat, mem.dtype)
+            operands.append(f"[{addr}+{off}]")
+        level = "cg" if s.nbytes == 16 else "ca"
+        self.k.raw(f"cp.async.{level}.shared.global {operands[0]}, {operands[1]}, {s.nbytes};")
 
     def emit_CpAsyncCommit(self, _s: CpAsyncCommit) -> None:
         self.k.raw("cp.async.commit_group;")
@@ -412,83 +449,101 @@ class Lowering:
         self.k.raw(f"cp.async.wait_group {s.group};")
 
     def _declare_shared(self, decls: list[Smem]) -> dict[str, SharedBuf]:
-        """Static ``.shared`` arrays, or offsets into one dynamic pool past the static cap."""
+        """Every Smem buffer of the kernel, declared once up front in declaration order: each a
+        static ``.shared`` array, or, when together they pass ``STATIC_SMEM_CAP``, an offset
+        into one dynamic pool the launcher sizes (``// @ptxgen dynamic_smem=``)."""
         k = self.k
         offsets, total = pack_shared(decls)
-        pool = total > STATIC_SMEM_CAP
-        out: dict[str, SharedBuf] = {}
-        if pool:
-            align = max(16, *(int(s.align or 0) for s in decls))
-            k.module_decls.append(f".extern .shared .align {align} .b8 smem_pool[];\n")
+        pooled = total > STATIC_SMEM_CAP
+        if pooled:
+            pool_align = max([16, *(int(d.align or 0) for d in decls)])
+            k.module_decls.append(f".extern .shared .align {pool_align} .b8 smem_pool[];\n")
             k.header_notes.append(f"// @ptxgen dynamic_smem={total}")
-        for s in decls:
-            dtype = smem_dtype(s.dtype)
-            if dtype not in ("f32", "f64", "f16", "bf16", "i32", "u32", "i64", "u64"):
-                raise NotImplementedError(f"Smem: dtype {s.dtype}")
-            if s.name in self.buffers:
-                raise ValueError(f"Smem {s.name!r}: name already declared")
-            shape, esz = tuple(int(e) for e in s.extents), size(mem_type(dtype))
-            align = max(16, int(s.align or 0), esz)
-            if pool:
-                base = k.pure("mov.u32", "u32", "smem_pool", mult=16)
-                out[s.name] = SharedBuf(shape, dtype, base, offsets[s.name], 16)
-                continue
-            sym = f"smem_{s.name}"
-            k.shared_decls.append(f"\t.shared .align {align} .b8 {sym}[{math.prod(shape) * esz}];")
-            out[s.name] = SharedBuf(shape, dtype, k.pure("mov.u32", "u32", sym), 0, align)
-            k.align[out[s.name].base] = align
+        out: dict[str, SharedBuf] = {}
+        for d in decls:
+            out[d.name] = self._shared_buffer(d, offsets[d.name] if pooled else None)
         return out
 
-    @staticmethod
-    def _flat(buf: str, shape: tuple[int, ...], parts: list[Aff]) -> Aff:
-        """Row-major element offset of ``buf[parts]``; a single index is already flat."""
-        if len(parts) <= 1:
-            return parts[0] if parts else Aff()
-        if len(parts) != len(shape):
-            raise NotImplementedError(f"{buf}: {len(parts)}-d index into a {len(shape)}-d buffer")
-        flat, stride = Aff(), 1
-        for i, extent in zip(reversed(parts), reversed(shape), strict=True):
-            flat, stride = flat + i * stride, stride * extent
-        return flat
+    def _shared_buffer(self, d: Smem, pool_offset: int | None) -> SharedBuf:
+        dtype = smem_dtype(d.dtype)
+        if dtype not in _SHARED_DTYPES:
+            raise NotImplementedError(f"Smem: dtype {d.dtype}")
+        if d.name in self.buffers:
+            raise ValueError(f"Smem {d.name!r}: name already declared")
+        k = self.k
+        shape = tuple(int(e) for e in d.extents)
+        esz = size(mem_type(dtype))
+        if pool_offset is not None:
+            base = k.pure("mov.u32", "u32", "smem_pool", mult=16)
+            return SharedBuf(shape, dtype, base, pool_offset, 16)
+        align = max(16, int(d.align or 0), esz)
+        symbol = f"smem_{d.name}"
+        k.shared_decls.append(
+            f"\t.shared .align {align} .b8 {symbol}[{math.prod(shape) * esz}];")
+        base = k.pure("mov.u32", "u32", symbol)
+        k.align[base] = align
+        return SharedBuf(shape, dtype, base, 0, align)
 
     # --- data -------------------------------------------------------------------------
     def emit_Assign(self, s: Assign) -> None:
-        dtype = s.dtype.name if s.dtype is not None else None
-        self._define(s.name, ops.assign(self.k, s.op.name, dtype, [self._data(a) for a in s.args]))
+        args = [self._data(a) for a in s.args]
+        dtype = None if s.dtype is None else s.dtype.name
+        self._define(s.name, ops.assign(self.k, s.op.name, dtype, args))
 
     def emit_Let(self, s: Let) -> None:
-        v = self.expr(s.value) if s.dtype is None else self._value(s.value, s.dtype.name)
-        if isinstance(v, Val):
-            self._define(s.name, v)
+        """An untyped Let binds whatever its expression is (an index stays an index); a typed
+        one binds data of its dtype."""
+        if s.dtype is None:
+            value = self.expr(s.value)
         else:
-            self.env[s.name] = v
+            value = self._value(s.value, s.dtype.name)
+        if isinstance(value, Val):
+            self._define(s.name, value)
+        else:
+            self.env[s.name] = value
 
     def emit_Init(self, s: Init) -> None:
         self._init(s.name, s.identity, s.dtype.name)
 
     def emit_Select(self, s: Select) -> None:
-        self._define(s.name, self._value(TernaryExpr(s.cond, s.if_true, s.if_false), "f32"))
+        choice = TernaryExpr(s.cond, s.if_true, s.if_false)
+        self._define(s.name, self._value(choice, "f32"))
 
     def emit_Accum(self, s: Accum) -> None:
-        k, name = self.k, ops.canonical(s.op.name)
-        dtype = s.dtype.name if s.dtype is not None else "f32"
-        if name not in ops.ACCUM:
+        """``acc = base op value`` in place (``base`` is the accumulator itself unless the
+        statement names one, as an online-softmax rescale does)."""
+        op = ops.canonical(s.op.name)
+        dtype = "f32" if s.dtype is None else s.dtype.name
+        if op not in ops.ACCUM:
             raise NotImplementedError(f"Accum: op {s.op.name} is not a binary op")
         if s.name not in self.env:  # no seeding loop: start from the identity here
             self._init(s.name, s.op.identity, dtype)
+        k = self.k
         acc = self._variable(s.name, dtype).reg
         value = ops.convert(k, self._data(s.value), dtype).reg
-        base = acc if s.base is None else ops.convert(k, self._data(s.base), dtype).reg
-        typ = reg_type(dtype)
-        if name == "add" and (fma := ops.fma_operands(k, typ, value, base)) is not None:
-            k.emit(f"fma.rn.{typ}", (acc,), fma)
-        elif typ == "bf16" or (typ == "f16" and name == "divide"):  # no native form: in f32
-            f32 = [Val(ops.cvt(k, r, typ, "f32"), "f32") for r in (base, value)]
-            k.emit(f"cvt.rn.{typ}.f32", (acc,), (ops.apply(k, name, f32, "f32").reg,))
-        else:
-            m = ops.ACCUM[name][0 if typ in ("f32", "f64", "f16") else 1]
-            k.emit(f"{ops.arith(k, m)}.{typ}", (acc,), (base, value))
+        base = acc
+        if s.base is not None:
+            base = ops.convert(k, self._data(s.base), dtype).reg
+        self._fold_into(acc, op, reg_type(dtype), base, value)
         k.forget(acc)
+
+    def _fold_into(self, acc: str, op: str, typ: str, base: str, value: str) -> None:
+        """One instruction (or an f32 detour) writing ``base op value`` into ``acc``: an add of
+        a reusable product fuses into an fma; bf16, and f16 division, have no native form and
+        compute in f32, rounded back once."""
+        k = self.k
+        if op == "add":
+            fused = ops.fma_operands(k, typ, value, base)
+            if fused is not None:
+                k.emit(f"fma.rn.{typ}", (acc,), fused)
+                return
+        if typ == "bf16" or (typ == "f16" and op == "divide"):
+            wide = [Val(ops.cvt(k, r, typ, "f32"), "f32") for r in (base, value)]
+            k.emit(f"cvt.rn.{typ}.f32", (acc,), (ops.apply(k, op, wide, "f32").reg,))
+            return
+        float_form, int_form = ops.ACCUM[op]
+        mnemonic = float_form if typ in ("f32", "f64", "f16") else int_form
+        k.emit(f"{ops.arith(k, mnemonic)}.{typ}", (acc,), (base, value))
 
     # --- reduce -----------------------------------------------------------------------
     def _combine(self, program: Sequence[Assign], states: Sequence[str]) -> None:
@@ -516,24 +571,26 @@ class Lowering:
         return None
 
     def emit_WarpShuffle(self, s: WarpShuffle) -> None:
-        if getattr(s, "prefix", False):
-            raise NotImplementedError("WarpShuffle: prefix (shfl.up) form")
-        if not 2 <= s.length <= 32 or s.length & (s.length - 1):
-            raise ValueError(f"WarpShuffle: length {s.length} is not a power of two in [2, 32]")
-        if len(s.state) != len(s.state_b):
-            raise ValueError("WarpShuffle: state and state_b differ in length")
-        k, dtype = self.k, s.dtype.name
-        for st in s.state:
-            self._variable(st, dtype)
-        mask = k.reg("u32")
-        k.emit("activemask.b32", (mask,))
-        if (form := self._redux_form(s)) is not None:
-            st = s.state[0]
-            out = k.reg(reg_type(dtype))
-            k.emit(form, (out,), (self._data(st).reg, mask))
-            self._write(st, Val(out, dtype))
+        """A butterfly across ``length`` lanes of each state variable, combined by the Assign
+        program at every stride (one ``redux.sync`` where that is exact)."""
+        problem = _shuffle_problem(s)
+        if problem is not None:
+            raise problem
+        dtype = s.dtype.name
+        states = [self._variable(st, dtype) for st in s.state]
+        mask = self._active_mask()
+        form = self._redux_form(s)
+        if form is None:
+            self._ladder(s.state, s.state_b, s.combine_states, s.length, dtype, mask)
             return
-        self._ladder(s.state, s.state_b, s.combine_states, s.length, dtype, mask)
+        reduced = self.k.reg(reg_type(dtype))
+        self.k.emit(form, (reduced,), (self._data(s.state[0]).reg, mask))
+        self._write(s.state[0], Val(reduced, states[0].dtype))
+
+    def _active_mask(self) -> str:
+        mask = self.k.reg("u32")
+        self.k.emit("activemask.b32", (mask,))
+        return mask
 
     def _ladder(self, state: Sequence[str], state_b: Sequence[str], program: Sequence[Assign],
                 length: int, dtype: str, mask: str) -> None:
@@ -569,23 +626,25 @@ class Lowering:
     def emit_TreeHalve(self, s: TreeHalve) -> None:
         """The halving tree over shared slots: at each level slot t folds in slot t + half,
         until slot 0 holds the result, which every thread takes. Segmented (``inner``): slot t
-        is buf[t * scale + inner]."""
-        if s.length < 2 or s.length & (s.length - 1):
-            raise ValueError(f"TreeHalve: length {s.length} is not a power of two >= 2")
-        if not len(s.bufs) == len(s.state) == len(s.state_b):
-            raise ValueError("TreeHalve: bufs, state and state_b differ in length")
-        trees = [(self.mem[b], st, sb) for b, st, sb in zip(s.bufs, s.state, s.state_b,
-                                                            strict=True)]
+        is buf[t * scale + inner]. Up to 32 unsegmented shared slots are reduced by a shuffle
+        ladder over one read of the slots instead (``_tree_by_shuffle``), with the same
+        result."""
+        problem = _tree_problem(s)
+        if problem is not None:
+            raise problem
+        trees = [(self.mem[buf], st, sb)
+                 for buf, st, sb in zip(s.bufs, s.state, s.state_b, strict=True)]
         for mem, st, _ in trees:
             self._variable(st, mem.dtype)
-        t = self._int(Var(s.tid_var))
-        if s.length <= 32 and s.inner is None and all(isinstance(m, SharedBuf) for m, _, _ in
-                                                        trees):
-            self._tree_by_shuffle(s, trees)
-            if self._touched_after(s, s.bufs):
-                self.emit_Sync(Sync(barrier_id=s.barrier_id, count=s.barrier_count))
+        tid = self._int(Var(s.tid_var))
+        by_shuffle = s.length <= 32 and s.inner is None and all(
+            isinstance(mem, SharedBuf) for mem, _, _ in trees)
+        if not by_shuffle:
+            self._tree_by_halving(s, trees, tid)
             return
-        self._tree_by_halving(s, trees, t)
+        self._tree_by_shuffle(s, trees)
+        if self._touched_after(s, s.bufs):
+            self.emit_Sync(Sync(barrier_id=s.barrier_id, count=s.barrier_count))
 
     def _tree_by_shuffle(self, s: TreeHalve, trees: list[tuple[Memory, str, str]]) -> None:
         """Every warp reads the ``length`` slots into its lanes and runs the butterfly ladder
@@ -609,44 +668,57 @@ class Lowering:
             self._write(st, Val(top, v.dtype))
 
     def _tree_by_halving(self, s: TreeHalve, trees: list[tuple[Memory, str, str]], t: Aff) -> None:
+        """Level by level, halves ``length/2 .. 1``: thread t < half combines slot t with slot
+        t + half and stores the result in slot t; a barrier closes each level. Then every
+        thread reads the root slot."""
         k = self.k
-        scale, root = (1, Aff()) if s.inner is None else (s.inner[1], self._int(Var(s.inner[0])))
-        sync = Sync(barrier_id=s.barrier_id, count=s.barrier_count)
-        for half in (s.length >> i for i in range(1, s.length.bit_length())):
-            mine, stride = t * scale + root, half * scale
+        if s.inner is None:
+            scale, root = 1, Aff()
+        else:
+            scale, root = s.inner[1], self._int(Var(s.inner[0]))
+        level_done = Sync(barrier_id=s.barrier_id, count=s.barrier_count)
+        half = s.length // 2
+        while half:
+            mine = t * scale + root
             active = index.compare(k, "<", t, Aff.k(half))
             with self._where(active), self._block():
                 for mem, st, sb in trees:
                     self._write(st, self._load(mem, mine, mem.dtype)[0])
-                    self.env[sb] = self._load(mem, mine + stride, mem.dtype)[0]
+                    self.env[sb] = self._load(mem, mine + half * scale, mem.dtype)[0]
                 self._combine(s.combine_states, s.state)
                 for mem, st, _ in trees:
                     self._store(mem, mine, [self._data(st)])
-            self.emit_Sync(sync)
+            self.emit_Sync(level_done)
+            half //= 2
         for mem, st, _ in trees:
             self._write(st, self._load(mem, root, mem.dtype)[0])
 
     # --- control ----------------------------------------------------------------------
     def emit_Cond(self, s: Cond) -> None:
+        """``if``: a decided condition keeps one branch only; an ``if`` without ``else`` is a
+        predicated region; otherwise two regions joined by branches."""
         p = self._pred(s.cond)
         if isinstance(p, bool):
             with self._block():
                 self.body(s.body if p else s.else_body)
-            return
-        k = self.k
-        if not s.else_body:
+        elif not s.else_body:
             with self._where(p), self._block():
                 self.body(s.body)
-            return
-        other, end = k.label("else"), k.label("endif")
-        k.emit("bra", src=(other,), pred=f"!{p}", barrier=True)
-        with k.region(), self._block():
-            self.body(s.body)
-            k.emit("bra.uni", src=(end,), barrier=True)
-        k.place(other)
-        with k.region(), self._block():
-            self.body(s.else_body)
-        k.place(end)
+        else:
+            self._if_else(p, s.body, s.else_body)
+
+    def _if_else(self, p: str, then: Sequence[Stmt], otherwise: Sequence[Stmt]) -> None:
+        k = self.k
+        to_else, to_end = k.label("else"), k.label("endif")
+        k.emit("bra", src=(to_else,), pred=f"!{p}", barrier=True)
+        for label, stmts, leave in ((None, then, to_end), (to_else, otherwise, None)):
+            if label is not None:
+                k.place(label)
+            with k.region(), self._block():
+                self.body(stmts)
+                if leave is not None:
+                    k.emit("bra.uni", src=(leave,), barrier=True)
+        k.place(to_end)
 
     def emit_Loop(self, s: Loop | StridedLoop) -> None:
         """for (axis = start; axis < end; axis += step) body. Seeds the Accums of its own body,
@@ -654,77 +726,106 @@ class Lowering:
         more than one apart, a barrier meets differing counts, or unrolling is off; otherwise
         a full unroll when it fits ``UNROLL_BUDGET``, else a counted loop of ``f`` copies per
         trip followed by the leftover trips as copies (guarded where some thread stops)."""
-        k = self.k
-        if isinstance(s, StridedLoop):
-            step = self._int(s.step) if isinstance(s.step, Expr) else Aff.k(int(s.step))
-            start = self._int(s.start)
-            end = None if s.end is None else self._int(s.end)
-        else:
-            if getattr(s, "carries", None):
-                raise NotImplementedError("Loop: carried state")
-            start, step, end = Aff(), Aff.k(1), None
-        if end is None:
-            if not s.axis.extent.is_static:
-                raise NotImplementedError(f"loop over {s.axis.name}: symbolic extent")
-            end = Aff.k(s.axis.extent.as_static())
-
-        seen: set[str] = set()
-        for st in s.body:
-            if not isinstance(st, Accum) or st.name in seen:
-                continue
-            seen.add(st.name)
-            if s.seed:
-                self._init(st.name, st.op.identity,
-                           st.dtype.name if st.dtype is not None else "f32")
-            elif st.name not in self.env:
-                raise ValueError(f"Accum {st.name!r}: seed=False but no enclosing seed")
-
+        start, step, end = self._loop_range(s)
+        self._seed_accumulators(s)
         stmts = list(walk(s.body))
-        names = sorted({n for st in stmts for n in self._written(st)} & set(self.env))
-        written = [self._variable(n).reg for n in names]
-        for reg in written:  # whatever the loop's shape, no product of these survives into it
-            k.forget(reg)
-
+        written = self._carried(stmts)
         trips = None if self.no_unroll else self._trips(start, step, end, stmts)
         self.loop_depth += 1
         try:
             if trips is None:
                 self._runtime_loop(s, start, step, end, written)
-                return
-            lo, hi = trips
-            n = step.const
-            if hi <= 1:
-                self._unrolled(s, start, n, end, lo, range(hi))
-                return
-            cost = max(1, self._cost(s.body))
-            if hi * cost <= UNROLL_BUDGET or s.unroll is True and hi * cost <= 4 * UNROLL_BUDGET:
-                self._unrolled(s, start, n, end, lo, range(hi))
-                return
-            nested = any(isinstance(st, Loop | StridedLoop) for st in stmts)
-            f = NESTED_COPIES if nested else 1 << max(0, (BODY_BUDGET // cost).bit_length() - 1)
-            f = max(1, min(f, MAX_COPIES, hi))
-            m = lo // f * f
-            if m == 0:
-                self._unrolled(s, start, n, end, lo, range(hi))
-                return
-            self._counted(s, start, n, m, f, written)
-            self._unrolled(s, start, n, end, lo, range(m, hi))
+            else:
+                self._static_loop(s, start, step.const, end, trips, stmts, written)
         finally:
             self.loop_depth -= 1
+
+    def _loop_range(self, s: Loop | StridedLoop) -> tuple[Aff, Aff, Aff]:
+        """(start, step, end) of the loop's axis; a Loop runs 0, 1, ... up to its extent, a
+        StridedLoop from its own start by its own step up to its end (default: the extent)."""
+        end: Aff | None = None
+        if isinstance(s, StridedLoop):
+            step = self._int(s.step) if isinstance(s.step, Expr) else Aff.k(int(s.step))
+            start = self._int(s.start)
+            if s.end is not None:
+                end = self._int(s.end)
+        else:
+            if getattr(s, "carries", None):
+                raise NotImplementedError("Loop: carried state")
+            start, step = Aff(), Aff.k(1)
+        if end is None:
+            extent = s.axis.extent
+            if not extent.is_static:
+                raise NotImplementedError(f"loop over {s.axis.name}: symbolic extent")
+            end = Aff.k(extent.as_static())
+        return start, step, end
+
+    def _seed_accumulators(self, s: Loop | StridedLoop) -> None:
+        """A seeding loop starts each accumulator its body folds into at the op's identity;
+        otherwise an enclosing loop must have seeded it."""
+        firsts: dict[str, Accum] = {}
+        for st in s.body:
+            if isinstance(st, Accum):
+                firsts.setdefault(st.name, st)
+        for name, acc in firsts.items():
+            if s.seed:
+                self._init(name, acc.op.identity, "f32" if acc.dtype is None else acc.dtype.name)
+            elif name not in self.env:
+                raise ValueError(f"Accum {name!r}: seed=False but no enclosing seed")
+
+    def _carried(self, stmts: Sequence[Stmt]) -> list[str]:
+        """The variables of the names the loop body writes in place (live across every trip);
+        no result computed from them before the loop may be reused inside it."""
+        names = {n for st in stmts for n in _state_written(st)} & set(self.env)
+        regs = [self._variable(n).reg for n in sorted(names)]
+        for reg in regs:
+            self.k.forget(reg)
+        return regs
+
+    def _static_loop(self, s: Loop | StridedLoop, start: Aff, n: int, end: Aff,
+                     trips: tuple[int, int], stmts: Sequence[Stmt], written: list[str]) -> None:
+        """A loop whose trip counts the facts bound (``lo`` every thread runs, ``hi`` some):
+        fully unrolled, or ``f`` copies per counted trip and the rest unrolled."""
+        lo, hi = trips
+        f = self._unroll_factor(s, hi, stmts)
+        m = 0 if f is None else lo // f * f  # trips the counted loop runs
+        if m:
+            self._counted(s, start, n, m, f, written)
+        self._unrolled(s, start, n, end, lo, range(m, hi))
+
+    def _unroll_factor(self, s: Loop | StridedLoop, hi: int, stmts: Sequence[Stmt]
+                       ) -> int | None:
+        """Copies per trip of a counted loop, or None to unroll every trip: when there is at
+        most one, or all ``hi`` copies fit ``UNROLL_BUDGET`` estimated instructions (four
+        times that for a loop marked unroll). A loop around loops takes ``NESTED_COPIES``,
+        others the largest power of two whose copies fit ``BODY_BUDGET``."""
+        if hi <= 1:
+            return None
+        cost = max(1, self._cost(s.body))
+        budget = UNROLL_BUDGET * (4 if s.unroll is True else 1)
+        if hi * cost <= UNROLL_BUDGET or hi * cost <= budget:
+            return None
+        if any(isinstance(st, Loop | StridedLoop) for st in stmts):
+            f = NESTED_COPIES
+        else:
+            f = 1 << max(0, (BODY_BUDGET // cost).bit_length() - 1)
+        return max(1, min(f, MAX_COPIES, hi))
 
     emit_StridedLoop = emit_Loop
 
     def _unrolled(self, s: Loop | StridedLoop, start: Aff, n: int, end: Aff, lo: int,
                   trips: range) -> None:
-        """Copy j of the body for each j in ``trips``, the axis at start + j*n; copies from
-        ``lo`` on run only where start + j*n < end."""
+        """One copy of the body per trip j in ``trips``, the axis at ``start + j*n``. Trips
+        below ``lo`` run on every thread; a later copy runs where its axis value is still below
+        ``end``, and none after the first copy no thread reaches."""
         k = self.k
         for j in trips:
-            p = True if j < lo else index.compare(k, "<", start + j * n, end)
-            if p is False:
-                break
-            with self._where(p), self._block():
-                self.env[s.axis.name] = start + j * n
+            at = start + j * n
+            runs = True if j < lo else index.compare(k, "<", at, end)
+            if runs is False:
+                return
+            with self._where(runs), self._block():
+                self.env[s.axis.name] = at
                 self.body(s.body)
 
     def _loop_head(self, init: Aff, bound: Aff, rng: tuple[int, int] | None,
@@ -818,28 +919,24 @@ class Lowering:
         k.emit("bra", src=(top,), pred=again, barrier=True)
         k.place(done)
 
-    def _trips(self, start: Aff, step: Aff, end: Aff, stmts: list[Stmt]
+    def _trips(self, start: Aff, step: Aff, end: Aff, stmts: Sequence[Stmt]
                ) -> tuple[int, int] | None:
-        """(trips every thread runs, trips some thread runs) when at most one apart; a barrier
-        needs every thread on every trip. Else None."""
-        rng = start.range(self.k.ranges)
-        if not (step.is_const and step.const > 0 and end.is_const and rng is not None):
+        """(trips every thread runs, trips some thread runs) for a constant positive step and
+        end, when the two differ by at most one; a body with a barrier needs them equal (every
+        thread on every trip). Otherwise None: the loop runs as a runtime loop."""
+        first = start.range(self.k.ranges)
+        if first is None or not (step.is_const and step.const > 0 and end.is_const):
             return None
-        n = step.const
-        lo = max(0, -(-(end.const - rng[1]) // n))
-        hi = max(0, -(-(end.const - rng[0]) // n))
-        barrier = any(isinstance(st, BARRIERS) for st in stmts)
-        if hi - lo > 1 or (barrier and lo != hi):
-            return None
-        return lo, hi
 
-    @staticmethod
-    def _written(st: Stmt) -> Sequence[str]:
-        if isinstance(st, Accum):
-            return (st.name,)
-        if isinstance(st, WarpShuffle | TreeHalve):
-            return tuple(st.state)
-        return ()
+        def count(from_value: int) -> int:  # trips from an axis value: ceil((end - v) / step)
+            return max(0, -((from_value - end.const) // step.const))
+
+        fewest, most = count(first[1]), count(first[0])
+        if most - fewest > 1:
+            return None
+        if fewest != most and any(isinstance(st, BARRIERS) for st in stmts):
+            return None
+        return fewest, most
 
     def _cost(self, body: Sequence[Stmt]) -> int:
         """Estimated PTX instructions of one pass over ``body``."""
@@ -869,101 +966,223 @@ class Lowering:
         return c
 
     # --- expressions ------------------------------------------------------------------
-    def expr(self, e: Expr) -> Value:
-        """An index expression as an Aff, data as a Val, a decided predicate as a bool."""
-        k = self.k
-        if isinstance(e, Var):
-            return self._lookup(e.name)
-        if isinstance(e, Literal):
-            if e.dtype == "bool" or isinstance(e.value, bool):
-                return bool(e.value)
-            if e.dtype == "int" or isinstance(e.value, int):
-                return Aff.k(int(e.value))
-            return Val(ops.const(k, float(e.value), "f32"), "f32")
-        if isinstance(e, BinaryExpr):
-            return self._binary(e)
-        if isinstance(e, TernaryExpr):
-            p = self._pred(e.cond)
-            if isinstance(p, bool):
-                return self.expr(e.if_true if p else e.if_false)
-            a, b = self.expr(e.if_true), self.expr(e.if_false)
-            if isinstance(a, Aff) and isinstance(b, Aff):
-                return index.select(k, p, a, b)
-            va, vb = self._as_val(a), self._as_val(b)
-            dtype = va.dtype if va.dtype == vb.dtype else "f32"
-            x, y = ops.convert(k, va, dtype).reg, ops.convert(k, vb, dtype).reg
-            return ops.select(k, p, x, y, dtype)
-        if isinstance(e, FuncCallExpr):
-            return ops.apply(k, e.name, [self._value(a, "f32") for a in e.args], "f32")
-        if isinstance(e, CastExpr) and e.dtype == "float":
-            return self._value(e.expr, "f32")
-        raise NotImplementedError(f"expression {e!r}")
+    # An expression evaluates to an index (``Aff``), data (``Val``), or a ``bool`` for a
+    # predicate the index facts decide. Each Expr class has its own method (``_EXPR``).
 
-    def _binary(self, e: BinaryExpr) -> Value:
-        k, op = self.k, e.op
-        if op in ("&&", "||"):
-            pa, pb = self._pred(e.left), self._pred(e.right)
-            if isinstance(pa, str) and isinstance(pb, str):
-                return Val(k.pure("and.pred" if op == "&&" else "or.pred", "pred", pa, pb),
-                           "bool")
-            c, other = (pa, pb) if isinstance(pa, bool) else (pb, pa)
-            p = other if c == (op == "&&") else c
+    def expr(self, e: Expr) -> Value:
+        method = _EXPR.get(type(e))
+        if method is None:
+            raise NotImplementedError(f"expression {e!r}")
+        return method(self, e)
+
+    def _expr_var(self, e: Var) -> Value:
+        return self._lookup(e.name)
+
+    def _expr_literal(self, e: Literal) -> Value:
+        if e.dtype == "bool" or isinstance(e.value, bool):
+            return bool(e.value)
+        if e.dtype == "int" or isinstance(e.value, int):
+            return Aff.k(int(e.value))
+        return Val(ops.const(self.k, float(e.value), "f32"), "f32")
+
+    def _expr_ternary(self, e: TernaryExpr) -> Value:
+        p = self._pred(e.cond)
+        if isinstance(p, bool):
+            return self.expr(e.if_true if p else e.if_false)
+        yes, no = self.expr(e.if_true), self.expr(e.if_false)
+        if isinstance(yes, Aff) and isinstance(no, Aff):
+            return index.select(self.k, p, yes, no)
+        vy, vn = self._as_val(yes), self._as_val(no)
+        dtype = vy.dtype if vy.dtype == vn.dtype else "f32"
+        ry = ops.convert(self.k, vy, dtype).reg
+        rn = ops.convert(self.k, vn, dtype).reg
+        return ops.select(self.k, p, ry, rn, dtype)
+
+    def _expr_call(self, e: FuncCallExpr) -> Value:
+        args = [self._value(a, "f32") for a in e.args]
+        return ops.apply(self.k, e.name, args, "f32")
+
+    def _expr_cast(self, e: CastExpr) -> Value:
+        if e.dtype != "float":
+            raise NotImplementedError(f"expression {e!r}")
+        return self._value(e.expr, "f32")
+
+    def _expr_binary(self, e: BinaryExpr) -> Value:
+        if e.op in ("&&", "||"):
+            return self._logical(e.op, self._pred(e.left), self._pred(e.right))
+        left, right = self.expr(e.left), self.expr(e.right)
+        if isinstance(left, Aff) and isinstance(right, Aff):
+            return self._index_binary(e, left, right)
+        x = ops.convert(self.k, self._as_val(left), "f32")
+        y = ops.convert(self.k, self._as_val(right), "f32")
+        if e.op in ops.CMP_SYMBOL:
+            return Val(self.k.pure(f"setp.{ops.CMP_SYMBOL[e.op]}.f32", "pred", x.reg, y.reg),
+                       "bool")
+        if e.op not in F32_SYMBOL:
+            raise NotImplementedError(f"f32 expression {e!r}")
+        return ops.apply(self.k, F32_SYMBOL[e.op], [x, y], "f32")
+
+    def _logical(self, op: str, pa: str | bool, pb: str | bool) -> Value:
+        """``pa && pb`` / ``pa || pb``. A decided side either settles the result (false for
+        ``&&``, true for ``||``) or leaves the other side as the result."""
+        if isinstance(pa, str) and isinstance(pb, str):
+            opcode = "and.pred" if op == "&&" else "or.pred"
+            return Val(self.k.pure(opcode, "pred", pa, pb), "bool")
+        settles = op == "||"
+        known, other = (pa, pb) if isinstance(pa, bool) else (pb, pa)
+        result = known if known == settles else other
+        return result if isinstance(result, bool) else Val(result, "bool")
+
+    def _index_binary(self, e: BinaryExpr, a: Aff, b: Aff) -> Value:
+        k = self.k
+        if e.op in ops.CMP_SYMBOL:
+            p = index.compare(k, e.op, a, b)
             return p if isinstance(p, bool) else Val(p, "bool")
-        a, b = self.expr(e.left), self.expr(e.right)
-        if isinstance(a, Aff) and isinstance(b, Aff):
-            if op in ops.CMP_SYMBOL:
-                p = index.compare(k, op, a, b)
-                return p if isinstance(p, bool) else Val(p, "bool")
-            if op == "+":
-                return a + b
-            if op == "-":
-                return a - b
-            if op == "*":
-                return index.mul(k, a, b)
-            if op in ("/", "//"):
-                return index.div(k, a, b)
-            if op == "%":
-                return index.mod(k, a, b)
+        fold = _INDEX_OPS.get(e.op)
+        if fold is None:
             raise NotImplementedError(f"index expression {e!r}")
-        x, y = (ops.convert(k, self._as_val(v), "f32") for v in (a, b))
-        if op in ops.CMP_SYMBOL:
-            return Val(k.pure(f"setp.{ops.CMP_SYMBOL[op]}.f32", "pred", x.reg, y.reg), "bool")
-        if op in F32_SYMBOL:
-            return ops.apply(k, F32_SYMBOL[op], [x, y], "f32")
-        raise NotImplementedError(f"f32 expression {e!r}")
+        return fold(k, a, b)
 
     def _as_val(self, v: Value) -> Val:
+        """Any value as data: an index as an i32 register, a decided bool as a predicate."""
         if isinstance(v, Val):
             return v
+        k = self.k
         if isinstance(v, bool):
-            one = index.reg_of(self.k, Aff.k(int(v)))
-            return Val(self.k.pure("setp.ne.u32", "pred", one, "0"), "bool")
-        return Val(index.reg_of(self.k, v), "i32")
+            word = index.reg_of(k, Aff.k(1 if v else 0))
+            return Val(k.pure("setp.ne.u32", "pred", word, "0"), "bool")
+        return Val(index.reg_of(k, v), "i32")
 
     def _value(self, e: Expr, dtype: str) -> Val:
-        """Expression ``e`` as data of ``dtype``; a literal is a constant of that type."""
-        if isinstance(e, Literal) and e.dtype != "bool" and not isinstance(e.value, bool):
+        """Expression ``e`` as data of ``dtype``; a number literal becomes a constant of that
+        type directly."""
+        numeric = isinstance(e, Literal) and e.dtype != "bool" and not isinstance(e.value, bool)
+        if numeric:
             return Val(ops.const(self.k, float(e.value), reg_type(dtype)), dtype)
         return ops.convert(self.k, self._as_val(self.expr(e)), dtype)
 
     def _int(self, e: Expr) -> Aff:
-        """Expression ``e`` as an index; integer data is copied out of a variable first, since
-        an index may outlive the variable's current value."""
+        """Expression ``e`` as an index. Integer data in a variable is copied out first: the
+        index may be used after the variable changes."""
         v = self.expr(e)
         if isinstance(v, Aff):
             return v
         if isinstance(v, bool) or not is_int(v.dtype):
             raise NotImplementedError(f"index expression {e!r} is not an integer")
-        reg = ops.convert(self.k, v, "i32").reg
-        if reg in self.k.variables:
-            copy, reg = reg, self.k.reg("u32")
-            self.k.emit("mov.b32", (reg,), (copy,))
+        k = self.k
+        reg = ops.convert(k, v, "i32").reg
+        if reg in k.variables:
+            snapshot = k.reg("u32")
+            k.emit("mov.b32", (snapshot,), (reg,))
+            reg = snapshot
         return Aff.of(reg)
 
     def _pred(self, e: Expr) -> str | bool:
+        """Expression ``e`` as a predicate register, or a bool when it is decided here; an index
+        is true where it is nonzero."""
         v = self.expr(e)
         if isinstance(v, bool):
             return v
         if isinstance(v, Aff):
             return index.compare(self.k, "!=", v, Aff())
         return ops.convert(self.k, v, "bool").reg
+
+def _expressions_of(st: Stmt) -> Iterator[Expr]:
+    """Every expression a statement holds directly (nested statements' bodies excluded), with
+    all of their subexpressions."""
+    pending: list[object] = [getattr(st, f) for f in getattr(st, "__dataclass_fields__", {})
+                             if f not in ("body", "else_body")]
+    while pending:
+        item = pending.pop()
+        if isinstance(item, tuple):
+            pending.extend(item)
+        elif isinstance(item, Expr):
+            yield item
+            pending.extend(getattr(item, f) for f in getattr(item, "__dataclass_fields__", {}))
+
+
+# statement class -> the Lowering method that emits it (``emit_<ClassName>``)
+_HANDLERS: dict[type, str] = {
+    cls: f"emit_{cls.__name__}" for cls in (
+        Accum, Assign, Cond, CpAsyncCommit, CpAsyncCopy, CpAsyncWait, Init, Let, Load, Loop,
+        Select, Smem, StridedLoop, Sync, Tile, TreeHalve, WarpShuffle, Write)
+    if hasattr(Lowering, f"emit_{cls.__name__}")}
+
+
+def _raster_pair(t: Tile) -> tuple[int, int, int] | None:
+    """(grouped axis, other axis, group size) when the Tile orders a pair of adjacent block
+    axes in raster groups, else None. ``raster_orient`` "m" groups the first axis of
+    ``raster_axes``, otherwise the second; a group of one, or a grouped axis of extent one,
+    leaves plain row-major order."""
+    names = [a.name for a in t.axes]
+    wanted = t.raster_axes or ()
+    if not t.raster_group or not wanted or any(n not in names for n in wanted):
+        return None
+    first, second = (names.index(n) for n in wanted)
+    if second != first + 1:
+        return None
+    grouped, other = (first, second) if t.raster_orient == "m" else (second, first)
+    size = min(t.raster_group, t.extents[grouped])
+    if t.extents[grouped] <= 1 or size <= 1:
+        return None
+    return grouped, other, size
+
+
+# the red.global.add type of each buffer dtype an atomic Write can add into
+_RED_ADD = {"f32": "f32", "f64": "f64", "f16": "noftz.f16", "bf16": "noftz.bf16",
+            "i32": "s32", "u32": "u32", "u64": "u64", "i64": "u64"}
+
+
+def _row_major(buf: str, shape: tuple[int, ...], parts: Sequence[Aff]) -> Aff:
+    """The row-major element offset of ``buf[parts]``: a single index is already flat;
+    otherwise one index per axis, each scaled by the product of the extents after it."""
+    if len(parts) < 2:
+        return parts[0] if parts else Aff()
+    if len(parts) != len(shape):
+        raise NotImplementedError(f"{buf}: {len(parts)}-d index into a {len(shape)}-d buffer")
+    scales = [math.prod(shape[i + 1:]) for i in range(len(shape))]
+    return Aff.combine(*zip(parts, scales, strict=True))
+
+
+# index arithmetic of a binary expression over two indices
+_INDEX_OPS = {"+": lambda k, a, b: a + b, "-": lambda k, a, b: a - b, "*": index.mul,
+              "/": index.div, "//": index.div, "%": index.mod}
+
+# Expr class -> the Lowering method that evaluates it
+_EXPR = {Var: Lowering._expr_var, Literal: Lowering._expr_literal,
+         BinaryExpr: Lowering._expr_binary, TernaryExpr: Lowering._expr_ternary,
+         FuncCallExpr: Lowering._expr_call, CastExpr: Lowering._expr_cast}
+
+
+def _shuffle_problem(s: WarpShuffle) -> Exception | None:
+    """Why this lowering cannot take the shuffle, or None."""
+    if getattr(s, "prefix", False):
+        return NotImplementedError("WarpShuffle: prefix (shfl.up) form")
+    n = s.length
+    if n < 2 or n > 32 or n & (n - 1):
+        return ValueError(f"WarpShuffle: length {n} is not a power of two in [2, 32]")
+    if len(s.state) != len(s.state_b):
+        return ValueError("WarpShuffle: state and state_b differ in length")
+    return None
+
+
+_SHARED_DTYPES = frozenset({"f32", "f64", "f16", "bf16", "i32", "u32", "i64", "u64"})
+
+
+def _state_written(st: Stmt) -> Sequence[str]:
+    """Names a statement writes in place: an accumulator, a reduction's state."""
+    if isinstance(st, Accum):
+        return (st.name,)
+    if isinstance(st, WarpShuffle | TreeHalve):
+        return tuple(st.state)
+    return ()
+
+
+def _tree_problem(s: TreeHalve) -> Exception | None:
+    """Why this lowering cannot take the halving tree, or None."""
+    n = s.length
+    if n < 2 or n & (n - 1):
+        return ValueError(f"TreeHalve: length {n} is not a power of two >= 2")
+    if len({len(s.bufs), len(s.state), len(s.state_b)}) != 1:
+        return ValueError("TreeHalve: bufs, state and state_b differ in length")
+    return None

@@ -1,9 +1,15 @@
 """Data values and the instruction sequences of Emmy's elementwise ops.
 
-A data value is a ``Val``: a register and its Emmy dtype (a bool is a predicate register). Emmy's
-dtype rule decides where an op computes (reference ``ptxgen/ops.py:173-192``): natively for f16's
-simple ops, integer ops and f64; every other op converts its inputs to f32, computes, and converts
-the result back once.
+A data value is a ``Val``: a register and its Emmy dtype (a bool is a predicate register).
+
+Every elementwise op is one row of ``SPECS``: its arity, its mnemonic on float registers, its
+mnemonic on integer registers, how its operands are formed (``x, x`` for a square, ``x, 0`` for a
+relu, the ``cvt.rXi`` form of a rounding), and on which float types it computes natively. Where an
+op computes is Emmy's dtype rule (reference ``ptxgen/ops.py:173-192``), stated by itself in
+``compute_type``: natively for f16's simple ops, for integer ops over integers and for f64; every
+other op converts its inputs to f32, computes, and converts the result back once. One emitter,
+``_emit``, turns a row into instructions for the chosen type; the f32 fast-math functions come
+from ``fastmath``.
 
 Float arithmetic rounds to nearest and says so: ``add.rn``, ``sub.rn`` and ``mul.rn`` carry the
 modifier explicitly, which stops ptxas from contracting a multiply and an add on its own. The
@@ -22,20 +28,16 @@ from __future__ import annotations
 
 from collections.abc import Callable, Sequence
 from dataclasses import dataclass
-from functools import partial
 
 from . import fastmath
 from .dtypes import FLOAT_TYPES, is_float, is_int, literal, move_type, reg_type, size
 from .ptx import Kernel
-
-Op = Callable[..., str]
 
 # Other spellings of Emmy's op names.
 ALIASES = {"sub": "subtract", "mul": "multiply", "div": "divide", "max": "maximum",
            "min": "minimum", "sum": "add", "prod": "multiply", "amax": "maximum",
            "amin": "minimum", "true_divide": "divide", "neg": "negative", "pow_": "pow",
            "power": "pow", "rsqrt_": "rsqrt"}
-BINARY = {"add", "subtract", "multiply", "divide", "maximum", "minimum", "pow"}
 # Ops an accumulator folds with -> (float mnemonic, integer mnemonic).
 ACCUM = {"add": ("add.rn", "add"), "subtract": ("sub.rn", "sub"), "multiply": ("mul.rn", "mul.lo"),
          "divide": ("div.rn", "div"), "maximum": ("max", "max"), "minimum": ("min", "min")}
@@ -56,6 +58,57 @@ class Val:
     dtype: str
 
 
+@dataclass(frozen=True)
+class Spec:
+    """How one elementwise op lowers.
+
+    ``fop`` is its mnemonic on float registers (None: no float instruction; f32 may still have
+    a fast-math function), ``iop`` its integer mnemonic and whether that takes a ``.b<bits>``
+    type. ``operands`` forms the instruction's sources: ``"args"`` as given, ``"self"`` the one
+    argument twice, ``"zero"`` the argument and 0. ``rounding`` ops are ``cvt.<mode>.t.t``.
+    ``natives`` lists the float types that compute the op natively besides f32."""
+
+    arity: int
+    fop: str | None = None
+    iop: tuple[str, bool] | None = None
+    operands: str = "args"
+    rounding: bool = False
+    natives: frozenset[str] = frozenset({"f16", "f64"})
+
+
+_F64_ONLY = frozenset({"f64"})
+SPECS: dict[str, Spec] = {
+    "add": Spec(2, "add.rn", ("add", False)),
+    "subtract": Spec(2, "sub.rn", ("sub", False)),
+    "multiply": Spec(2, "mul.rn", ("mul.lo", False)),
+    "divide": Spec(2, "div.rn", natives=_F64_ONLY),
+    "maximum": Spec(2, "max", ("max", False)),
+    "minimum": Spec(2, "min", ("min", False)),
+    "pow": Spec(2),
+    "relu": Spec(1, "max", operands="zero"),
+    "negative": Spec(1, "neg"),
+    "abs": Spec(1, "abs"),
+    "square": Spec(1, "mul.rn", operands="self", natives=_F64_ONLY),
+    "reciprocal": Spec(1, "rcp.rn", natives=_F64_ONLY),
+    "sqrt": Spec(1, "sqrt.rn", natives=_F64_ONLY),
+    "rsqrt": Spec(1, "rsqrt.approx", natives=frozenset()),
+    "floor": Spec(1, "cvt.rmi", rounding=True, natives=_F64_ONLY),
+    "ceil": Spec(1, "cvt.rpi", rounding=True, natives=_F64_ONLY),
+    "trunc": Spec(1, "cvt.rzi", rounding=True, natives=_F64_ONLY),
+    "round": Spec(1, "cvt.rni", rounding=True, natives=_F64_ONLY),
+    "floor_divide": Spec(2, iop=("div", False)),
+    "remainder": Spec(2, iop=("rem", False)),
+    "mod": Spec(2, iop=("rem", False)),
+    "left_shift": Spec(2, iop=("shl", True)),
+    "right_shift": Spec(2, iop=("shr", False)),
+    "bitwise_and": Spec(2, iop=("and", True)),
+    "bitwise_or": Spec(2, iop=("or", True)),
+    "bitwise_xor": Spec(2, iop=("xor", True)),
+}
+for _name in fastmath.F32_FUNCS:
+    SPECS.setdefault(_name, Spec(1))
+
+
 def const(k: Kernel, value: float, typ: str) -> str:
     """A register holding ``value`` (16-bit float arithmetic takes no immediates)."""
     return k.pure(f"mov.{move_type(typ)}", typ, literal(value, typ))
@@ -71,134 +124,164 @@ def arith(k: Kernel, m: str) -> str:
     return UNFUSED.get(m, m) if k.no_fusion else m
 
 
-def _bin(m: str, t: str, k: Kernel, a: str, b: str) -> str:
-    return k.pure(f"{arith(k, m)}.{t}", t, a, b)
-
-
-def _un(m: str, t: str, k: Kernel, x: str) -> str:
-    return k.pure(f"{m}.{t}", t, x)
-
-
 def fma_operands(k: Kernel, t: str, a: str, b: str) -> tuple[str, str, str] | None:
     """``(x, y, c)`` when ``a + b`` is ``x * y + c`` for a multiply of type ``t`` that is still
-    reusable here, trying ``a`` first; never with fusion off, and only for f32/f64."""
+    reusable here, trying ``a`` as the product first; never with fusion off, and only for
+    f32/f64."""
     if k.no_fusion or t not in ("f32", "f64"):
         return None
-    for prod, c in ((a, b), (b, a)):
-        key = k.definition(prod)
-        if key and key[0] == f"mul.rn.{t}":
-            return key[1], key[2], c
+    wanted = f"mul.rn.{t}"
+    for prod, addend in ((a, b), (b, a)):
+        key = k.definition(prod)  # (mnemonic, x, y), plus a uniquifier with CSE off
+        if key is not None and key[0] == wanted:
+            return key[1], key[2], addend
     return None
 
 
-def _add(t: str, k: Kernel, a: str, b: str) -> str:
-    if (f := fma_operands(k, t, a, b)) is not None:
-        return k.pure(f"fma.rn.{t}", t, *f)
-    return _bin("add.rn", t, k, a, b)
+# --- where an op computes, and the instructions ---------------------------------------------
 
 
-def _float_ops(t: str) -> dict[str, Op]:
-    def zero(k: Kernel) -> str:
-        return const(k, 0.0, t) if t == "f16" else literal(0.0, t)
-
-    return {
-        "add": partial(_add, t),
-        "subtract": partial(_bin, "sub.rn", t),
-        "multiply": partial(_bin, "mul.rn", t),
-        "divide": partial(_bin, "div.rn", t),
-        "maximum": partial(_bin, "max", t),
-        "minimum": partial(_bin, "min", t),
-        "relu": lambda k, x: _bin("max", t, k, x, zero(k)),
-        "negative": partial(_un, "neg", t),
-        "abs": partial(_un, "abs", t),
-        "square": lambda k, x: _bin("mul.rn", t, k, x, x),
-        "reciprocal": partial(_un, "rcp.rn", t),
-        "sqrt": partial(_un, "sqrt.rn", t),
-        "floor": partial(_un, "cvt.rmi", t + "." + t) if t != "f16" else None,
-        "ceil": partial(_un, "cvt.rpi", t + "." + t) if t != "f16" else None,
-        "trunc": partial(_un, "cvt.rzi", t + "." + t) if t != "f16" else None,
-        "round": partial(_un, "cvt.rni", t + "." + t) if t != "f16" else None,
-    }
+def compute_type(name: str, arg_dtypes: Sequence[str], dtype: str) -> str:
+    """The Emmy dtype op ``name`` computes in for result ``dtype``: f16's simple ops over f16
+    arguments, integer ops over integer arguments and f64 ops compute natively; everything else
+    in f32."""
+    spec = SPECS.get(name)
+    if spec is not None:
+        typ = reg_type(dtype)
+        if typ == "f16":
+            same = all(d == dtype for d in arg_dtypes)
+            if same and spec.fop is not None and "f16" in spec.natives:
+                return dtype
+        elif is_int(dtype):
+            if spec.iop is not None and all(is_int(d) for d in arg_dtypes):
+                return dtype
+        elif dtype == "f64" and spec.fop is not None and "f64" in spec.natives:
+            return dtype
+    return "f32"
 
 
-def _rounding(m: str, t: str, k: Kernel, x: str) -> str:
-    return k.pure(f"{m}.{t}.{t}", t, x)
+def _emit(k: Kernel, name: str, spec: Spec, typ: str, srcs: list[str]) -> str:
+    """The instructions of op ``name`` on registers of PTX type ``typ``."""
+    if spec.iop is not None and typ not in FLOAT_TYPES:
+        mnemonic, bit_typed = spec.iop
+        if mnemonic in ("shl", "shr") and size(typ) != 4:
+            raise NotImplementedError(f"{typ} op {name}: shift of a non-32-bit integer")
+        suffix = f"b{size(typ) * 8}" if bit_typed else typ
+        return k.pure(f"{mnemonic}.{suffix}", typ, *srcs)
+    if spec.rounding:
+        return k.pure(f"{spec.fop}.{typ}.{typ}", typ, *srcs)
+    if name == "add" and (fused := fma_operands(k, typ, *srcs)) is not None:
+        return k.pure(f"fma.rn.{typ}", typ, *fused)
+    if spec.operands == "self":
+        srcs = [srcs[0], srcs[0]]
+    elif spec.operands == "zero":
+        zero = const(k, 0.0, typ) if typ == "f16" else literal(0.0, typ)
+        srcs = [srcs[0], zero]
+    return k.pure(f"{arith(k, spec.fop)}.{typ}", typ, *srcs)
 
 
-F32_OPS: dict[str, Op] = {n: f for n, f in _float_ops("f32").items() if f is not None}
-F32_OPS |= {"rsqrt": partial(_un, "rsqrt.approx", "f32")}
-for _m, _n in (("cvt.rmi", "floor"), ("cvt.rpi", "ceil"), ("cvt.rzi", "trunc"),
-               ("cvt.rni", "round")):
-    F32_OPS[_n] = partial(_rounding, _m, "f32")
-F64_OPS: dict[str, Op] = {n: f for n, f in _float_ops("f64").items() if f is not None}
-for _m, _n in (("cvt.rmi", "floor"), ("cvt.rpi", "ceil"), ("cvt.rzi", "trunc"),
-               ("cvt.rni", "round")):
-    F64_OPS[_n] = partial(_rounding, _m, "f64")
-# f16 computes natively only where Emmy does (its simple ops); the rest go through f32.
-F16_OPS = {n: f for n, f in _float_ops("f16").items()
-           if f is not None and n not in ("divide", "reciprocal", "sqrt", "square", "floor",
-                                          "ceil", "trunc", "round")}
-# Integer ops Emmy keeps integer: op -> (mnemonic, whether it takes a .b<bits> type).
-INT_OPS = {"add": ("add", False), "subtract": ("sub", False), "multiply": ("mul.lo", False),
-           "floor_divide": ("div", False), "remainder": ("rem", False), "mod": ("rem", False),
-           "left_shift": ("shl", True), "right_shift": ("shr", False),
-           "bitwise_and": ("and", True), "bitwise_or": ("or", True),
-           "bitwise_xor": ("xor", True), "maximum": ("max", False), "minimum": ("min", False)}
+def _operation(name: str, at: str) -> Callable[[Kernel, list[str]], str] | None:
+    """How op ``name`` runs on registers of Emmy dtype ``at``, or None if it cannot."""
+    spec = SPECS.get(name)
+    typ = reg_type(at)
+    if at == "f32" and spec is not None and spec.fop is None and name in fastmath.F32_FUNCS:
+        return lambda k, srcs: fastmath.F32_FUNCS[name](k, *srcs)
+    if spec is None:
+        return None
+    if typ in FLOAT_TYPES and spec.fop is None:
+        return None
+    if typ not in FLOAT_TYPES and spec.iop is None:
+        return None
+    return lambda k, srcs: _emit(k, name, spec, typ, srcs)
 
 
-def _int_op(name: str, t: str, k: Kernel, a: str, b: str) -> str:
-    m, bits = INT_OPS[name]
-    if m in ("shl", "shr") and size(t) != 4:
-        raise NotImplementedError(f"{t} op {name}: shift of a non-32-bit integer")
-    return k.pure(f"{m}.{f'b{size(t) * 8}' if bits else t}", t, a, b)
+def apply(k: Kernel, name: str, args: Sequence[Val], dtype: str) -> Val:
+    """name(args) at result ``dtype`` under Emmy's rule: native where Emmy computes there,
+    otherwise in f32, converted once."""
+    name = canonical(name)
+    at = compute_type(name, [a.dtype for a in args], dtype)
+    run = _operation(name, at)
+    if run is None:
+        raise NotImplementedError(f"{at} op {name}")
+    want = SPECS[name].arity
+    if len(args) != want:
+        raise ValueError(f"{at} op {name} takes {want} argument(s), got {len(args)}")
+    srcs = [convert(k, a, at).reg for a in args]
+    return convert(k, Val(run(k, srcs), at), dtype)
+
+
+# --- conversions -----------------------------------------------------------------------------
+
+
+def _cvt_modifier(src: str, dst: str) -> str:
+    """C's rules: a float result rounds to nearest (widening a float is exact and takes none),
+    a float to integer truncates, integer to integer needs none."""
+    if src in FLOAT_TYPES and dst in FLOAT_TYPES:
+        return "" if size(dst) > size(src) else ".rn"
+    if dst in FLOAT_TYPES:
+        return ".rn"
+    return ".rzi" if src in FLOAT_TYPES else ""
 
 
 def cvt(k: Kernel, x: str, src: str, dst: str) -> str:
-    """Register ``x`` from PTX type ``src`` to ``dst`` with C's rules: floats round to nearest,
-    float to integer truncates, two 16-bit floats meet in f32 (exact)."""
+    """Register ``x`` from PTX type ``src`` to ``dst``: two floats neither of which is f32 meet
+    in f32 (exact for the 16-bit ones); bf16 -> f32 is a register pack."""
     if src == dst:
         return x
-    if src in FLOAT_TYPES and dst in FLOAT_TYPES and "f32" not in (src, dst):
+    both_float = src in FLOAT_TYPES and dst in FLOAT_TYPES
+    if both_float and src != "f32" and dst != "f32":
         return cvt(k, cvt(k, x, src, "f32"), "f32", dst)
-    if src == "bf16" and dst == "f32":
+    if (src, dst) == ("bf16", "f32"):
         # exact: the bf16 bits are the upper half of the f32 bits. A register pack runs on the
         # integer pipe, where cvt.f32.bf16 would take a slot of the XU pipe that ex2/rcp need.
-        zero = k.pure("mov.b16", "b16", "0")
-        return k.pure("mov.b32", "f32", f"{{{zero}, {x}}}")
-    if src in FLOAT_TYPES and dst in FLOAT_TYPES:
-        rnd = "" if size(dst) > size(src) else ".rn"  # widening is exact
-    elif dst in FLOAT_TYPES:
-        rnd = ".rn"
-    elif src in FLOAT_TYPES:
-        rnd = ".rzi"
+        low = k.pure("mov.b16", "b16", "0")
+        return k.pure("mov.b32", "f32", f"{{{low}, {x}}}")
+    return k.pure(f"cvt{_cvt_modifier(src, dst)}.{dst}.{src}", dst, x)
+
+
+def _bool_to(k: Kernel, p: str, dtype: str) -> Val:
+    """A predicate as 1 / 0 of ``dtype`` (16-bit floats take registers, not immediates)."""
+    typ = reg_type(dtype)
+    if typ in ("f16", "bf16"):
+        one = const(k, 1.0, typ)
+        zero = const(k, 0.0, typ)
     else:
-        rnd = ""
-    return k.pure(f"cvt{rnd}.{dst}.{src}", dst, x)
+        one, zero = literal(1.0, typ), literal(0.0, typ)
+    return select(k, p, one, zero, dtype)
+
+
+def _to_bool(k: Kernel, v: Val) -> Val:
+    """Nonzero as true: compared in f32 for floats, in i32 for integers."""
+    wide = convert(k, v, "f32" if is_float(v.dtype) else "i32")
+    typ = reg_type(wide.dtype)
+    return Val(k.pure(f"setp.ne.{typ}", "pred", wide.reg, literal(0.0, typ)), "bool")
 
 
 def convert(k: Kernel, v: Val, dtype: str) -> Val:
     """``v`` as Emmy dtype ``dtype``: rounding conversions, bool as 1/0, nonzero as true."""
     if v.dtype == dtype:
         return v
-    typ = reg_type(dtype)
     if v.dtype == "bool":
-        one, zero = (const(k, 1.0, typ), const(k, 0.0, typ)) if typ in ("f16", "bf16") else (
-            literal(1.0, typ), literal(0.0, typ))
-        return select(k, v.reg, one, zero, dtype)
+        return _bool_to(k, v.reg, dtype)
     if dtype == "bool":
-        x = convert(k, v, "f32" if is_float(v.dtype) else "i32")
-        zero = literal(0.0, reg_type(x.dtype))
-        return Val(k.pure(f"setp.ne.{reg_type(x.dtype)}", "pred", x.reg, zero), dtype)
-    return Val(cvt(k, v.reg, reg_type(v.dtype), typ), dtype)
+        return _to_bool(k, v)
+    return Val(cvt(k, v.reg, reg_type(v.dtype), reg_type(dtype)), dtype)
 
 
 def select(k: Kernel, cond: str, a: str, b: str, dtype: str) -> Val:
+    """``cond ? a : b``; bools by predicate logic (a selp has no predicate form)."""
     typ = reg_type(dtype)
-    if typ == "pred":
-        out = k.pure("or.pred", "pred", k.pure("and.pred", "pred", cond, a),
-                     k.pure("and.pred", "pred", k.pure("not.pred", "pred", cond), b))
-        return Val(out, dtype)
-    return Val(k.pure(f"selp.{move_type(typ)}", typ, a, b, cond), dtype)
+    if typ != "pred":
+        return Val(k.pure(f"selp.{move_type(typ)}", typ, a, b, cond), dtype)
+    take_a = k.pure("and.pred", "pred", cond, a)
+    take_b = k.pure("and.pred", "pred", k.pure("not.pred", "pred", cond), b)
+    return Val(k.pure("or.pred", "pred", take_a, take_b), dtype)
+
+
+# --- Assign ----------------------------------------------------------------------------------
+
+
+_FLOAT_RANK = ("f16", "bf16", "f32", "f64")
 
 
 def promote(name: str, dtypes: Sequence[str]) -> str:
@@ -206,90 +289,81 @@ def promote(name: str, dtypes: Sequence[str]) -> str:
     cases Kernel IR leaves implicit: combine programs, whose arguments share one dtype)."""
     if name in COMPARE:
         return "bool"
-    ds = list(dict.fromkeys(dtypes))
-    if len(ds) == 1:
-        return ds[0]
-    floats = [d for d in ds if d != "bool" and is_float(d)]
+    distinct = list(dict.fromkeys(dtypes))
+    if len(distinct) == 1:
+        return distinct[0]
+    floats = {d for d in distinct if d != "bool" and is_float(d)}
+    if floats == {"f16", "bf16"}:
+        return "f32"
     if floats:
-        order = ["f16", "bf16", "f32", "f64"]
-        best = max(floats, key=order.index)
-        if set(floats) == {"f16", "bf16"}:
-            return "f32"
-        return best
-    ints = [d for d in ds if d != "bool"]
+        return max(floats, key=_FLOAT_RANK.index)
+    ints = [d for d in distinct if d != "bool"]
     return max(ints, key=size) if ints else "bool"
 
 
-def apply(k: Kernel, name: str, args: Sequence[Val], dtype: str) -> Val:
-    """name(args) at result ``dtype`` under Emmy's rule: native where Emmy computes there,
-    otherwise in f32, converted once."""
-    name, typ = canonical(name), reg_type(dtype)
-    at, fn = dtype, None
-    if typ == "f16" and all(a.dtype == dtype for a in args):
-        fn = F16_OPS.get(name)
-    elif is_int(dtype) and all(is_int(a.dtype) for a in args) and name in INT_OPS:
-        fn = partial(_int_op, name, typ)
-    elif dtype == "f64":
-        fn = F64_OPS.get(name)
-    if fn is None:
-        at, fn = "f32", F32_OPS.get(name) or fastmath.F32_FUNCS.get(name)
-    if fn is None:
-        raise NotImplementedError(f"{at} op {name}")
-    arity = 2 if name in BINARY else 1
-    if len(args) != arity:
-        raise ValueError(f"{at} op {name} takes {arity} argument(s), got {len(args)}")
-    out = fn(k, *(convert(k, a, at).reg for a in args))
-    return convert(k, Val(out, at), dtype)
+def _compare(k: Kernel, name: str, args: Sequence[Val], dtype: str) -> Val:
+    x, y = (convert(k, v, "f32").reg for v in args)
+    return convert(k, Val(k.pure(f"setp.{COMPARE[name]}.f32", "pred", x, y), "bool"), dtype)
+
+
+def _where(k: Kernel, name: str, args: Sequence[Val], dtype: str) -> Val:
+    cond = convert(k, args[0], "bool").reg
+    x, y = (convert(k, v, dtype).reg for v in args[1:])
+    return select(k, cond, x, y, dtype)
+
+
+def _logic(k: Kernel, name: str, args: Sequence[Val], dtype: str) -> Val:
+    preds = [convert(k, v, "bool").reg for v in args]
+    opcode = {"logical_and": "and.pred", "logical_or": "or.pred", "logical_not": "not.pred"}
+    return convert(k, Val(k.pure(opcode[name], "pred", *preds), "bool"), dtype)
+
+
+def _copy(k: Kernel, name: str, args: Sequence[Val], dtype: str) -> Val:
+    return convert(k, args[0], dtype)
+
+
+_STRUCTURAL: dict[str, Callable[[Kernel, str, Sequence[Val], str], Val]] = {
+    **dict.fromkeys(COMPARE, _compare), "where": _where,
+    **dict.fromkeys(("logical_and", "logical_or", "logical_not"), _logic),
+    **dict.fromkeys(("copy", "pad", "identity", "cast", "to"), _copy),
+}
 
 
 def assign(k: Kernel, name: str, dtype: str | None, args: Sequence[Val]) -> Val:
-    """The value of an Assign of op ``name`` over ``args`` (compares compute in f32)."""
+    """The value of an Assign of op ``name`` over ``args``: compares (in f32), selects, logic
+    and copies by their own rules, every other op through ``apply``."""
     name = canonical(name)
-    dtype = dtype if dtype is not None else promote(name, [v.dtype for v in args])
-    if name in COMPARE:
-        x, y = (convert(k, v, "f32").reg for v in args)
-        p = Val(k.pure(f"setp.{COMPARE[name]}.f32", "pred", x, y), "bool")
-        return convert(k, p, dtype)
-    if name == "where":
-        cond = convert(k, args[0], "bool").reg
-        x, y = (convert(k, v, dtype).reg for v in args[1:])
-        return select(k, cond, x, y, dtype)
-    if name in ("logical_and", "logical_or"):
-        x, y = (convert(k, v, "bool").reg for v in args)
-        op = "and.pred" if name == "logical_and" else "or.pred"
-        return convert(k, Val(k.pure(op, "pred", x, y), "bool"), dtype)
-    if name == "logical_not":
-        x = convert(k, args[0], "bool").reg
-        return convert(k, Val(k.pure("not.pred", "pred", x), "bool"), dtype)
-    if name in ("copy", "pad", "identity", "cast", "to"):
-        return convert(k, args[0], dtype)
+    if dtype is None:
+        dtype = promote(name, [v.dtype for v in args])
+    handler = _STRUCTURAL.get(name)
+    if handler is not None:
+        return handler(k, name, args, dtype)
     return apply(k, name, args, dtype)
 
 
-# --- shuffles -------------------------------------------------------------------------------
+# --- shuffles --------------------------------------------------------------------------------
 
 
 def shfl(k: Kernel, x: str, typ: str, mode: str, lane: str | int, clamp: int, mask: str) -> str:
-    """One ``shfl.sync`` of ``x``: 64-bit values move as two halves, 16-bit ones widen."""
+    """One ``shfl.sync`` of ``x``. The instruction moves 32-bit words: a 64-bit value moves as
+    its two halves, a 16-bit value widened to a word, a predicate as a 0/1 word."""
 
-    def one(v: str, t: str) -> str:
-        out = k.reg(t)
-        k.emit(f"shfl.sync.{mode}.b32", (out,), (v, str(lane), str(clamp), mask))
+    def move(word: str, word_typ: str = "u32") -> str:
+        out = k.reg(word_typ)
+        k.emit(f"shfl.sync.{mode}.b32", (out,), (word, str(lane), str(clamp), mask))
         return out
 
+    if typ == "pred":
+        word = move(k.pure("selp.u32", "u32", "1", "0", x))
+        return k.pure("setp.ne.u32", "pred", word, "0")
     if size(typ) == 4:
-        return one(x, typ)
-    out = k.reg(typ)
+        return move(x, typ)
+    out = k.reg(typ)  # the result's register, filled from the moved words
     if size(typ) == 8:
-        lo, hi = k.reg("u32"), k.reg("u32")
-        k.emit("mov.b64", (f"{{{lo}, {hi}}}",), (x,))
-        a, b = one(lo, "u32"), one(hi, "u32")
-        k.emit("mov.b64", (out,), (f"{{{a}, {b}}}",))
-    elif typ == "pred":
-        w = k.pure("selp.u32", "u32", "1", "0", x)
-        r = one(w, "u32")
-        return k.pure("setp.ne.u32", "pred", r, "0")
+        halves = (k.reg("u32"), k.reg("u32"))
+        k.emit("mov.b64", (f"{{{halves[0]}, {halves[1]}}}",), (x,))
+        moved = [move(h) for h in halves]
+        k.emit("mov.b64", (out,), (f"{{{moved[0]}, {moved[1]}}}",))
     else:
-        wide = k.pure("cvt.u32.u16", "u32", x)
-        k.emit("cvt.u16.u32", (out,), (one(wide, "u32"),))
+        k.emit("cvt.u16.u32", (out,), (move(k.pure("cvt.u32.u16", "u32", x)),))
     return out

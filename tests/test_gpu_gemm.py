@@ -3,8 +3,10 @@ operands (and against the oracle's run of the SIMT IR it replaces), split-K, odd
 and the bounded-wait give-up path.
 
 Bar: the tensor cores accumulate in f32 in their own order, so results are not bit-equal to the
-SIMT nest; the bound is rel 1e-2 on each element with an absolute floor of 1e-3 of the largest
-|C| (the north-star bound for bf16 GEMM with f32 accumulation); the observed error is reported.
+SIMT nest; the bound is rel 1e-2 on each element (the north-star bound for bf16 GEMM with f32
+accumulation) with an absolute floor of 1e-4 of the largest |C|, for elements near zero, whose
+relative error an f32 sum of K products does not bound. Measured on a B200, the largest error is
+1e-7..1.3e-6 of max |C| for these cases and about 9e-6 at K = 8192 and 65536; it is printed.
 """
 
 from __future__ import annotations
@@ -33,7 +35,7 @@ def operands(spec: problems.ProblemSpec, ins: dict[str, np.ndarray]) -> tuple[np
 def assert_gemm_close(got: np.ndarray, want: np.ndarray) -> float:
     err = np.abs(got.astype(np.float64) - want)
     scale = np.abs(want).max()
-    bad = err > 1e-2 * np.abs(want) + 1e-3 * scale
+    bad = err > 1e-2 * np.abs(want) + 1e-4 * scale
     assert not bad.any(), f"{bad.sum()} elements off; max err {err.max():.3e} (|C| max {scale:.3e})"
     return float(err.max() / scale)
 
