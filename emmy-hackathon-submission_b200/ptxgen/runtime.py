@@ -26,7 +26,8 @@ import numpy as np
 
 from .build import LIB
 
-_NOTE = re.compile(r"^// @ptxgen (\w+) (.*)$", re.M)
+# "// @ptxgen <key> <fields>" or "// @ptxgen <key>=<value>" (dynamic_smem=N)
+_NOTE = re.compile(r"^// @ptxgen (\w+)[ =](.*)$", re.M)
 _DTYPE_CODE = {"u8": 0, "f16": 1, "bf16": 2, "f32": 3}
 
 
@@ -142,6 +143,7 @@ class Module:
         _check(library().pg_module_load(ptx.encode(), ctypes.byref(handle)), "pg_module_load")
         self.handle = handle
         self.tensormaps = [TensorMapNote.parse(t) for t in self.notes.get("tensormap", [])]
+        self._filled: tuple[int, ...] | None = None  # the buffer addresses the maps describe
         launch = _kv(self.notes["launch"][0]) if "launch" in self.notes else {}
         self.grid = int(launch["grid"]) if "grid" in launch else None
         self.block = int(launch["block"]) if "block" in launch else None
@@ -160,7 +162,14 @@ class Module:
         return Kernel(self, handle, entry)
 
     def fill_tensormaps(self, pointers: dict[str, int]) -> None:
-        """Write every tensor map the module names, over the buffers at ``pointers``."""
+        """Write every tensor map the module names, over the buffers at ``pointers``. The
+        maps are written only when an address differs from the last call's, so a launch on the
+        same buffers costs no call into the library (a rewrite waits for the device to idle)."""
+        if not self.tensormaps:
+            return
+        now = tuple(pointers[t.buffer] for t in self.tensormaps)
+        if now == self._filled:
+            return
         lib = library()
         for t in self.tensormaps:
             rank = len(t.dims)
@@ -170,6 +179,7 @@ class Module:
             _check(lib.pg_tensormap_fill(self.handle, t.symbol.encode(), _DTYPE_CODE[t.dtype],
                                          rank, pointers[t.buffer], dims, strides, box,
                                          t.swizzle), f"pg_tensormap_fill({t.symbol})")
+        self._filled = now
 
     def write_global(self, symbol: str, data: bytes) -> None:
         """Copy ``data`` into the module's ``.global`` symbol (at most its size)."""

@@ -22,8 +22,13 @@ i * nctaid``, so any grid size computes every tile once):
   the stage's shared-memory descriptors, ``tcgen05.commit``s each stage back to its ``empty``
   barrier and each finished tile to the accumulator's ``tmem_full`` barrier;
 * warps 4-7 -- epilogue: ``tcgen05.ld`` (32 lanes x 32 columns per load) of the finished
-  accumulator, stores into C (``red.global.add.v4.f32`` for split-K), then ``tmem_empty``; with
-  two accumulators the epilogue of one tile overlaps the MMAs of the next.
+  accumulator; each warp writes its 32 x 32 block into one of its two shared-memory staging
+  buffers (128-byte swizzled, so the stores are conflict-free), fences it to the async proxy,
+  and one lane writes the whole block into C with a single TMA op (``cp.async.bulk.tensor``
+  store, or ``cp.reduce.async.bulk.tensor`` add for split-K: whole 128-byte lines, where a
+  per-thread ``red.global.add.v4`` touches 32 rows per instruction); then ``tmem_empty``. With
+  two accumulators the epilogue of one tile overlaps the MMAs of the next. The tensor map over
+  C covers this GPU's own buffer only, and no load multicasts.
 
 The work is a table of segments baked into the module: (m tile, n tile, first K block, K-block
 count), and CTA ``c`` takes entries ``c, c + nctaid, ...``. A plain GEMM has one whole-K segment
@@ -39,7 +44,10 @@ zeroed C); only the f32 association differs, as it does between atomic orders. T
 parameters stay the plain device pointers of meta.json's arg_order. Every mbarrier wait is
 bounded by ``%globaltimer``; a wait that runs out sets a bit of the module's ``ptxgen_status``
 word, and the kernel winds down: the producer waits (bounded) for its own TMA loads to land, the
-MMA thread for its MMAs, then TMEM is freed. Every CTA loads its own tiles.
+MMA thread for its MMAs, the epilogue lanes for their TMA writes, then TMEM is freed. Every CTA
+loads its own tiles. At entry the kernel compares ``%dynamic_smem_size`` with what its layout
+needs; a launch that granted less sets status bit ``SMEM_SHORT`` and every CTA returns before any
+barrier exists.
 """
 
 from __future__ import annotations
@@ -61,6 +69,10 @@ MIN_SEGMENT = 8  # K blocks a split-K segment has at least
 SEGMENT_COST = 2  # a segment's epilogue, in K blocks of MMA time, when choosing the split count
 EPILOGUE_WARPS = (4, 5, 6, 7)
 BAR_BYTES = 8
+SMEM_SHORT = 8  # status bit: the launch gave less dynamic shared memory than the layout needs
+SMEM_LIMIT = 232448  # dynamic shared memory one CTA may opt into on sm_100 (227 KiB)
+STAGE_BLOCK = 32  # rows and columns of the f32 block an epilogue warp stages per TMA op
+STAGE_BUF = STAGE_BLOCK * STAGE_BLOCK * 4  # 4 KiB: 32 rows of 128 bytes, 128-byte swizzled
 
 
 @dataclass(frozen=True)
@@ -81,6 +93,9 @@ class MatmulPlan:
     atomic: bool
     schedule: tuple[tuple[int, int, int], ...]  # (m tile, n tile, split) per tile index
     pair: bool = False  # two CTAs (an SM pair) per 256-row tile, cta_group::2
+    # the epilogue stages each warp's 32 x 32 blocks of C in shared memory and writes them
+    # with one TMA op each (a reduce-add for split-K); False: per-thread global stores/reds
+    staged: bool = True
 
     @property
     def kc(self) -> int:
@@ -441,9 +456,13 @@ def emit(p: MatmulPlan) -> str:
     b_chunk = BK * 64 * 2  # 8 KiB: 64 K rows x 64 columns
     b_stage = BK * nb * 2
     stages = MAX_STAGES if pair else p.stages
+    staging = 2 * STAGE_BUF * len(EPILOGUE_WARPS) if p.staged else 0
+    while stages > 2 and 1024 + stages * (a_stage + b_stage) + staging + 256 > SMEM_LIMIT:
+        stages -= 1  # the staging buffers take the place of a stage where both do not fit
     stage_tx = g * (a_stage + b_stage)  # bytes the MMA's full barrier waits for
     b_off = stages * a_stage
-    bar_off = stages * (a_stage + b_stage)
+    epi_off = stages * (a_stage + b_stage)  # 1024-byte aligned: whole stages before it
+    bar_off = epi_off + staging
     full, empty = 0, stages * BAR_BYTES
     tfull = 2 * stages * BAR_BYTES
     tempty = tfull + 2 * BAR_BYTES
@@ -522,11 +541,25 @@ def emit(p: MatmulPlan) -> str:
     x(f"mov.u32 {r('smem')}, smem_pool;")
     x("add.u32 %smem, %smem, 1023;")
     x("and.b32 %smem, %smem, -1024;")  # stages need 1024-byte alignment (128-byte swizzle)
+    # the launch must have granted the whole layout; otherwise every CTA leaves at once (before
+    # any barrier or TMEM exists), with a status bit, instead of touching memory past its end
+    x(f"mov.u32 {r('dyn')}, %dynamic_smem_size;")
+    x(f"mov.u32 {r('dyn_end')}, smem_pool;")
+    x("add.u32 %dyn_end, %dyn_end, %dyn;")
+    x(f"add.u32 {r('dyn_need')}, %smem, {bar_off + slot + 8};")
+    x(f"setp.gt.u32 {r('pshort', pred)}, %dyn_need, %dyn_end;")
+    x(f"setp.eq.u32 {r('pshort0', pred)}, %tid, 0;")
+    x("and.pred %pshort0, %pshort0, %pshort;")
+    x(f"@%pshort0 red.global.or.b32 [ptxgen_status], {1 << SMEM_SHORT};")
+    x("@%pshort ret;")
     x(f"add.u32 {r('bars')}, %smem, {bar_off};")
     x(f"mov.u64 {r('tmap_a', u64)}, {e}_tmap_a;")
     x("cvta.global.u64 %tmap_a, %tmap_a;")
     x(f"mov.u64 {r('tmap_b', u64)}, {e}_tmap_b;")
     x("cvta.global.u64 %tmap_b, %tmap_b;")
+    if p.staged:
+        x(f"mov.u64 {r('tmap_c', u64)}, {e}_tmap_c;")
+        x("cvta.global.u64 %tmap_c, %tmap_c;")
     x(f"mov.u64 %sched, {e}_sched;")
     x(f"setp.eq.u32 {r('p', pred)}, %tid, 0;")
     init_done = x.label("init_done")
@@ -543,6 +576,8 @@ def emit(p: MatmulPlan) -> str:
     x("fence.proxy.async.shared::cta;")
     x("prefetch.tensormap [%tmap_a];")
     x("prefetch.tensormap [%tmap_b];")
+    if p.staged:
+        x("prefetch.tensormap [%tmap_c];")
     x(f"{init_done}:")
     alloc_done = x.label("alloc_done")
     x("setp.eq.u32 %p, %warp, 1;")
@@ -717,9 +752,43 @@ def emit(p: MatmulPlan) -> str:
     x(f"bra.uni {teardown};")
 
     # --- epilogue: TMEM -> registers -> C ------------------------------------------------------
+    vals = [r(f"v{i}", "b32") for i in range(32)]
+    tma_out = ("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group"
+               if p.atomic else "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group")
+
+    def stage_block(chunk: int) -> None:
+        """The warp's 32 x 32 block (each lane one row, in %v0..%v31) into its staging buffer
+        ``chunk & 1``, then one TMA op of the whole block into C: rows srow.., columns
+        scol + 32*chunk... Lane 0 first waits until the TMA op issued two blocks ago has read
+        that buffer. Lane L writes its row's 16-byte piece j at piece j ^ (L & 7) of row L (the
+        128-byte swizzle the tensor map names), so the 8 lanes of each quarter-warp store to
+        all 32 banks at once."""
+        buf, lane_base = (("%sb1", "%sbuf1") if chunk & 1 else ("%sb0", "%sbuf0"))
+        x("@%plane0 cp.async.bulk.wait_group.read 1;")
+        x("bar.warp.sync -1;")
+        for j in range(8):
+            x(f"xor.b32 {r('saddr')}, {lane_base}, {j * 16};")
+            x(f"st.shared.v4.b32 [%saddr], {{{', '.join(vals[4 * j:4 * j + 4])}}};")
+        x("fence.proxy.async.shared::cta;")  # the generic stores, before the TMA reads them
+        x("bar.warp.sync -1;")
+        x(f"add.u32 {r('sx')}, %scol, {chunk * STAGE_BLOCK};")
+        x(f"@%plane0 {tma_out} [%tmap_c, {{%sx, %srow}}], [{buf}];")
+        x("@%plane0 cp.async.bulk.commit_group;")
+
     x(f"{epi}:")
     x(f"sub.u32 {r('quad')}, %warp, {EPILOGUE_WARPS[0]};")
     x(f"shl.b32 {r('lanebase')}, %quad, 21;")  # TMEM lane (quad*32) in bits 16..31
+    if p.staged:
+        # two staging buffers per warp after the stage ring; each lane's swizzled row base
+        x(f"mad.lo.u32 {r('sb0')}, %quad, {2 * STAGE_BUF}, %smem;")
+        x(f"add.u32 %sb0, %sb0, {epi_off};")
+        x(f"add.u32 {r('sb1')}, %sb0, {STAGE_BUF};")
+        x(f"and.b32 {r('sswz')}, %lane, 7;")
+        x("shl.b32 %sswz, %sswz, 4;")
+        x(f"mad.lo.u32 %sswz, %lane, {STAGE_BLOCK * 4}, %sswz;")
+        x(f"add.u32 {r('sbuf0')}, %sb0, %sswz;")
+        x(f"add.u32 {r('sbuf1')}, %sb1, %sswz;")
+        x(f"setp.eq.u32 {r('plane0', pred)}, %lane, 0;")
     for n in ("tc", "ab", "aph"):
         x(f"mov.u32 %{n}, 0;")
     x("mov.u32 %t, %cta;")
@@ -739,20 +808,27 @@ def emit(p: MatmulPlan) -> str:
         x(f"mad.lo.u32 %m0, %mt, {g * BM}, %half;")
     else:
         x("shl.b32 %m0, %mt, 7;")
-    x(f"mad.lo.u32 {r('row')}, %quad, 32, %lane;")
-    x("add.u32 %row, %row, %m0;")
-    x(f"mul.wide.u32 {r('crow', u64)}, %row, {p.n * 4};")
-    x(f"mul.lo.u32 %n0, %nt, {p.bn * 4};")
-    x(f"cvt.u64.u32 {r('ncol64', u64)}, %n0;")
-    x("add.s64 %crow, %crow, %ncol64;")
-    x("add.s64 %crow, %crow, %c_ptr;")
     x(f"add.u32 {r('taddr')}, %tmem, %lanebase;")
     x(f"mad.lo.u32 %taddr, %ab, {p.bn}, %taddr;")
-    vals = [r(f"v{i}", "b32") for i in range(32)]
+    if p.staged:
+        # this warp's rows of C start at m0 + quad*32; its blocks at columns nt*BN + 32*chunk
+        x(f"mad.lo.u32 {r('srow')}, %quad, {STAGE_BLOCK}, %m0;")
+        x(f"mul.lo.u32 {r('scol')}, %nt, {p.bn};")
+    else:
+        x(f"mad.lo.u32 {r('row')}, %quad, 32, %lane;")
+        x("add.u32 %row, %row, %m0;")
+        x(f"mul.wide.u32 {r('crow', u64)}, %row, {p.n * 4};")
+        x(f"mul.lo.u32 %n0, %nt, {p.bn * 4};")
+        x(f"cvt.u64.u32 {r('ncol64', u64)}, %n0;")
+        x("add.s64 %crow, %crow, %ncol64;")
+        x("add.s64 %crow, %crow, %c_ptr;")
     for chunk in range(p.bn // 32):
         x(f"add.u32 {r('tcol')}, %taddr, {chunk * 32};")
         x(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(vals)}}}, [%tcol];")
         x("tcgen05.wait::ld.sync.aligned;")
+        if p.staged:
+            stage_block(chunk)
+            continue
         for j in range(8):
             quad = ", ".join(vals[4 * j:4 * j + 4])
             off = chunk * 128 + j * 16
@@ -775,6 +851,8 @@ def emit(p: MatmulPlan) -> str:
 
     # --- teardown ----------------------------------------------------------------------------
     x(f"{teardown}:")
+    if p.staged:  # the epilogue's TMA ops have finished with its staging buffers
+        x("cp.async.bulk.wait_group 0;")
     x("tcgen05.fence::before_thread_sync;")
     cta_sync()
     x("setp.ne.u32 %p, %warp, 1;")
@@ -804,6 +882,8 @@ def emit(p: MatmulPlan) -> str:
         f"dims={p.k},{p.m} strides={p.k * esz} box={BK},{BM} swizzle=128",
         f"// @ptxgen tensormap symbol={e}_tmap_b buffer={p.b} dtype={p.dtype} "
         f"dims={p.n},{p.k} strides={p.n * esz} box=64,{BK} swizzle=128",
+        *([f"// @ptxgen tensormap symbol={e}_tmap_c buffer={p.c} dtype=f32 dims={p.n},{p.m} "
+           f"strides={p.n * 4} box={STAGE_BLOCK},{STAGE_BLOCK} swizzle=128"] if p.staged else []),
         f"// @ptxgen matmul m={p.m} n={p.n} k={p.k} bn={p.bn} splits={p.splits} "
         f"stages={stages} tiles={p.tiles} segments={entries} cta_group={g}",
         "",
@@ -811,6 +891,7 @@ def emit(p: MatmulPlan) -> str:
         ".extern .shared .align 1024 .b8 smem_pool[];",
         f".global .align 64 .b8 {e}_tmap_a[128];",
         f".global .align 64 .b8 {e}_tmap_b[128];",
+        *([f".global .align 64 .b8 {e}_tmap_c[128];"] if p.staged else []),
         ".global .align 4 .u32 ptxgen_status;",
         f".global .align 8 .u32 {e}_sched[{len(sched_words)}] = {{\n\t"
         + ",\n\t".join(rows) + "\n};",

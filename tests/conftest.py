@@ -49,15 +49,16 @@ def reference_inputs(meta: dict[str, Any]) -> dict[str, np.ndarray]:
 
 
 def gpu_run(graph: dict[str, Any], meta: dict[str, Any], inputs: dict[str, np.ndarray],
-            guard: int = 0, **flags: bool) -> dict[str, np.ndarray]:
-    """Compile, launch on cuda:0 through the C-ABI launcher, and return every output buffer
-    (bf16 as uint16 bits). With ``guard`` > 0 each output gets that many canary elements past
-    its end, and the test fails if the kernel touched them."""
+            guard: int = 0, ptx: str = "", **flags: bool) -> dict[str, np.ndarray]:
+    """Compile (or take the given ``ptx`` module), launch on cuda:0 through the C-ABI
+    launcher, and return every output buffer (bf16 as uint16 bits). With ``guard`` > 0 each
+    output gets that many canary elements past its end, and the test fails if the kernel
+    touched them."""
     import torch
 
     from ptxgen.runtime import Problem
 
-    prob = Problem(graph, meta, flags=flags)
+    prob = Problem(graph, meta, ptx=ptx, flags=flags)
     tensors = prob.allocate(extra_guard=guard)
     launch = prob.launch_entry
     for a in launch["args"]:

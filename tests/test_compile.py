@@ -55,10 +55,21 @@ TMA_LOAD = re.compile(r"^\s*cp\.async\.bulk\.tensor\.2d\.(shared::cluster\.globa
                       r"\[%\w+\];$")
 
 
+# The staged GEMM epilogue's TMA ops: one lane writes a block of this CTA's shared memory into
+# C (a store, or a reduce-add for split-K), and waits for its own bulk groups.
+TMA_OUT = re.compile(r"^\s*@%\w+ cp\.(reduce\.async\.bulk\.tensor\.2d\.global\.shared::cta\.add|"
+                     r"async\.bulk\.tensor\.2d\.global\.shared::cta)\.tile\.bulk_group "
+                     r"\[%\w+, \{%\w+, %\w+\}\], \[%\w+\];$")
+BULK_GROUP = re.compile(r"^\s*(@%\w+ )?cp\.async\.bulk\.(commit_group|wait_group(\.read)? \d);$")
+
+
 def assert_plain_tma(ptx: str) -> None:
     for line in ptx.splitlines():
-        if "cp.async.bulk" in line:
-            assert TMA_LOAD.match(line), f"unexpected bulk-copy form: {line.strip()}"
+        if "cp.async.bulk" in line or "cp.reduce.async.bulk" in line:
+            assert TMA_LOAD.match(line) or TMA_OUT.match(line) or BULK_GROUP.match(line), \
+                f"unexpected bulk-copy form: {line.strip()}"
+        assert "multicast::cluster" not in line or line.lstrip().startswith("tcgen05.commit"), \
+            f"multicast outside tcgen05.commit: {line.strip()}"
 
 
 SMALL = {
@@ -193,11 +204,12 @@ def test_gemm_uses_the_tcgen05_template() -> None:
     # 256-row tiles on SM pairs: one A and two B loads (this CTA's half of B) a stage
     assert "tcgen05.mma.cta_group::2.kind::f16" in ptx and "tcgen05.alloc.cta_group::2" in ptx
     assert ".reqnctapercluster 2, 1, 1" in ptx and "cluster=2" in ptx
-    assert ptx.count("cp.async.bulk.tensor") == 1 + 128 // 64
+    loads = "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global"
+    assert ptx.count(loads) == 1 + 128 // 64
     # an odd number of 128-row tiles keeps one SM per tile: one A and four B loads a stage
     single = compile_spec(problems.matmul(384, 512, 512))
     assert "tcgen05.mma.cta_group::1.kind::f16" in single and ".reqnctapercluster" not in single
-    assert single.count("cp.async.bulk.tensor") == 1 + 256 // 64
+    assert single.count("cp.async.bulk.tensor.2d.shared::cluster.global") == 1 + 256 // 64
     assert_plain_tma(single)
     assert "// @ptxgen tensormap symbol=" in ptx and "persistent=1" in ptx
     assert_plain_tma(ptx)
@@ -229,6 +241,55 @@ def test_gemm_epilogue_wait_is_warp_uniform(tmp_path) -> None:
     for warp in (False, True):
         for arrive in (False, True):
             ptxas(wait_probe_ptx(1000, warp=warp, arrive=arrive), tmp_path)
+
+
+def test_gemm_staged_epilogue_structure(tmp_path) -> None:
+    """The staged epilogue: C's tensor map (f32, 32 x 32 box, 128-byte swizzle) beside A's and
+    B's; per block, lane 0 waits for the buffer's previous TMA read, the warp stores and fences
+    the generic stores to the async proxy before lane 0's TMA op (a reduce-add for split-K, a
+    store otherwise); the teardown waits for every bulk group; shared memory fits the limit."""
+    import re
+
+    from ptxgen.templates.matmul import SMEM_LIMIT
+
+    for key, op in (("c5b_matmul_splitk", "cp.reduce.async.bulk.tensor.2d.global.shared::cta"
+                     ".add.tile.bulk_group"),
+                    ("c5_matmul", "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group")):
+        ptx = compile_spec(problems.CONFIGS[key]())
+        note = next(ln for ln in ptx.splitlines() if "_tmap_c" in ln and "@ptxgen" in ln)
+        assert "dtype=f32" in note and "box=32,32" in note and "swizzle=128" in note
+        epi = ptx[ptx.index("$M_epilogue:"):ptx.index("$M_teardown:")]
+        assert epi.count(op) == 8 and "red.global.add" not in epi and "st.global" not in epi
+        first = epi.index("cp.async.bulk.wait_group.read 1")
+        assert first < epi.index("st.shared.v4.b32") < epi.index("fence.proxy.async.shared::cta")
+        assert epi.index("fence.proxy.async.shared::cta") < epi.index(op)
+        tail = ptx[ptx.index("$M_teardown:"):]
+        assert tail.index("cp.async.bulk.wait_group 0") < tail.index("tcgen05.dealloc")
+        smem = int(re.search(r"dynamic_smem=(\d+)", ptx).group(1))
+        assert smem <= SMEM_LIMIT
+        assert_plain_tma(ptx)
+        ptxas(ptx, tmp_path)
+
+
+def test_launch_notes_give_the_module_its_shared_memory() -> None:
+    """Every ``// @ptxgen`` note the runtime reads parses, ``dynamic_smem=N`` included: a
+    launch asks for the larger of meta.json's ``smem_bytes`` and the module's own figure (the
+    GEMM template's layout is larger than meta.json's 198,656 bytes), and the template checks
+    at entry that it got what its layout needs."""
+    import re
+
+    from ptxgen.runtime import header_notes
+    from ptxgen.templates.matmul import SMEM_SHORT
+
+    spec = problems.CONFIGS["c5b_matmul_splitk"]()
+    ptx = compile_spec(spec)
+    notes = header_notes(ptx)
+    want = int(re.search(r"// @ptxgen dynamic_smem=(\d+)", ptx).group(1))
+    assert int(notes["dynamic_smem"][0]) == want > int(spec.kernel["smem_bytes"])
+    assert {"launch", "tensormap", "matmul"} <= set(notes) and len(notes["tensormap"]) == 3
+    assert "%dynamic_smem_size" in ptx and f"[ptxgen_status], {1 << SMEM_SHORT}" in ptx
+    head = ptx[:ptx.index("mbarrier.init")]
+    assert "ret;" in head  # a short launch leaves before any barrier exists
 
 
 def gemm_plan(spec: problems.ProblemSpec):

@@ -59,15 +59,39 @@ CASES = {
 }
 
 
+def template_ptx(spec: problems.ProblemSpec, staged: bool) -> str:
+    """The GEMM template's module for ``spec`` with the chosen epilogue: staged (each warp's
+    32 x 32 blocks through shared memory, one TMA store or reduce-add per block; the default)
+    or per thread (``st.global.v4`` / ``red.global.add.v4`` from registers)."""
+    import dataclasses
+
+    from ptxgen.compiler import kernel_for_meta
+    from ptxgen.lower import Buffer
+    from ptxgen.templates import matmul
+
+    op, launch = kernel_for_meta(Graph.from_dict(spec.graph), spec.meta)
+    bufs = {a["name"]: Buffer(tuple(a["shape"]), a["dtype"],
+                              bool(a.get("output")) or a["name"] in op.outputs)
+            for a in launch["args"]}
+    plan = matmul.match(op, bufs, launch["arg_order"], launch["block"][0],
+                        int(launch.get("smem_bytes", 0)))
+    assert plan is not None
+    return matmul.emit(dataclasses.replace(plan, staged=staged))
+
+
+@pytest.mark.parametrize("staged", [True, False], ids=["staged", "per_thread"])
 @pytest.mark.parametrize("key", sorted(CASES))
-def test_tcgen05_gemm(cuda, key: str) -> None:
+def test_tcgen05_gemm(cuda, key: str, staged: bool) -> None:
     spec = CASES[key]()
-    assert "tcgen05.mma" in to_ptx(Graph.from_dict(spec.graph), spec.meta)
+    ptx = template_ptx(spec, staged)
+    assert "tcgen05.mma" in ptx and ("_tmap_c" in ptx) == staged
+    if staged:
+        assert ptx == to_ptx(Graph.from_dict(spec.graph), spec.meta)  # the default form
     ins = reference_inputs(spec.meta)
-    got = gpu_run(spec.graph, spec.meta, ins, guard=64)["matmul"]
+    got = gpu_run(spec.graph, spec.meta, ins, guard=64, ptx=ptx)["matmul"]
     a, b = operands(spec, ins)
     worst = assert_gemm_close(got, a @ b)
-    print(f"{key}: max |err| / max |C| = {worst:.3e}")
+    print(f"{key} ({'staged' if staged else 'per thread'}): max |err| / max |C| = {worst:.3e}")
 
 
 def test_tcgen05_matches_oracle_small(cuda) -> None:
@@ -119,12 +143,14 @@ def test_bounded_wait(cuda, warp: bool, arrive: bool) -> None:
 
 def test_launcher_times_launches(cuda) -> None:
     """``pg_kernel_time`` (CUDA events around each launch) agrees with PyTorch's events on the
-    same back-to-back launches of the config-5 template, within a factor of 1.5."""
+    same back-to-back launches of the config-5 template, within a factor of 1.5. The GEMM is
+    large enough (4096 x 4096 x 2048, tens of microseconds) that the GPU, not the host's
+    enqueueing, sets the pace of the PyTorch-timed loop."""
     import torch
 
     from ptxgen.runtime import Problem
 
-    spec = problems.matmul(1024, 1024, 1024)
+    spec = problems.matmul(4096, 4096, 2048)
     prob = Problem(spec.graph, spec.meta)
     tensors = prob.allocate()
     for t in tensors.values():
