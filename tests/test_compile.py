@@ -68,7 +68,8 @@ def assert_plain_tma(ptx: str) -> None:
         if "cp.async.bulk" in line or "cp.reduce.async.bulk" in line:
             assert TMA_LOAD.match(line) or TMA_OUT.match(line) or BULK_GROUP.match(line), \
                 f"unexpected bulk-copy form: {line.strip()}"
-        assert "multicast::cluster" not in line or line.lstrip().startswith("tcgen05.commit"), \
+        # the only multicast form allowed is tcgen05.commit's arrival on both CTAs of a pair
+        assert "multicast" not in line or line.lstrip().startswith("tcgen05.commit"), \
             f"multicast outside tcgen05.commit: {line.strip()}"
 
 
