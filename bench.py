@@ -7,8 +7,9 @@ configuration's Tile axis (``ptxgen.shard``), and only the full sum all-reduces 
 
 A step is one launch of the workload's kernel over its whole (per-rank) input, compiled from
 Kernel IR by this repository's compiler and launched through its C-ABI launcher, with the inputs
-already resident in HBM. L2 is flushed (a 256 MiB write) before every timed step, outside the
-kernel's CUDA events. The printed ``value`` is the whole job's algorithmic bytes (or flops) per
+already resident in HBM. L2 is flushed before every timed step, outside the kernel's CUDA
+events: a 256 MiB write, then a 256 MiB read, so no input line is in L2 and the flush's own dirty
+lines are written back before the step starts (``--l2``). The printed ``value`` is the whole job's algorithmic bytes (or flops) per
 second over the slowest rank's mean kernel time; ``e2e`` is the same metric through the one-call
 host-buffer path (``pg_run_host``: page-locked inputs copied in, launch, result copied out;
 two steps in flight on two streams).
@@ -56,12 +57,14 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--share", type=int, default=1,
                    help="on one GPU, run one share of a K-way strong split of the workload (a "
                         "smaller case of the same kernel, e.g. for a profiler capture)")
-    p.add_argument("--l2", choices=("write", "clean", "none"), default="write",
-                   help="write: flush L2 with a 256 MiB write before each timed step, leaving it "
-                        "full of dirty lines the next kernel writes back; clean: follow that write "
-                        "with a 256 MiB read, so L2 holds clean unrelated lines; none: no flush, "
-                        "steps back to back over inputs larger than L2 (each step writes back "
-                        "the previous step's dirty lines, the steady state)")
+    p.add_argument("--l2", choices=("clean", "write", "none"), default="clean",
+                   help="clean (default): flush L2 before each timed step with a 256 MiB write "
+                        "followed by a 256 MiB read, so no input line is in L2 and the flush's "
+                        "own dirty lines are written back before the step starts; write: the "
+                        "write alone, which leaves L2 full of dirty lines that the timed kernel "
+                        "then writes back (up to 126 MB charged to it); none: no flush, steps "
+                        "back to back over inputs larger than L2 (each step writes back the "
+                        "previous step's dirty lines, the steady state)")
     p.add_argument("--ablation", action="store_true",
                    help="instead of the benchmark: time the reference's shipped example kernels "
                         "under each compiler flag (its published ablation tables), one JSON line")
@@ -348,13 +351,15 @@ def check_output(name: str, plan: Any, tensors: dict[str, Any], world: int) -> d
 
 
 L2_MODES = {
-    "write": "flushed (256 MiB write) before every timed step",
-    "clean": "flushed (256 MiB write, then a 256 MiB read: clean) before every timed step",
+    "clean": "flushed before every timed step: a 256 MiB write, then a 256 MiB read (no input "
+             "line in L2, and the flush's dirty lines written back before the step)",
+    "write": "flushed (256 MiB write) before every timed step; the timed kernel writes back the "
+             "flush's dirty lines",
     "none": "not flushed: inputs larger than L2 (126 MB), steps back to back in steady state",
 }
 
 
-def measure_kernel(plan: Any, steps: int, warmup: int, world: int, l2: str = "write",
+def measure_kernel(plan: Any, steps: int, warmup: int, world: int, l2: str = "clean",
                    via: str = "peer") -> dict[str, Any]:
     """Mean kernel time over ``steps`` timed launches (each after an L2 flush), the slowest
     rank's, with the launch count and NVML clocks of the timed region."""
