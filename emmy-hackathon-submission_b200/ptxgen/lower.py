@@ -22,6 +22,7 @@ predicate the ranges decide is a Python ``bool``. Semantics follow the reference
 from __future__ import annotations
 
 import math
+from typing import Any
 from collections.abc import Iterator, Mapping, Sequence
 from contextlib import AbstractContextManager, contextmanager, nullcontext
 from dataclasses import dataclass
@@ -34,7 +35,7 @@ from .ir import (Accum, Assign, BinaryExpr, CastExpr, Cond, CpAsyncCommit, CpAsy
                  Select, Smem, Stmt, StridedLoop, Sync, TernaryExpr, Tile, TreeHalve, Var,
                  WarpShuffle, Write, walk)
 from .ops import Val
-from .ptx import BUFFER_ALIGN, SM_COUNT, Kernel, pow2_part
+from .ptx import BUFFER_ALIGN, SM_COUNT, Ins, Kernel, pow2_part
 
 UNROLL_BUDGET = 6144  # instructions a loop may fully unroll to
 BODY_BUDGET = 768  # instructions the copies in one trip of a partly unrolled loop may hold
@@ -42,6 +43,7 @@ MAX_COPIES = 16
 NESTED_COPIES = 2
 STATIC_SMEM_CAP = 48 * 1024  # past this, shared buffers live in one dynamic pool
 MAX_IMM_OFFSET = 1 << 30  # larger constant byte offsets are added into the address register
+PREFETCH_TRIPS = 16  # how many trips ahead a single-wave runtime loop prefetches its loads
 BARRIERS = (Sync, WarpShuffle, TreeHalve, CpAsyncWait)
 F32_SYMBOL = {"+": "add", "-": "subtract", "*": "multiply", "/": "divide"}
 
@@ -905,11 +907,13 @@ class Lowering:
         with k.loop(entered=enters is True, counter=self._iv_counter(s, i),
                     step=const_step) as mark:
             k.place(top)
+            top_label = k.body[-1]
             for reg in written:
                 k.forget(reg)
             with self._block():
                 self.env[s.axis.name] = Aff.of(i)
                 self.body(s.body)
+        self._prefetch_ahead(mark, top_label, i, const_step, end_op)
         k.ranges.pop(i, None)
         again = k.reg("pred")
         for ptr, delta in mark.incs:
@@ -918,6 +922,30 @@ class Lowering:
         k.emit("setp.lt.s32", (again,), (i, end_op))
         k.emit("bra", src=(top,), pred=again, barrier=True)
         k.place(done)
+
+    def _prefetch_ahead(self, mark: Any, top_label: Any, i: str, step: int, end_op: str) -> None:
+        """In a single-wave kernel a runtime loop's trips wait on their own loads: one body per
+        trip, each load feeding that trip's arithmetic, and too few warps per SM to cover the
+        latency. So each read-only global load that walks an induction pointer is prefetched
+        into L1 ``PREFETCH_TRIPS`` trips ahead, at the top of the body, where the counter then
+        stands; the trip's own load then finds its line in L1. The prefetch is predicated on
+        that trip existing, so it never reaches past the loop's end. It moves no data into
+        registers and changes no result."""
+        k = self.k
+        if k.min_ctas != 1 or step <= 0 or not mark.incs:
+            return
+        start = next(n for n, ins in enumerate(k.body) if ins is top_label)
+        loaded = {ins.mem.addr for ins in k.body[start:]
+                  if ins.mem is not None and ins.mem.kind == "ld" and ins.mem.space == "global.nc"}
+        streams = [(ptr, delta) for ptr, delta in mark.incs if ptr in loaded]
+        if not streams:
+            return
+        ahead, exists = k.reg("u32"), k.reg("pred")
+        code = [Ins("add.u32", (ahead,), (i, str(PREFETCH_TRIPS * step))),
+                Ins("setp.lt.s32", (exists,), (ahead, end_op))]
+        code += [Ins("prefetch.global.L1", (), (f"[{ptr}+{PREFETCH_TRIPS * delta}]",), exists)
+                 for ptr, delta in streams]
+        k.body[start + 1:start + 1] = code
 
     def _trips(self, start: Aff, step: Aff, end: Aff, stmts: Sequence[Stmt]
                ) -> tuple[int, int] | None:

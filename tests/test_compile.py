@@ -293,6 +293,34 @@ def test_launch_notes_give_the_module_its_shared_memory() -> None:
     assert "ret;" in head  # a short launch leaves before any barrier exists
 
 
+def test_single_wave_runtime_loops_prefetch_ahead(tmp_path) -> None:
+    """The shipped r02 (one 128-thread block summing 65,536 floats) with unrolling off: its
+    rolled loop prefetches each trip's read-only load into L1 sixteen trips ahead, through the
+    same induction pointer plus sixteen trips' worth of bytes, predicated on that trip
+    existing. The default build unrolls instead and has no prefetch; neither has a grid of more
+    than one wave."""
+    import re
+
+    from ptxgen.lower import PREFETCH_TRIPS
+
+    graph, meta = shipped("r02_big_sum")
+    rolled = to_ptx(Graph.from_dict(graph), meta, no_unroll=True)
+    loop = rolled[rolled.index("$L_loop"):rolled.index("$L_loop_end")]
+    pf = re.search(r"@(%p\d+) prefetch\.global\.L1 \[(%rd\d+)\+(\d+)\];", loop)
+    assert pf is not None, loop
+    ld = re.search(r"ld\.global\.nc\.f32 %f\d+, \[(%rd\d+)\];", loop)
+    step = re.search(r"add\.s64 (%rd\d+), %rd\d+, (\d+);", loop)
+    assert ld.group(1) == pf.group(2) == step.group(1)
+    assert int(pf.group(3)) == PREFETCH_TRIPS * int(step.group(2))
+    guard = re.search(rf"setp\.lt\.s32 {re.escape(pf.group(1))}, %r\d+, (\d+);", loop)
+    assert guard is not None and guard.group(1) == "65536"
+    assert loop.index("prefetch") < loop.index("ld.global.nc")
+    assert "prefetch" not in to_ptx(Graph.from_dict(graph), meta)
+    wide = compile_spec(problems.CONFIGS["c4_full_sum"]())  # 1184 blocks: several waves
+    assert "prefetch" not in wide
+    ptxas(rolled, tmp_path)
+
+
 def gemm_plan(spec: problems.ProblemSpec):
     from ptxgen.compiler import kernel_for_meta
     from ptxgen.lower import Buffer
