@@ -72,6 +72,10 @@ def parse_args() -> argparse.Namespace:
                    help="how the sharded sum's partials are summed across ranks: inside the sum "
                         "kernel (its last block exchanges over NVLink peer memory), by a "
                         "separate one-warp kernel over peer memory, or by NCCL")
+    p.add_argument("--splitk-shard", choices=("k", "m"), default="k",
+                   help="how the split-K GEMM divides across ranks: along K (each rank 1/N of A "
+                        "and B, the partial C reduce-scattered by rows over NCCL) or along M "
+                        "(rows of A and C, B replicated, no collective)")
     p.add_argument("--e2e-lanes", type=int, default=2,
                    help="steps of the host-buffer (e2e) path in flight at once, one stream each")
     p.add_argument("--only", default=None,
@@ -316,6 +320,19 @@ def check_output(name: str, plan: Any, tensors: dict[str, Any], world: int) -> d
         got = float(view("sum_1").double()[0])
         err = abs(got - total) / max(abs(total), 1e-30)
         ok = err <= 1e-5
+    elif name == "c5b_matmul_splitk" and plan.reduce_scatter and world > 1:
+        # each rank holds a K slice of A and B: the product is the sum over ranks of the f64
+        # products of the slices; this rank's rows of it against the rows it was left with
+        import torch.distributed as tdist
+
+        part = view("x0").double() @ view("x1").double()
+        tdist.all_reduce(part)
+        rank = tdist.get_rank()
+        got = tensors["matmul@rows"]
+        ref = part[rank * got.shape[0]:(rank + 1) * got.shape[0]]
+        diff = (got.double() - ref).abs()
+        ok = bool((diff <= 1e-2 * ref.abs() + 1e-4 * ref.abs().max()).all())
+        err = float(diff.max() / ref.abs().max())
     elif name in ("c5_matmul", "c5b_matmul_splitk"):
         a, b, c = view("x0"), view("x1"), view("matmul")
         m = a.shape[0]
@@ -383,11 +400,12 @@ def measure_kernel(plan: Any, steps: int, warmup: int, world: int, l2: str = "cl
         if l2 == "clean":
             torch.sum(reread.view(torch.int64), dim=(0,), out=sink)
 
-    collective = bool(plan.allreduce) and world > 1
-    fused = collective and via == "fused"  # the kernel sums its partial across ranks itself
+    collective = bool(plan.allreduce or plan.reduce_scatter) and world > 1
+    # the kernel sums its (scalar) partial across ranks itself
+    fused = collective and via == "fused" and bool(plan.allreduce)
     mids: list[Any] = []
     peer = slots = None
-    if collective and via == "peer":
+    if collective and via == "peer" and plan.allreduce:
         from ptxgen.peer import PeerSum
 
         peer = PeerSum()
@@ -407,6 +425,15 @@ def measure_kernel(plan: Any, steps: int, warmup: int, world: int, l2: str = "cl
             with torch.cuda.stream(s):
                 tdist.all_reduce(t)
 
+    # reduce-scattered outputs: this rank's rows of the summed partials
+    shapes = {a["name"]: a["shape"] for a in plan.spec.kernel["args"]}
+    rows_out = {}
+    if collective:
+        for name in plan.reduce_scatter:
+            m, n = shapes[name]
+            rows_out[name] = torch.empty(m // world, n, dtype=tensors[name].dtype,
+                                         device=tensors[name].device)
+
     def step(mid: Any = None) -> None:
         prob.launch(tensors, stream=stream.cuda_stream)
         if collective and not fused:
@@ -414,6 +441,12 @@ def measure_kernel(plan: Any, steps: int, warmup: int, world: int, l2: str = "cl
                 mid.record(stream)
             for name in plan.allreduce:
                 combine(tensors[name], stream)
+            for name, out in rows_out.items():
+                import torch.distributed as tdist
+
+                with torch.cuda.stream(stream):
+                    tdist.reduce_scatter_tensor(out, tensors[name][:out.numel() * world]
+                                                .view(-1, out.shape[1]))
 
     align = torch.zeros(1, dtype=torch.float32, device="cuda")
 
@@ -468,8 +501,9 @@ def measure_kernel(plan: Any, steps: int, warmup: int, world: int, l2: str = "cl
     out = {"mean_ms": max_over_ranks(mean_ms, world),
            "median_ms": max_over_ranks(statistics.median(times), world),
            "min_ms": max_over_ranks(min(times), world), "launches": steps,
-           "clocks": sampler.summary(), "tensors": tensors, "prob": prob, "peer": peer,
-           "slots": slots}
+           "clocks": sampler.summary(),
+           "tensors": {**tensors, **{f"{n}@rows": t for n, t in rows_out.items()}},
+           "prob": prob, "peer": peer, "slots": slots}
     return out
 
 
@@ -505,7 +539,8 @@ def _host_lane(prob: Any, tensors: dict[str, Any], stream: int) -> dict[str, Any
     prob.module.fill_tensormaps({n: tensors[n].data_ptr() for n in tensors})
     args = (prob.grid(), launch["block"][0], int(launch.get("smem_bytes", 0)), stream,
             dev, host, nbytes, flags)
-    return {"kernel": prob.load(), "args": args, "keep": keep, "tensors": tensors,
+    cols = {a["name"]: a["shape"][-1] for a in launch["args"]}
+    return {"kernel": prob.load(), "args": args, "keep": keep, "tensors": tensors, "cols": cols,
             "h2d": h2d, "d2h": d2h}
 
 
@@ -523,7 +558,8 @@ def measure_e2e(plan: Any, prob: Any, tensors: dict[str, Any], steps: int, world
     from ptxgen.runtime import Problem
 
     lanes = [_host_lane(prob, tensors, torch.cuda.Stream().cuda_stream)]
-    while len(lanes) < in_flight and not (plan.allreduce and world > 1):
+    collective = bool(plan.allreduce or plan.reduce_scatter) and world > 1
+    while len(lanes) < in_flight and not collective:
         other = Problem(plan.spec.graph, plan.spec.meta)
         other.load()
         lanes.append(_host_lane(other, {n: t.clone() for n, t in tensors.items()},
@@ -535,6 +571,15 @@ def measure_e2e(plan: Any, prob: Any, tensors: dict[str, Any], steps: int, world
     def run(lane: dict[str, Any], count: int) -> None:
         for _ in range(count):
             lane["kernel"].run_host(*lane["args"])
+            if plan.reduce_scatter and world > 1:
+                import torch.distributed as tdist
+
+                for name in plan.reduce_scatter:
+                    full = lane["tensors"][name]
+                    rows = torch.empty(full.numel() // world // lane["cols"][name],
+                                       lane["cols"][name], dtype=full.dtype, device=full.device)
+                    tdist.reduce_scatter_tensor(rows, full.view(-1, lane["cols"][name]))
+                torch.cuda.synchronize()
             if plan.allreduce and world > 1 and not fused:
                 import torch.distributed as tdist
 
@@ -761,7 +806,8 @@ def run_ours(args: argparse.Namespace) -> None:
     def plan_for(name: str) -> Any:
         if args.share > 1:
             return shard.local_problem(name, args.share)
-        plan = shard.local_problem(name, world, weak=args.scaling == "weak")
+        plan = shard.local_problem(name, world, weak=args.scaling == "weak",
+                                   rows=args.splitk_shard == "m")
         if args.collective == "fused" and plan.allreduce and world > 1:
             import dataclasses
 
@@ -854,11 +900,14 @@ def run_ours(args: argparse.Namespace) -> None:
                   "parallelism": f"tile-axis x{world}" if world > 1 else "single GPU",
                   "l2": L2_MODES[args.l2],
                   "allreduce": list(plan.allreduce),
+                  "reduce_scatter": list(plan.reduce_scatter),
                   "collective": ({"fused": "inside the sum kernel: its last block exchanges "
                                            "the partials over NVLink peer memory",
                                   "peer": "a separate one-warp kernel over NVLink peer memory",
                                   "nccl": "NCCL all-reduce"}[args.collective]
-                                 if plan.allreduce and world > 1 else None)},
+                                 if plan.allreduce and world > 1 else
+                                 "NCCL reduce-scatter of the partial C by rows"
+                                 if plan.reduce_scatter and world > 1 else None)},
         "check": head["check"]["result"] if not failed else "fail",
         "checks": {head["workload"]: head["check"],
                    **{x["workload"]: x.get("check", {"result": "error"}) for x in extras}},

@@ -1,24 +1,27 @@
 """Multi-GPU partitioning of the benchmark configurations: one process per GPU.
 
-Each configuration's Tile axis is independent work, so a rank runs the same kernel on a
-contiguous share of it, with no collective on the data path:
+A rank runs the same kernel on a contiguous share of the configuration:
 
 * pointwise add / gelu chain / row softmax: the element (or row) axis splits into ``world``
   contiguous ranges; each rank holds its inputs and writes its outputs, which stay sharded;
-* GEMM (and split-K GEMM): the M axis splits; each rank holds its rows of A and C and all of B
-  (split-K also splits further along K inside the rank so every rank keeps the same number of
-  CTAs);
-* full sum: the element axis splits; each rank reduces its share to one partial, and the only
-  collective of the whole path, one all-reduce of those partials, combines them.
+* GEMM: the M axis splits; each rank holds its rows of A and C and all of B, with no
+  collective;
+* split-K GEMM: the K axis splits, so each rank holds 1/N of A (its columns) and of B (its
+  rows), computes all of C as a partial sum, and the ranks reduce-scatter C by rows (the
+  split-K reduction across GPUs): each keeps its M/N rows of the product. Splitting along M
+  instead (``rows=True``) replicates B, and at 8 ranks each rank then reads 144 MB for 1/8
+  of the flops;
+* full sum: the element axis splits; each rank reduces its share to one partial, and an
+  all-reduce of those partials combines them.
 
 By default the ranks split the configuration's fixed size (strong scaling: the same problem at
 every rank count); ``weak=True`` instead gives each rank a benchmark-sized share of a problem
 ``world`` times larger along the split axis.
 
 ``local_problem`` returns the rank's Plan: its Kernel IR problem (every rank's has the same
-shape, so each rank compiles the same module), which arguments are split along their first axis
-(``sharded``), and which outputs are summed across ranks (``allreduce``). ``slice_inputs`` and
-``combine`` apply that contract to concrete arrays.
+shape, so each rank compiles the same module), which arguments are split (``sharded``, along
+``axes``), and which outputs are summed across ranks (``allreduce``) or summed and split by rows
+(``reduce_scatter``). ``slice_inputs`` and ``combine`` apply that contract to concrete arrays.
 """
 
 from __future__ import annotations
@@ -38,36 +41,47 @@ class Plan:
     name: str
     world: int
     spec: ProblemSpec
-    sharded: tuple[str, ...] = ()  # arguments split along their first axis, rank-contiguous
+    sharded: tuple[str, ...] = ()  # arguments split rank-contiguously (along ``axes``)
     allreduce: tuple[str, ...] = ()  # outputs summed across ranks after the kernel
     units: str = "bytes"  # what ``work`` counts: "bytes" (HBM) or "flops" (tensor)
     work: int = 0  # algorithmic bytes or flops of one rank's step
     extra: dict[str, Any] = field(default_factory=dict)
+    # the axis each sharded argument is split along (default: its first)
+    axes: dict[str, int] = field(default_factory=dict)
+    # outputs each rank computes in full as a partial sum, then reduce-scatters by rows: the
+    # ranks' partials are summed and rank r keeps rows [r*M/N, (r+1)*M/N)
+    reduce_scatter: tuple[str, ...] = ()
 
     def slice_inputs(self, full: dict[str, np.ndarray], rank: int) -> dict[str, np.ndarray]:
         """This rank's input arrays, cut from the whole problem's."""
         out = {}
         for name, arr in full.items():
             if name in self.sharded:
-                n = arr.shape[0] // self.world
-                out[name] = arr[rank * n:(rank + 1) * n]
+                axis = self.axes.get(name, 0)
+                n = arr.shape[axis] // self.world
+                out[name] = np.take(arr, np.arange(rank * n, (rank + 1) * n), axis=axis)
             else:
                 out[name] = arr
         return out
 
     def combine(self, local: dict[str, np.ndarray], group: Any = None) -> dict[str, np.ndarray]:
         """Finish a rank's outputs: all-reduce (sum) the ``allreduce`` ones across ``group``
-        (a torch.distributed group; None is the default group). Sharded outputs stay local."""
-        if not self.allreduce or self.world == 1:
+        (a torch.distributed group; None is the default group); sum the ``reduce_scatter`` ones
+        and keep this rank's rows. Sharded outputs stay local."""
+        if (not self.allreduce and not self.reduce_scatter) or self.world == 1:
             return local
         import torch
         import torch.distributed as dist
 
         out = dict(local)
-        for name in self.allreduce:
+        for name in (*self.allreduce, *self.reduce_scatter):
             t = torch.from_numpy(np.ascontiguousarray(local[name]))
             dist.all_reduce(t, group=group)
             out[name] = t.numpy()
+        rank = dist.get_rank(group)
+        for name in self.reduce_scatter:
+            rows = out[name].shape[0] // self.world
+            out[name] = out[name][rank * rows:(rank + 1) * rows]
         return out
 
 
@@ -82,7 +96,7 @@ SPLIT_AXIS: dict[str, str] = {
     "c1_vector_add": "elements", "c2_gelu_chain": "rows", "c3_row_softmax": "rows",
     "c4_full_sum": "elements (per-rank partials summed across ranks)",
     "c5_matmul": "rows of A and C (B replicated)",
-    "c5b_matmul_splitk": "rows of A and C (B replicated)",
+    "c5b_matmul_splitk": "K (columns of A, rows of B); partial C reduce-scattered by rows",
 }
 
 
@@ -127,6 +141,24 @@ def _c5(world: int, size: tuple[int, ...]) -> Plan:
 
 
 def _c5b(world: int, size: tuple[int, ...]) -> Plan:
+    """Split-K GEMM across ranks along K: rank r holds columns K_r of A and rows K_r of B (1/N
+    of each operand), computes the whole of C from them as a partial sum with the split-K
+    template, and the ranks reduce-scatter C by rows (the split-K reduction across GPUs), so
+    each ends with its M/N rows of the product, as the row split leaves them."""
+    m, n, k = size
+    if world == 1:
+        return _c5b_rows(world, size)
+    _split(m, world, "rows of C")
+    kl = _split(k, world, "K")
+    split = 4 if kl % (4 * 64) == 0 else 1
+    return Plan("c5b_matmul_splitk", world,
+                problems.matmul(m, n, kl, split_k=split, raster_group=None), ("x0", "x1"),
+                units="flops", work=2 * m * n * kl, axes={"x0": 1, "x1": 0},
+                reduce_scatter=("matmul",))
+
+
+def _c5b_rows(world: int, size: tuple[int, ...]) -> Plan:
+    """Split-K GEMM split along M (rows of A and C; B replicated), no collective."""
     m, n, k = size
     ml = _split(m, world, "rows of A")
     # four K splits per 1024 rows, more when a rank holds fewer rows, so each rank keeps enough
@@ -146,7 +178,7 @@ BUILDERS: dict[str, Callable[[int, tuple[int, ...]], Plan]] = {
 
 
 def local_problem(name: str, world: int = 1, size: tuple[int, ...] | None = None,
-                  weak: bool = False) -> Plan:
+                  weak: bool = False, rows: bool = False) -> Plan:
     """The plan one of ``world`` ranks runs for configuration ``name``. ``size`` is the whole
     problem (default: the benchmark size). With ``weak`` the whole problem is ``world`` times
     that size along the sharded axis, so each rank keeps a benchmark-sized share (weak scaling);
@@ -156,4 +188,6 @@ def local_problem(name: str, world: int = 1, size: tuple[int, ...] | None = None
     whole = tuple(size) if size is not None else SIZES[name]
     if weak:
         whole = (whole[0] * world, *whole[1:])
+    if rows and name == "c5b_matmul_splitk":  # the M split, for comparison
+        return _c5b_rows(world, whole)
     return BUILDERS[name](world, whole)

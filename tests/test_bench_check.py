@@ -65,7 +65,15 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
         outs = FORMULAS[name](local, plan.spec.meta)
         if name == "c4_full_sum":  # every rank holds the combined total, as the exchange leaves it
             outs = plan.combine(outs)
-        good = bench.check_output(name, plan, _tensors(plan, local, outs), world)
+        rows = {}
+        if plan.reduce_scatter:  # the K-split GEMM: this rank's rows of the summed partials
+            combined = plan.combine(outs)
+            import torch
+            rows = {f"{n}@rows": torch.from_numpy(np.ascontiguousarray(combined[n]))
+                    for n in plan.reduce_scatter}
+        good = bench.check_output(name, plan, {**_tensors(plan, local, outs), **rows}, world)
+        if plan.reduce_scatter:  # the planted mistake goes into the rows the check reads
+            outs = {f"{n}@rows": combined[n] for n in plan.reduce_scatter}
         bad_outs = {k: v.copy() for k, v in outs.items()}
         if rank == 1:  # one wrong element on one rank only
             key = next(iter(bad_outs))
@@ -74,7 +82,13 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
                 flat[-1] ^= 0x4000  # flip a high exponent bit of the bf16 value
             else:
                 flat[-1] = flat[-1] * 1.01 + 0.5
-        bad = bench.check_output(name, plan, _tensors(plan, local, bad_outs), world)
+        if plan.reduce_scatter:
+            import torch
+            bad_t = {**_tensors(plan, local, FORMULAS[name](local, plan.spec.meta)),
+                     **{k: torch.from_numpy(np.ascontiguousarray(v)) for k, v in bad_outs.items()}}
+        else:
+            bad_t = _tensors(plan, local, bad_outs)
+        bad = bench.check_output(name, plan, bad_t, world)
         results[name] = (good, bad)
     dist.barrier()
     Path(out_dir, f"rank{rank}.pkl").write_bytes(pickle.dumps(results))
