@@ -72,10 +72,10 @@ def parse_args() -> argparse.Namespace:
                    help="how the sharded sum's partials are summed across ranks: inside the sum "
                         "kernel (its last block exchanges over NVLink peer memory), by a "
                         "separate one-warp kernel over peer memory, or by NCCL")
-    p.add_argument("--splitk-shard", choices=("k", "m"), default="k",
-                   help="how the split-K GEMM divides across ranks: along K (each rank 1/N of A "
-                        "and B, the partial C reduce-scattered by rows over NCCL) or along M "
-                        "(rows of A and C, B replicated, no collective)")
+    p.add_argument("--splitk-shard", choices=("m", "k"), default="m",
+                   help="how the split-K GEMM divides across ranks: along M (default: rows of A "
+                        "and C, B replicated, no collective) or along K (each rank 1/N of A and "
+                        "B, the partial C reduce-scattered by rows over NCCL)")
     p.add_argument("--e2e-lanes", type=int, default=2,
                    help="steps of the host-buffer (e2e) path in flight at once, one stream each")
     p.add_argument("--only", default=None,
@@ -807,7 +807,7 @@ def run_ours(args: argparse.Namespace) -> None:
         if args.share > 1:
             return shard.local_problem(name, args.share)
         plan = shard.local_problem(name, world, weak=args.scaling == "weak",
-                                   rows=args.splitk_shard == "m")
+                                   ksplit=args.splitk_shard == "k")
         if args.collective == "fused" and plan.allreduce and world > 1:
             import dataclasses
 

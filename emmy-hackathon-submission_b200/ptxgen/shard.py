@@ -4,13 +4,13 @@ A rank runs the same kernel on a contiguous share of the configuration:
 
 * pointwise add / gelu chain / row softmax: the element (or row) axis splits into ``world``
   contiguous ranges; each rank holds its inputs and writes its outputs, which stay sharded;
-* GEMM: the M axis splits; each rank holds its rows of A and C and all of B, with no
-  collective;
-* split-K GEMM: the K axis splits, so each rank holds 1/N of A (its columns) and of B (its
-  rows), computes all of C as a partial sum, and the ranks reduce-scatter C by rows (the
-  split-K reduction across GPUs): each keeps its M/N rows of the product. Splitting along M
-  instead (``rows=True``) replicates B, and at 8 ranks each rank then reads 144 MB for 1/8
-  of the flops;
+* GEMM and split-K GEMM: the M axis splits; each rank holds its rows of A and C and all of B,
+  with no collective;
+* split-K GEMM along K instead (``ksplit=True``): each rank holds 1/N of A (its columns) and of
+  B (its rows), computes all of C as a partial sum, and the ranks reduce-scatter C by rows
+  over NCCL (the split-K reduction across GPUs), each keeping its M/N rows of the product.
+  Measured at 2 ranks it lost to the M split (93.7 µs against 58.6: a 62 µs kernel of short
+  segments, then 31 µs of reduce-scatter for 4 MB), so it is not the default;
 * full sum: the element axis splits; each rank reduces its share to one partial, and an
   all-reduce of those partials combines them.
 
@@ -96,7 +96,7 @@ SPLIT_AXIS: dict[str, str] = {
     "c1_vector_add": "elements", "c2_gelu_chain": "rows", "c3_row_softmax": "rows",
     "c4_full_sum": "elements (per-rank partials summed across ranks)",
     "c5_matmul": "rows of A and C (B replicated)",
-    "c5b_matmul_splitk": "K (columns of A, rows of B); partial C reduce-scattered by rows",
+    "c5b_matmul_splitk": "rows of A and C (B replicated)",
 }
 
 
@@ -140,14 +140,14 @@ def _c5(world: int, size: tuple[int, ...]) -> Plan:
                 work=2 * ml * n * k)
 
 
-def _c5b(world: int, size: tuple[int, ...]) -> Plan:
+def _c5b_k(world: int, size: tuple[int, ...]) -> Plan:
     """Split-K GEMM across ranks along K: rank r holds columns K_r of A and rows K_r of B (1/N
     of each operand), computes the whole of C from them as a partial sum with the split-K
     template, and the ranks reduce-scatter C by rows (the split-K reduction across GPUs), so
     each ends with its M/N rows of the product, as the row split leaves them."""
     m, n, k = size
     if world == 1:
-        return _c5b_rows(world, size)
+        return _c5b(world, size)
     _split(m, world, "rows of C")
     kl = _split(k, world, "K")
     split = 4 if kl % (4 * 64) == 0 else 1
@@ -157,7 +157,7 @@ def _c5b(world: int, size: tuple[int, ...]) -> Plan:
                 reduce_scatter=("matmul",))
 
 
-def _c5b_rows(world: int, size: tuple[int, ...]) -> Plan:
+def _c5b(world: int, size: tuple[int, ...]) -> Plan:
     """Split-K GEMM split along M (rows of A and C; B replicated), no collective."""
     m, n, k = size
     ml = _split(m, world, "rows of A")
@@ -178,7 +178,7 @@ BUILDERS: dict[str, Callable[[int, tuple[int, ...]], Plan]] = {
 
 
 def local_problem(name: str, world: int = 1, size: tuple[int, ...] | None = None,
-                  weak: bool = False, rows: bool = False) -> Plan:
+                  weak: bool = False, ksplit: bool = False) -> Plan:
     """The plan one of ``world`` ranks runs for configuration ``name``. ``size`` is the whole
     problem (default: the benchmark size). With ``weak`` the whole problem is ``world`` times
     that size along the sharded axis, so each rank keeps a benchmark-sized share (weak scaling);
@@ -188,6 +188,6 @@ def local_problem(name: str, world: int = 1, size: tuple[int, ...] | None = None
     whole = tuple(size) if size is not None else SIZES[name]
     if weak:
         whole = (whole[0] * world, *whole[1:])
-    if rows and name == "c5b_matmul_splitk":  # the M split, for comparison
-        return _c5b_rows(world, whole)
+    if ksplit and name == "c5b_matmul_splitk":  # the K split, for comparison
+        return _c5b_k(world, whole)
     return BUILDERS[name](world, whole)

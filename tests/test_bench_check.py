@@ -60,7 +60,7 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
         full = shard.local_problem(name, 1, size)
         ins = {a["name"]: problems.seeded_input(a) for a in full.spec.kernel["args"]
                if not a.get("output")}
-        plan = shard.local_problem(name, world, size)
+        plan = shard.local_problem(name, world, size, ksplit=True)
         local = plan.slice_inputs(ins, rank)
         outs = FORMULAS[name](local, plan.spec.meta)
         if name == "c4_full_sum":  # every rank holds the combined total, as the exchange leaves it

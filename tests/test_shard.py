@@ -52,7 +52,7 @@ def _sharded_worker(rank: int, world: int, port: int, out_dir: str) -> None:
         full = shard.local_problem(name, 1, size)
         ins = {a["name"]: problems.seeded_input(a) for a in full.spec.kernel["args"]
                if not a.get("output")}
-        plan = shard.local_problem(name, world, size)
+        plan = shard.local_problem(name, world, size, ksplit=True)
         local = plan.slice_inputs(ins, rank)
         out = run_kernel(plan.spec.graph, plan.spec.meta, local)
         out = plan.combine(out)
@@ -79,7 +79,7 @@ def test_sharded_plans_equal_unsharded(tmp_path) -> None:
         ins = {a["name"]: problems.seeded_input(a) for a in full.spec.kernel["args"]
                if not a.get("output")}
         want = run_kernel(full.spec.graph, full.spec.meta, ins)
-        plan = shard.local_problem(name, world, size)
+        plan = shard.local_problem(name, world, size, ksplit=True)
         for out, ref in want.items():
             parts = [r[out] for r in results[name]]
             if out in plan.reduce_scatter:  # K-split partials summed: f32 order differs
