@@ -141,6 +141,47 @@ def test_bounded_wait(cuda, warp: bool, arrive: bool) -> None:
     assert dummy.item() == 1.0
 
 
+def test_short_shared_memory_launch_reports_and_returns(cuda) -> None:
+    """A GEMM launched with less dynamic shared memory than its layout needs (here meta.json's
+    figure, which is what every launch got before the runtime read the module's own) leaves at
+    entry with status bit ``SMEM_SHORT``, before any barrier, TMEM or shared access exists; the
+    context stays usable and the same module then runs correctly with its full figure."""
+    import torch
+
+    from ptxgen.runtime import Problem, library
+    from ptxgen.templates.matmul import SMEM_SHORT
+
+    spec = problems.matmul(256, 256, 256)
+    prob = Problem(spec.graph, spec.meta)
+    tensors = prob.allocate()
+    ins = reference_inputs(spec.meta)
+    for name, arr in ins.items():
+        tensors[name].copy_(torch.from_numpy(arr.reshape(-1).view(np.int16)).view(torch.bfloat16))
+    tensors["matmul"].fill_(float("nan"))
+    kernel, module = prob.load(), prob.module
+    need = module.dynamic_smem
+    short = int(spec.kernel["smem_bytes"])
+    assert short < need
+    module.fill_tensormaps({n: t.data_ptr() for n, t in tensors.items()})
+    launch = prob.launch_entry
+    ptrs = [tensors[n].data_ptr() for n in launch["arg_order"]]
+    import ctypes
+
+    arr = (ctypes.c_uint64 * len(ptrs))(*ptrs)
+    stream = torch.cuda.current_stream().cuda_stream
+    rc = library().pg_kernel_launch(kernel.handle, prob.grid(), launch["block"][0], short,
+                                    stream, arr, len(ptrs))
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert module.status() == 1 << SMEM_SHORT
+    assert torch.isnan(tensors["matmul"]).all()  # nothing was written
+    prob.launch(tensors, check_status=True)  # the module's own figure: runs and is right
+    torch.cuda.synchronize()
+    got = tensors["matmul"].cpu().numpy().reshape(256, 256)
+    a, b = operands(spec, ins)
+    assert_gemm_close(got, a @ b)
+
+
 def test_launcher_times_launches(cuda) -> None:
     """``pg_kernel_time`` (CUDA events around each launch) agrees with PyTorch's events on the
     same back-to-back launches of the config-5 template, within a factor of 1.5. The GEMM is
