@@ -70,6 +70,12 @@ SEGMENT_COST = 2  # a segment's epilogue, in K blocks of MMA time, when choosing
 EPILOGUE_WARPS = (4, 5, 6, 7)
 BAR_BYTES = 8
 SMEM_SHORT = 8  # status bit: the launch gave less dynamic shared memory than the layout needs
+NARROW = (192, 128, 64)  # widths a mixed-width plan may cut beside whole 256-column tiles
+MIXED_GAIN = 0.05  # ... used only when the cost model finishes that much sooner than whole tiles
+# a pair's time for one K block of a tile of each width, against a whole tile's, measured on a
+# B200 with one tile per pair (K = 8192): the loads of A and B and the pipeline around the MMAs,
+# not the MMAs, set the pace of a narrow tile, so a narrower tile is barely faster
+K_BLOCK_TIME = {256: 1.0, 192: 0.98, 128: 0.95, 64: 0.90}
 SMEM_LIMIT = 232448  # dynamic shared memory one CTA may opt into on sm_100 (227 KiB)
 STAGE_BLOCK = 32  # rows and columns of the f32 block an epilogue warp stages per TMA op
 STAGE_BUF = STAGE_BLOCK * STAGE_BLOCK * 4  # 4 KiB: 32 rows of 128 bytes, 128-byte swizzled
@@ -96,6 +102,9 @@ class MatmulPlan:
     # the epilogue stages each warp's 32 x 32 blocks of C in shared memory and writes them
     # with one TMA op each (a reduce-add for split-K); False: per-thread global stores/reds
     staged: bool = True
+    # a plain pair GEMM may cut some tiles narrower to even out the pairs' work (``columns``);
+    # False keeps whole tiles
+    mixed: bool = True
 
     @property
     def kc(self) -> int:
@@ -130,6 +139,69 @@ class MatmulPlan:
         table = tuple((mt, nt, cut[j], cut[j + 1] - cut[j])
                       for j in range(splits) for mt, nt in tiles)
         return table, min(slots, len(table)) * rows
+
+    def columns(self) -> tuple[tuple[tuple[int, int, int], ...], int] | None:
+        """A plain pair GEMM's tiles in mixed widths, for when whole 256-column tiles would
+        leave the last wave of SM pairs part-empty: (256-row band, first column, width) per
+        entry (width 0: a gap the pair skips) and the grid; None keeps the uniform table.
+
+        Each band of C is cut into whole 256-column tiles and, at its right end, tiles of one
+        narrower width ``w`` from ``NARROW`` (as many in every band as keep the rest a multiple
+        of 256 columns). The tiles go to the pairs widest first, each to the pair with the least
+        work so far (a tile costs its K blocks at its width's ``K_BLOCK_TIME`` plus
+        ``SEGMENT_COST``; ties to the lowest pair, so the whole tiles keep the IR's order
+        round-robin), and the table lists them round by round: entry ``r * used + q`` is pair
+        ``q``'s ``r``-th tile, which the kernel's ``cluster + i * nclusters`` walk hands it. The
+        plan with the shortest longest pair wins if it beats whole tiles by ``MIXED_GAIN``.
+        With the measured times that happens where the tiles do not fill one wave of pairs (a
+        1024^3 GEMM's 16 tiles become 64 of 64 columns); a last wave that is only part full
+        stays as it is, since a narrower tile is barely faster per K block. Every element of C
+        is still one tile's whole K loop, in the same K order."""
+        if not self.mixed or self.atomic or not self.pair or self.n % 256:
+            return None
+        kbs = self.k // BK
+        pairs = SM_COUNT // 2
+        bands = self.m // (2 * BM)
+        order = list(dict.fromkeys((mt // 2, nt) for mt, nt, _ in self.schedule))
+
+        def cost(w: int) -> float:
+            return kbs * K_BLOCK_TIME[w] + SEGMENT_COST
+
+        best: tuple[float, list | None] = (
+            (1 - MIXED_GAIN) * -(-len(order) // pairs) * cost(256), None)
+        for w in NARROW:
+            step = 256 // math.gcd(w, 256)  # narrow tiles a band adds at a time
+            for groups in range(1, min(bands * (self.n // (w * step)),
+                                       -(-2 * pairs // step)) + 1):
+                per_band = [groups // bands + (b < groups % bands) for b in range(bands)]
+                whole = [(self.n - g * step * w) // 256 for g in per_band]
+                tiles = [(mt, nt * 256, 256) for mt, nt in order if nt < whole[mt]]
+                tiles += [(mt, whole[mt] * 256 + j * w, w)
+                          for mt in range(bands) for j in range(per_band[mt] * step)]
+                lists, span = _spread([t[2] for t in tiles], pairs, cost)
+                if span < best[0]:
+                    best = (span, [[tiles[i] for i in q] for q in lists if q])
+        if best[1] is None:
+            return None
+        lists = best[1]
+        used, rounds = len(lists), max(map(len, lists))
+        table = tuple(lists[q][r] if r < len(lists[q]) else (0, 0, 0)
+                      for r in range(rounds) for q in range(used))
+        return table, 2 * used
+
+
+def _spread(widths: list[int], pairs: int, cost) -> tuple[list[list[int]], float]:
+    """Tile indexes per pair, widest first, each to the least-loaded pair (the lowest on a
+    tie), and the longest pair's load."""
+    import heapq
+
+    heap = [(0.0, q) for q in range(pairs)]
+    lists: list[list[int]] = [[] for _ in range(pairs)]
+    for i in sorted(range(len(widths)), key=lambda i: -widths[i]):
+        load, q = heapq.heappop(heap)
+        lists[q].append(i)
+        heapq.heappush(heap, (load + cost(widths[i]), q))
+    return lists, max(load for load, _ in heap)
 
 
 # --- matching ----------------------------------------------------------------------------------
@@ -447,7 +519,9 @@ def instr_desc(dtype: str, bn: int, a_mn_major: bool = False, b_mn_major: bool =
 def emit(p: MatmulPlan) -> str:
     e = p.entry
     x = _Text()
-    table, ctas = p.segments()
+    cols = p.columns()
+    mixed = cols is not None  # per-entry width and first column (pair GEMMs only)
+    table, ctas = cols if mixed else p.segments()
     entries = len(table)
     pair = p.pair
     g = 2 if pair else 1  # the tcgen05 cta_group
@@ -489,13 +563,20 @@ def emit(p: MatmulPlan) -> str:
         bounded_wait(x, bar_addr, parity, code, fail, sem=sem, warp=warp)
 
     def sched_lookup(skip: str) -> None:
-        """Entry %t of the table into %mt, %nt, %kb0, %cnt; an empty entry branches to skip."""
+        """Entry %t of the table into %mt, %nt, %kb0, %cnt (mixed widths: %mt, %col, %wid,
+        %cnt, with %kb0 0); an empty entry branches to skip."""
         x(f"mul.wide.u32 {r('s_off', u64)}, %t, 8;")
         x(f"add.s64 %s_off, {r('sched', u64)}, %s_off;")
         x(f"ld.global.nc.v2.u32 {{{r('code')}, {r('code2')}}}, [%s_off];")
         x(f"and.b32 {r('mt')}, %code, 65535;")
-        x(f"shr.u32 {r('nt')}, %code, 16;")
-        x(f"and.b32 {r('kb0')}, %code2, 65535;")
+        if mixed:
+            x(f"shr.u32 {r('col')}, %code, 16;")
+            x("shl.b32 %col, %col, 5;")
+            x(f"and.b32 {r('wid')}, %code2, 65535;")
+            x(f"mov.u32 {r('kb0')}, 0;")
+        else:
+            x(f"shr.u32 {r('nt')}, %code, 16;")
+            x(f"and.b32 {r('kb0')}, %code2, 65535;")
         x(f"shr.u32 {r('cnt')}, %code2, 16;")
         x("setp.eq.u32 %p, %cnt, 0;")
         x(f"@%p bra {skip};")
@@ -616,7 +697,15 @@ def emit(p: MatmulPlan) -> str:
     x(f"setp.ge.u32 %p, %t, {entries};")
     x(f"@%p bra {p_drain};")
     sched_lookup(p_next)
-    if pair:  # this CTA's half: rows rank*128 of the 256-row tile, B columns rank*128
+    if mixed:  # this CTA's half: rows rank*128 of the band, B columns rank*wid/2 of the tile
+        x(f"shl.b32 {r('half')}, %rank, 7;")
+        x(f"mad.lo.u32 {r('m0')}, %mt, {g * BM}, %half;")
+        x(f"shr.u32 {r('hw')}, %wid, 1;")
+        x(f"mad.lo.u32 {r('n0')}, %rank, %hw, %col;")
+        # a half of 64 columns or fewer is one 64-column chunk of B; the second is not loaded
+        x(f"setp.gt.u32 {r('pb2', pred)}, %hw, 64;")
+        x(f"selp.u32 {r('tx')}, {stage_tx}, {stage_tx - g * b_chunk}, %pb2;")
+    elif pair:  # this CTA's half: rows rank*128 of the 256-row tile, B columns rank*128
         x(f"shl.b32 {r('half')}, %rank, 7;")
         x(f"mad.lo.u32 {r('m0')}, %mt, {g * BM}, %half;")
         x(f"mad.lo.u32 {r('n0')}, %nt, {p.bn}, %half;")
@@ -637,7 +726,8 @@ def emit(p: MatmulPlan) -> str:
     if pair:
         # both CTAs' loads land on the leader's full barrier, which the MMA waits on; the
         # leader expects the bytes of both halves
-        x(f"@%plead mbarrier.arrive.expect_tx.shared::cta.b64 _, [%fbar], {stage_tx};")
+        x(f"@%plead mbarrier.arrive.expect_tx.shared::cta.b64 _, [%fbar], "
+          f"{'%tx' if mixed else stage_tx};")
         x(f"mapa.shared::cluster.u32 {r('fbar_l')}, %fbar, 0;")
         tma, bar = ("cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global"
                     ".mbarrier::complete_tx::bytes"), "%fbar_l"
@@ -652,7 +742,8 @@ def emit(p: MatmulPlan) -> str:
     for cidx in range(nb // 64):
         x(f"add.u32 {r('ncol')}, %n0, {cidx * 64};")
         x(f"add.u32 {r('bdc')}, %bdst, {cidx * b_chunk};")
-        x(f"{tma} [%bdc], [%tmap_b, {{%ncol, %kk}}], [{bar}];")
+        guard = "@%pb2 " if mixed and cidx else ""
+        x(f"{guard}{tma} [%bdc], [%tmap_b, {{%ncol, %kk}}], [{bar}];")
     advance_stage()
     x(f"add.u32 %kk, %kk, {BK};")
     x("add.u32 %kb, %kb, 1;")
@@ -693,6 +784,7 @@ def emit(p: MatmulPlan) -> str:
         x(f"mov.u32 {r(n)}, 0;")
     x("mov.u32 %t, %cta;")
     x(f"mov.u32 {r('idesc')}, {idesc};")
+    idesc_n0 = instr_desc(p.dtype, 0, m=g * BM)  # the descriptor without its N field
     m_tile, m_k, m_end, m_free, m_next = (
         x.label(h) for h in ("m_tile", "m_k", "m_end", "m_free", "m_next"))
     x(f"{m_tile}:")
@@ -707,6 +799,10 @@ def emit(p: MatmulPlan) -> str:
     wait("%tebar", "%par", 3, m_end, ".acquire.cluster" if pair else "")
     x(f"{m_free}:")
     x("tcgen05.fence::after_thread_sync;")
+    if mixed:  # N = the tile's width, at bit 17 in units of 8
+        x(f"shr.u32 {r('idn')}, %wid, 3;")
+        x("shl.b32 %idn, %idn, 17;")
+        x(f"or.b32 %idesc, %idn, {idesc_n0};")
     x(f"mad.lo.u32 {r('dtm')}, %ab, {p.bn}, %tmem;")
     x("mov.u32 %kb, 0;")
     x(f"{m_k}:")
@@ -813,16 +909,26 @@ def emit(p: MatmulPlan) -> str:
     if p.staged:
         # this warp's rows of C start at m0 + quad*32; its blocks at columns nt*BN + 32*chunk
         x(f"mad.lo.u32 {r('srow')}, %quad, {STAGE_BLOCK}, %m0;")
-        x(f"mul.lo.u32 {r('scol')}, %nt, {p.bn};")
+        if mixed:
+            x(f"mov.u32 {r('scol')}, %col;")
+        else:
+            x(f"mul.lo.u32 {r('scol')}, %nt, {p.bn};")
     else:
         x(f"mad.lo.u32 {r('row')}, %quad, 32, %lane;")
         x("add.u32 %row, %row, %m0;")
         x(f"mul.wide.u32 {r('crow', u64)}, %row, {p.n * 4};")
-        x(f"mul.lo.u32 %n0, %nt, {p.bn * 4};")
+        if mixed:
+            x("shl.b32 %n0, %col, 2;")
+        else:
+            x(f"mul.lo.u32 %n0, %nt, {p.bn * 4};")
         x(f"cvt.u64.u32 {r('ncol64', u64)}, %n0;")
         x("add.s64 %crow, %crow, %ncol64;")
         x("add.s64 %crow, %crow, %c_ptr;")
+    chunks_done = x.label("chunks_done")
     for chunk in range(p.bn // 32):
+        if mixed and chunk >= 2:  # a tile of width wid has wid/32 blocks (64 at the least)
+            x(f"setp.le.u32 %p, %wid, {chunk * 32};")
+            x(f"@%p bra {chunks_done};")
         x(f"add.u32 {r('tcol')}, %taddr, {chunk * 32};")
         x(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(vals)}}}, [%tcol];")
         x("tcgen05.wait::ld.sync.aligned;")
@@ -836,6 +942,8 @@ def emit(p: MatmulPlan) -> str:
                 x(f"red.global.add.v4.f32 [%crow+{off}], {{{quad}}};")
             else:
                 x(f"st.global.v4.b32 [%crow+{off}], {{{quad}}};")
+    if mixed:
+        x(f"{chunks_done}:")
     x("tcgen05.fence::before_thread_sync;")
     x("mad.lo.u32 %tebar, %ab, 8, %bars;")
     x(f"add.u32 %tebar, %tebar, {tempty};")
@@ -865,10 +973,15 @@ def emit(p: MatmulPlan) -> str:
 
     # --- module ------------------------------------------------------------------------------
     sched_words = []
-    for mt, nt, kb0, cnt in table:
-        if max(mt, nt, kb0, cnt) >= 1 << 16:
+    kbs = p.k // BK
+    # mixed widths: (band | first column / 32 << 16, width | K blocks << 16); else
+    # (m tile | n tile << 16, first K block | K blocks << 16)
+    words = ([(mt, col // 32, w, kbs if w else 0) for mt, col, w in table] if mixed
+             else table)
+    for w0, w1, w2, w3 in words:
+        if max(w0, w1, w2, w3) >= 1 << 16:
             raise NotImplementedError("matmul template: more tiles than the schedule encodes")
-        sched_words += [str(mt | nt << 16), str(kb0 | cnt << 16)]
+        sched_words += [str(w0 | w1 << 16), str(w2 | w3 << 16)]
     rows = [", ".join(sched_words[i:i + 16]) for i in range(0, len(sched_words), 16)]
     params = ",\n".join(f"\t.param .u64 {e}_param_{q}" for q in p.params)
     decls = "\n".join(f"\t.reg .{t} %m_{n};" for n, t in x.regs.items())
@@ -885,7 +998,8 @@ def emit(p: MatmulPlan) -> str:
         *([f"// @ptxgen tensormap symbol={e}_tmap_c buffer={p.c} dtype=f32 dims={p.n},{p.m} "
            f"strides={p.n * 4} box={STAGE_BLOCK},{STAGE_BLOCK} swizzle=128"] if p.staged else []),
         f"// @ptxgen matmul m={p.m} n={p.n} k={p.k} bn={p.bn} splits={p.splits} "
-        f"stages={stages} tiles={p.tiles} segments={entries} cta_group={g}",
+        f"stages={stages} tiles={p.tiles} segments={entries} cta_group={g}"
+        + (" widths=mixed" if mixed else ""),
         "",
         f".version {PTX_VERSION}\n.target {TARGET}\n.address_size 64\n",
         ".extern .shared .align 1024 .b8 smem_pool[];",

@@ -48,8 +48,9 @@ def test_shipped_compiles_and_assembles(name: str, flags: dict, tmp_path) -> Non
 
 
 # The two forms of TMA load the kernels may issue: each CTA fills its own shared memory, and in
-# a CTA pair (cta_group::2) signals the pair leader's barrier. Neither form multicasts.
-TMA_LOAD = re.compile(r"^\s*cp\.async\.bulk\.tensor\.2d\.(shared::cluster\.global\.tile|"
+# a CTA pair (cta_group::2) signals the pair leader's barrier. Neither form multicasts. A load
+# may be predicated (a mixed-width GEMM skips a chunk of B that a narrow tile does not use).
+TMA_LOAD = re.compile(r"^\s*(@%\w+ )?cp\.async\.bulk\.tensor\.2d\.(shared::cluster\.global\.tile|"
                       r"cta_group::2\.shared::cluster\.global)"
                       r"\.mbarrier::complete_tx::bytes \[%\w+\], \[%\w+, \{%\w+, %\w+\}\], "
                       r"\[%\w+\];$")
@@ -375,6 +376,71 @@ def test_splitk_config_fills_the_sms() -> None:
     """Config 5b (16 pair tiles of 1024 K blocks): 9 splits, two full waves over 74 SM pairs."""
     table, ctas = gemm_plan(problems.CONFIGS["c5b_matmul_splitk"]()).segments()
     assert (len(table), ctas) == (144, 148)
+
+
+def proportional(monkeypatch) -> None:
+    """A cost model in which a tile's K block takes time in proportion to its width: the one
+    that makes the planner cut a part-full last wave into mixed widths."""
+    from ptxgen.templates import matmul
+
+    monkeypatch.setattr(matmul, "K_BLOCK_TIME", {w: w / 256 for w in matmul.K_BLOCK_TIME})
+
+
+@pytest.mark.parametrize("shape,scaled", [((512, 512, 512), False), ((1024, 1024, 1024), False),
+                                          ((256, 256, 256), False), ((1024, 8192, 8192), True),
+                                          ((2048, 8192, 8192), True), ((1280, 512, 256), True),
+                                          ((4096, 4096, 2048), True)])
+def test_gemm_mixed_widths_cover_c_once(shape, scaled, monkeypatch) -> None:
+    """The mixed-width table (under the measured cost model, or a width-proportional one that
+    cuts part-full last waves): every column of every 256-row band of C in exactly one tile;
+    widths from 256 and ``NARROW``, each tile inside C and starting on a 32-column boundary (the
+    table stores column / 32; TMA wants 16-byte starts); entry r * used + q is pair q's r-th
+    tile, and the longest pair's work (in the planner's own cost) is below whole tiles' waves."""
+    from collections import Counter
+
+    from ptxgen.templates import matmul
+    from ptxgen.templates.matmul import BK, MIXED_GAIN, NARROW, SEGMENT_COST, SM_COUNT
+
+    if scaled:
+        proportional(monkeypatch)
+    m, n, k = shape
+    p = gemm_plan(problems.matmul(m, n, k))
+    table, ctas = p.columns()
+    used = ctas // 2
+    assert used <= SM_COUNT // 2 and len(table) % used == 0
+    cover = Counter()
+    work = [0.0] * used
+    kbs = k // BK
+    for i, (band, col, w) in enumerate(table):
+        if not w:
+            continue
+        assert w in (256, *NARROW) and col % 32 == 0 and col + w <= n and band < m // 256
+        cover.update((band, c) for c in range(col, col + w))
+        work[i % used] += kbs * matmul.K_BLOCK_TIME[w] + SEGMENT_COST
+    assert set(cover.values()) == {1} and len(cover) == (m // 256) * n
+    whole = -(-(m // 256) * (n // 256) // (SM_COUNT // 2)) * (kbs + SEGMENT_COST)
+    assert max(work) <= (1 - MIXED_GAIN) * whole
+
+
+def test_config5_shares_tile_widths(monkeypatch) -> None:
+    """Config 5's kernel and every share of it keep whole 256-column tiles: a narrower tile runs
+    a K block in nearly a whole tile's time on a B200, so cutting the part-full last wave of the
+    1/4 and 1/8 shares (256 and 128 tiles over 74 pairs) gains nothing (measured: 96.6 against
+    96.4 us at 1/8). Under a width-proportional model the planner would give the longest pair
+    3.5 and 1.75 tiles' worth instead of 4 and 2."""
+    from ptxgen import shard
+
+    def longest(share: int) -> float:
+        table, ctas = gemm_plan(shard.local_problem("c5_matmul", share).spec).columns()
+        cols = [0] * (ctas // 2)
+        for i, (_, _, w) in enumerate(table):
+            cols[i % len(cols)] += w
+        return max(cols) / 256
+
+    for share in (1, 2, 4, 8):
+        assert gemm_plan(shard.local_problem("c5_matmul", share).spec).columns() is None
+    proportional(monkeypatch)
+    assert (longest(4), longest(8)) == (3.5, 1.75)
 
 
 def _normalised(lines: list[str]) -> list[str]:

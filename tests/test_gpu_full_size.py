@@ -123,19 +123,22 @@ def test_c4_full_size_against_f64(cuda) -> None:
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("key", ["c5_matmul", "c5b_matmul_splitk"])
+@pytest.mark.parametrize("key", ["c5_matmul", "c5b_matmul_splitk", "c5_matmul/4", "c5_matmul/8"])
 def test_gemm_full_size_rows(cuda, key: str) -> None:
-    """Config 5 at 8192^3: the picked rows of C (first, last and 16 seeded picks); config 5b
+    """Config 5 at 8192^3, and the 1/4 and 1/8 shares one rank of a strong-scaled run holds
+    (2048 and 1024 rows): the picked rows of C (first, last and 16 seeded picks); config 5b
     (1024 x 1024 x 65536, split-K): every row of C. Each against the f64 product of the same
     bf16 operands, at the GEMM bar."""
     from test_gpu_gemm import assert_gemm_close
 
     from oracle.fp import bf16_bits_to_f32
+    from ptxgen import shard
 
-    spec = problems.CONFIGS[key]()
+    name, _, share = key.partition("/")
+    spec = shard.local_problem(name, int(share or 1)).spec
     ins = reference_inputs(spec.meta)
     got = gpu_run(spec.graph, spec.meta, ins)["matmul"]
-    rows = picked_rows(got.shape[0]) if key == "c5_matmul" else np.arange(got.shape[0])
+    rows = picked_rows(got.shape[0]) if name == "c5_matmul" else np.arange(got.shape[0])
     a = bf16_bits_to_f32(ins["x0"][rows]).astype(np.float64)
     b = bf16_bits_to_f32(ins["x1"]).astype(np.float64)
     worst = assert_gemm_close(got[rows], a @ b)

@@ -59,10 +59,11 @@ CASES = {
 }
 
 
-def template_ptx(spec: problems.ProblemSpec, staged: bool) -> str:
+def template_ptx(spec: problems.ProblemSpec, staged: bool, mixed: bool = True) -> str:
     """The GEMM template's module for ``spec`` with the chosen epilogue: staged (each warp's
     32 x 32 blocks through shared memory, one TMA store or reduce-add per block; the default)
-    or per thread (``st.global.v4`` / ``red.global.add.v4`` from registers)."""
+    or per thread (``st.global.v4`` / ``red.global.add.v4`` from registers). ``mixed=False``
+    keeps whole 256-column tiles where the template would cut some narrower."""
     import dataclasses
 
     from ptxgen.compiler import kernel_for_meta
@@ -76,7 +77,7 @@ def template_ptx(spec: problems.ProblemSpec, staged: bool) -> str:
     plan = matmul.match(op, bufs, launch["arg_order"], launch["block"][0],
                         int(launch.get("smem_bytes", 0)))
     assert plan is not None
-    return matmul.emit(dataclasses.replace(plan, staged=staged))
+    return matmul.emit(dataclasses.replace(plan, staged=staged, mixed=mixed))
 
 
 @pytest.mark.parametrize("staged", [True, False], ids=["staged", "per_thread"])
@@ -92,6 +93,41 @@ def test_tcgen05_gemm(cuda, key: str, staged: bool) -> None:
     a, b = operands(spec, ins)
     worst = assert_gemm_close(got, a @ b)
     print(f"{key} ({'staged' if staged else 'per thread'}): max |err| / max |C| = {worst:.3e}")
+
+
+MIXED = {
+    # (problem, cost model): the planner's own choice with the measured K-block times, or a
+    # width-proportional model that cuts the part-full last wave into mixed widths
+    "64_wide": (lambda: problems.matmul(256, 256, 256), False),  # four 64-column tiles
+    "64_wide_1024": (lambda: problems.matmul(1024, 1024, 1024), False),
+    # config 5's 1/8 share layout (one 256- and one 192-column tile per pair) and its 1/4 share
+    # layout (two of each), at K = 1024
+    "share8_256_192": (lambda: problems.matmul(1024, 8192, 1024), True),
+    "share4_256_192": (lambda: problems.matmul(2048, 8192, 1024), True),
+    "128_wide_raster": (lambda: problems.matmul(1280, 512, 256, raster_group=4), True),
+}
+
+
+@pytest.mark.parametrize("key", sorted(MIXED))
+def test_mixed_widths_match_whole_tiles(cuda, key: str, monkeypatch) -> None:
+    """The mixed-width table against whole 256-column tiles on the same operands: bit for bit
+    (every element is one tile's whole K loop in the same K order either way), and at the GEMM
+    bar against the f64 product."""
+    from ptxgen.templates import matmul
+
+    build, scaled = MIXED[key]
+    spec = build()
+    if scaled:
+        monkeypatch.setattr(matmul, "K_BLOCK_TIME", {w: w / 256 for w in matmul.K_BLOCK_TIME})
+    mixed, whole = template_ptx(spec, True), template_ptx(spec, True, mixed=False)
+    assert "widths=mixed" in mixed and "widths=mixed" not in whole
+    ins = reference_inputs(spec.meta)
+    got = gpu_run(spec.graph, spec.meta, ins, guard=64, ptx=mixed)["matmul"]
+    ref = gpu_run(spec.graph, spec.meta, ins, guard=64, ptx=whole)["matmul"]
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+    a, b = operands(spec, ins)
+    worst = assert_gemm_close(got, a @ b)
+    print(f"{key}: bit-equal to whole tiles; max |err| / max |C| = {worst:.3e}")
 
 
 def test_tcgen05_matches_oracle_small(cuda) -> None:
