@@ -35,6 +35,7 @@ from .ir import (Accum, Assign, BinaryExpr, CastExpr, Cond, CpAsyncCommit, CpAsy
                  Select, Smem, Stmt, StridedLoop, Sync, TernaryExpr, Tile, TreeHalve, Var,
                  WarpShuffle, Write, walk)
 from .ops import Val
+from .pipeline import Pipe
 from .ptx import BUFFER_ALIGN, SM_COUNT, Ins, Kernel, pow2_part
 
 UNROLL_BUDGET = 6144  # instructions a loop may fully unroll to
@@ -913,7 +914,9 @@ class Lowering:
             with self._block():
                 self.env[s.axis.name] = Aff.of(i)
                 self.body(s.body)
-        self._prefetch_ahead(mark, top_label, i, const_step, end_op)
+        prefetch = self._prefetch_ahead(mark, top_label, i, const_step, end_op)
+        pre = Ins(text="")  # where the preheader ends, for the load pipeline pass
+        k.body.insert(mark.at, pre)
         k.ranges.pop(i, None)
         again = k.reg("pred")
         for ptr, delta in mark.incs:
@@ -921,31 +924,39 @@ class Lowering:
         k.emit("add.u32", (i,), (i, step_op))
         k.emit("setp.lt.s32", (again,), (i, end_op))
         k.emit("bra", src=(top,), pred=again, barrier=True)
+        if k.min_ctas == 1 and const_step > 0 and mark.incs:
+            # a single-wave loop's trips wait on their own loads: issue them trips ahead
+            k.pipes.append(Pipe(pre, top_label, k.body[-1], i, const_step, end_op,
+                                dict(mark.incs), prefetch))
+        k.markers.append(pre)
         k.place(done)
 
-    def _prefetch_ahead(self, mark: Any, top_label: Any, i: str, step: int, end_op: str) -> None:
+    def _prefetch_ahead(self, mark: Any, top_label: Any, i: str, step: int, end_op: str
+                        ) -> list[Ins]:
         """In a single-wave kernel a runtime loop's trips wait on their own loads: one body per
         trip, each load feeding that trip's arithmetic, and too few warps per SM to cover the
         latency. So each read-only global load that walks an induction pointer is prefetched
         into L1 ``PREFETCH_TRIPS`` trips ahead, at the top of the body, where the counter then
         stands; the trip's own load then finds its line in L1. The prefetch is predicated on
         that trip existing, so it never reaches past the loop's end. It moves no data into
-        registers and changes no result."""
+        registers and changes no result. Returns the inserted code (the load pipeline pass
+        removes it where its copies cover the same loads)."""
         k = self.k
         if k.min_ctas != 1 or step <= 0 or not mark.incs:
-            return
+            return []
         start = next(n for n, ins in enumerate(k.body) if ins is top_label)
         loaded = {ins.mem.addr for ins in k.body[start:]
                   if ins.mem is not None and ins.mem.kind == "ld" and ins.mem.space == "global.nc"}
         streams = [(ptr, delta) for ptr, delta in mark.incs if ptr in loaded]
         if not streams:
-            return
+            return []
         ahead, exists = k.reg("u32"), k.reg("pred")
         code = [Ins("add.u32", (ahead,), (i, str(PREFETCH_TRIPS * step))),
                 Ins("setp.lt.s32", (exists,), (ahead, end_op))]
         code += [Ins("prefetch.global.L1", (), (f"[{ptr}+{PREFETCH_TRIPS * delta}]",), exists)
                  for ptr, delta in streams]
         k.body[start + 1:start + 1] = code
+        return code
 
     def _trips(self, start: Aff, step: Aff, end: Aff, stmts: Sequence[Stmt]
                ) -> tuple[int, int] | None:

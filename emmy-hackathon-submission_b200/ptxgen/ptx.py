@@ -130,6 +130,8 @@ class Kernel:
         self.extern_shared: tuple[str, int] | None = None
         self.reqntid: int | None = None
         self.min_ctas: int | None = None
+        self.pipes: list = []  # runtime loops whose loads the pipeline pass issues ahead
+        self.markers: list[Ins] = []  # placeholder lines the render drops
         self._counts: dict[str, int] = {}
         self._labels = 0
         self._scopes: list[dict[tuple[str, ...], str]] = [{}]
@@ -361,9 +363,14 @@ class Kernel:
     def render(self) -> str:
         from .slp import SLP
 
+        from .pipeline import pipeline_loads
+
         self.drop_dead()
         self.vectorize()
         self.drop_dead()
+        pipeline_loads(self, self.pipes)
+        drop = {id(m) for m in self.markers}
+        self.body = [ins for ins in self.body if id(ins) not in drop]
         if not self.no_cse:  # pairing reuses values across copies, as CSE does
             self.body = SLP(self).run(self.body)
             self.drop_dead()

@@ -294,31 +294,49 @@ def test_launch_notes_give_the_module_its_shared_memory() -> None:
     assert "ret;" in head  # a short launch leaves before any barrier exists
 
 
-def test_single_wave_runtime_loops_prefetch_ahead(tmp_path) -> None:
+def test_single_wave_runtime_loops_copy_ahead(tmp_path) -> None:
     """The shipped r02 (one 128-thread block summing 65,536 floats) with unrolling off: its
-    rolled loop prefetches each trip's read-only load into L1 sixteen trips ahead, through the
-    same induction pointer plus sixteen trips' worth of bytes, predicated on that trip
-    existing. The default build unrolls instead and has no prefetch; neither has a grid of more
-    than one wave."""
+    rolled loop reads each trip's value from a shared-memory ring that ``cp.async`` fills
+    ``DEPTH - 1`` trips ahead. In front of the loop, trips 0 .. DEPTH-2 are copied (trip j > 0
+    only where it exists), one commit group each. Each trip waits for its own group
+    (``wait_group DEPTH-2``), copies trip t + DEPTH - 1 (where it exists) through the same
+    induction pointer into the slot trip t - 1 read, and reads its value with one
+    ``ld.shared``; the loop still adds one value per trip, in trip order, and waits for every
+    copy after it. The ring replaces the L1 prefetch. The default build unrolls instead; a
+    kernel of several waves gets neither."""
     import re
 
-    from ptxgen.lower import PREFETCH_TRIPS
+    from ptxgen.pipeline import DEPTH
 
     graph, meta = shipped("r02_big_sum")
     rolled = to_ptx(Graph.from_dict(graph), meta, no_unroll=True)
-    loop = rolled[rolled.index("$L_loop"):rolled.index("$L_loop_end")]
-    pf = re.search(r"@(%p\d+) prefetch\.global\.L1 \[(%rd\d+)\+(\d+)\];", loop)
-    assert pf is not None, loop
-    ld = re.search(r"ld\.global\.nc\.f32 %f\d+, \[(%rd\d+)\];", loop)
-    step = re.search(r"add\.s64 (%rd\d+), %rd\d+, (\d+);", loop)
-    assert ld.group(1) == pf.group(2) == step.group(1)
-    assert int(pf.group(3)) == PREFETCH_TRIPS * int(step.group(2))
-    guard = re.search(rf"setp\.lt\.s32 {re.escape(pf.group(1))}, %r\d+, (\d+);", loop)
-    assert guard is not None and guard.group(1) == "65536"
-    assert loop.index("prefetch") < loop.index("ld.global.nc")
-    assert "prefetch" not in to_ptx(Graph.from_dict(graph), meta)
+    loop = rolled[rolled.index("$L_loop_1:"):rolled.index("$L_loop_end")]
+    head = rolled[:rolled.index("$L_loop_1:")]
+    assert "prefetch" not in rolled and "ld.global" not in loop
+    assert re.search(r"\.shared \.align 16 \.b8 k_sum_1_reduce_ring0\[(\d+)\];", rolled).group(1) \
+        == str(DEPTH * 128 * 4)
+    fills = re.findall(r"(@%p\d+ )?cp\.async\.ca\.shared\.global \[%r\d+\+(\d+)\], "
+                       r"\[%rd\d+\+(\d+)\], 4;", head)
+    assert [(bool(p), int(d), int(s)) for p, d, s in fills] == \
+        [(j > 0, j * 512, j * 512) for j in range(DEPTH - 1)]
+    assert head.count("cp.async.commit_group") == DEPTH - 1
+    assert loop.index(f"cp.async.wait_group {DEPTH - 2};") < loop.index("ld.shared.f32")
+    refill = re.search(r"@(%p\d+) cp\.async\.ca\.shared\.global \[%r\d+\+0\], "
+                       r"\[(%rd\d+)\+(\d+)\], 4;", loop)
+    step = re.search(r"add\.s64 (%rd\d+), %rd\d+, 512;", loop)
+    assert refill and refill.group(2) == step.group(1) and int(refill.group(3)) == (DEPTH - 1) * 512
+    guard = re.search(rf"setp\.lt\.s32 {re.escape(refill.group(1))}, (%r\d+), 65536;", loop)
+    assert guard and re.search(rf"add\.u32 {re.escape(guard.group(1))}, %r\d+, "
+                               rf"{(DEPTH - 1) * 128};", loop)
+    assert loop.count("cp.async.commit_group") == 1 and loop.count("add.rn.f32") == 1
+    value = re.search(r"ld\.shared\.f32 (%f\d+), \[%r\d+\];", loop).group(1)
+    assert re.search(rf"add\.rn\.f32 (%f\d+), \1, {re.escape(value)};", loop)
+    after = rolled[rolled.index("@%p1 bra $L_loop_1;"):rolled.index("$L_loop_end")]
+    assert "cp.async.wait_all" in after
+    default = to_ptx(Graph.from_dict(graph), meta)
+    assert "cp.async" not in default and "$L_loop" not in default
     wide = compile_spec(problems.CONFIGS["c4_full_sum"]())  # 1184 blocks: several waves
-    assert "prefetch" not in wide
+    assert "cp.async" not in wide and "prefetch" not in wide
     ptxas(rolled, tmp_path)
 
 
@@ -539,7 +557,8 @@ def test_flat_runtime_loops_step_induction_pointers() -> None:
     live beside the outer loop's state, and ptxas spilled."""
     graph, meta = shipped("r02_big_sum")
     body = _loop_bodies(to_ptx(Graph.from_dict(graph), meta, no_unroll=True))[0]
-    assert body.count("ld.global.nc.f32") == 1 and body.count("add.s64") == 1
+    # the trip's value comes from the copy ring the pointer feeds (see the copy-ahead test)
+    assert body.count("ld.shared.f32") == 1 and body.count("add.s64") == 1
     assert not {"mul.wide.u32", "mad.lo.u32"} & set(body)
     step = re.search(r"add\.s64 (%rd\d+), \1, (\d+);", compile_spec(problems.full_sum(1 << 30)))
     assert step and int(step.group(2)) % (148 * 8 * 256 * 4) == 0
