@@ -80,6 +80,9 @@ def parse_args() -> argparse.Namespace:
                    help="steps of the host-buffer (e2e) path in flight at once, one stream each")
     p.add_argument("--only", default=None,
                    help="with --ablation: time only this shipped example (e.g. m01_matmul_512)")
+    p.add_argument("--flags", default=None, choices=("default", "no_loop_unroll", "no_fusion",
+                                                     "no_cse"),
+                   help="with --ablation: time only this flag set")
     p.add_argument("--cpu-seconds", type=float, default=12.0,
                    help="target seconds of CPU work for the CPU baseline sample")
     return p.parse_args()
@@ -1008,6 +1011,8 @@ def run_ablation(args: argparse.Namespace) -> None:
         meta = json.loads((d / "meta.json").read_text())
         row: dict[str, Any] = {"problem": d.name}
         for label, flags in ABLATION_FLAGS.items():
+            if args.flags and label != args.flags:
+                continue
             prob = Problem(graph, meta, flags=flags)
             tensors = prob.allocate()
             for i, a in enumerate(prob.launch_entry["args"]):

@@ -31,12 +31,13 @@ def compile_module(op: KernelOp, buffers: Mapping[str, Buffer], arg_order: Seque
         ptx = tpl.try_templates(op, buffers, arg_order, block_threads, smem_bytes)
         if ptx is not None:
             return ptx
-    if not no_unroll:  # sibling loops over one axis, trip by trip (``jam``)
-        from dataclasses import replace
+    # sibling loops over one axis, trip by trip (``jam``); with unrolling off the jammed loop is
+    # still a runtime loop with one body per trip
+    from dataclasses import replace
 
-        from .jam import jam
+    from .jam import jam
 
-        op = replace(op, body=replace(op.body, body=jam(op.body.body)))
+    op = replace(op, body=replace(op.body, body=jam(op.body.body)))
     k = Lowering(op, buffers, arg_order, block_threads, no_unroll=no_unroll,
                  no_fusion=no_fusion, no_cse=no_cse, exchange=exchange).run()
     return k.render()

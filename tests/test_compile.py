@@ -540,10 +540,10 @@ def test_simt_matmul_reads_shared_memory_in_vectors() -> None:
 def _loop_bodies(ptx: str) -> list[list[str]]:
     """The instruction mnemonics of each innermost runtime loop, in order."""
     out = []
-    for m in re.finditer(r"(\$L_loop_\d+):\n(.*?)\n\$L_loop_end_\d+:", ptx, re.S):
+    # a body that holds no other loop's label: from a loop's top to the first loop end after it
+    for m in re.finditer(r"(\$L_loop_\d+):\n((?:(?!\$L_loop_\d+:).)*?)\n\$L_loop_end_\d+:", ptx,
+                         re.S):
         lines = [ln.strip() for ln in m.group(2).splitlines()]
-        if any(ln.startswith("$L_loop_") for ln in lines):
-            continue
         out.append([ln.split()[0] for ln in lines if ln and not ln.startswith(("$", "//"))])
     return out
 
