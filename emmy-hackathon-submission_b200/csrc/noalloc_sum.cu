@@ -18,11 +18,10 @@
 // array and must not be made.
 //
 // Host code cannot use the array's name as a device address (there it names a host-side stand-in
-// for the symbol). The first call on each device, with that device current, asks the runtime for
-// the array's device address (cudaGetSymbolAddress) and keeps it; that set-up may load this
-// library's module, so the first call on a device should come before any stream capture. The
-// kept address belongs to the device's primary context: after cudaDeviceReset on a device the
-// module is loaded again elsewhere, and the library must not be called on that device again.
+// for the symbol). Every call asks the runtime for the array's device address in the current
+// context (cudaGetSymbolAddress); the first call on a device may load this library's module, so
+// it should come before any stream capture. Nothing is kept between calls, so a call after
+// cudaDeviceReset finds the array where the module was loaded again.
 //
 // The summation order is the emitted kernels': each thread adds its grid-stride share in index
 // order, a warp combines its lanes by the xor butterfly of strides 16..1 (v = v + other), the
@@ -33,7 +32,6 @@
 
 #include <cstdint>
 #include <cstdio>
-#include <mutex>
 
 #include "../../include/ptxgen_b200.h"
 
@@ -44,7 +42,6 @@ namespace {
 
 constexpr int kBlock = PG_GRID_SUM_BLOCK;
 constexpr int kWarps = kBlock / 32;
-constexpr int kMaxDevices = 64;
 // block_sum's second stage is an xor butterfly over one warp's lanes from kWarps / 2 down: it
 // needs whole warps, at most 32 of them, a power of two
 static_assert(kBlock % 32 == 0 && kWarps >= 1 && kWarps <= 32 && (kWarps & (kWarps - 1)) == 0,
@@ -92,30 +89,20 @@ __global__ void __launch_bounds__(kBlock) grid_sum_final(const float *__restrict
   if (threadIdx.x == 0) out[0] = total;
 }
 
-std::mutex g_setup_mu;
-float *g_scratch[kMaxDevices] = {};
-
 int runtime_fail(cudaError_t e, const char *what) {
   char buf[512];
   snprintf(buf, sizeof buf, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
   return pg_detail_fail(PG_ERR_RUNTIME, buf);
 }
 
-// The device address of g_partials on the current device, looked up once per device.
+// The device address of g_partials in the current context, looked up on every call (a host-side
+// table lookup that allocates nothing), so a call after the context was reset and the module
+// loaded again gets the new address.
 int scratch_address(float **out) {
-  int dev = -1;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return runtime_fail(e, "cudaGetDevice");
-  if (dev < 0 || dev >= kMaxDevices)
-    return pg_detail_fail(PG_ERR_ARGUMENT, "pg_grid_sum_f32_noalloc: device index out of range");
-  std::lock_guard<std::mutex> lock(g_setup_mu);
-  if (!g_scratch[dev]) {
-    void *p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_partials);
-    if (e != cudaSuccess) return runtime_fail(e, "cudaGetSymbolAddress(g_partials)");
-    g_scratch[dev] = static_cast<float *>(p);
-  }
-  *out = g_scratch[dev];
+  void *p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_partials);
+  if (e != cudaSuccess) return runtime_fail(e, "cudaGetSymbolAddress(g_partials)");
+  *out = static_cast<float *>(p);
   return PG_OK;
 }
 

@@ -158,11 +158,9 @@ int pg_run_host(pg_kernel *kernel, uint32_t grid, uint32_t block, uint32_t smem_
  * library's module is loaded until the process exits) and allocates nothing. It does make CUDA
  * calls itself (it launches two kernels), so it must not be called from a host function
  * enqueued on a stream (cudaLaunchHostFunc), where CUDA forbids CUDA calls. blocks must be
- * 1..PG_GRID_SUM_MAX_BLOCKS, else PG_ERR_ARGUMENT. The first call on a device looks up the
- * array's device address with that device current (it may load the module) and keeps it for
- * the process: make that first call before any stream capture, and make no call on a device
- * after cudaDeviceReset there (the kept address belongs to the context that the reset
- * destroyed). All calls share the array, so calls that overlap on the GPU (other streams, other
+ * 1..PG_GRID_SUM_MAX_BLOCKS, else PG_ERR_ARGUMENT. Every call looks up the array's device
+ * address in the current context; the first call on a device may load the module, so make it
+ * before any stream capture. All calls share the array, so calls that overlap on the GPU (other streams, other
  * threads) race and must not be made. Runtime failures return PG_ERR_RUNTIME. */
 #define PG_GRID_SUM_BLOCK 256
 #define PG_GRID_SUM_MAX_BLOCKS 4096

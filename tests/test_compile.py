@@ -296,14 +296,14 @@ def test_launch_notes_give_the_module_its_shared_memory() -> None:
 
 def test_single_wave_runtime_loops_copy_ahead(tmp_path) -> None:
     """The shipped r02 (one 128-thread block summing 65,536 floats) with unrolling off: its
-    rolled loop reads each trip's value from a shared-memory ring that ``cp.async`` fills
-    ``DEPTH - 1`` trips ahead. In front of the loop, trips 0 .. DEPTH-2 are copied (trip j > 0
-    only where it exists), one commit group each. Each trip waits for its own group
-    (``wait_group DEPTH-2``), copies trip t + DEPTH - 1 (where it exists) through the same
-    induction pointer into the slot trip t - 1 read, and reads its value with one
-    ``ld.shared``; the loop still adds one value per trip, in trip order, and waits for every
-    copy after it. The ring replaces the L1 prefetch. The default build unrolls instead; a
-    kernel of several waves gets neither."""
+    rolled loop takes each trip's value from a shared-memory ring that ``cp.async`` fills
+    ``DEPTH - 1`` trips ahead, read into registers one trip ahead. In front of the loop, trips
+    0 .. DEPTH-2 are copied (trip j > 0 only where it exists), one commit group each, and trip
+    0's slot is read once its group has landed. Each trip takes the value read ahead, waits for
+    trip t + 1's group (``wait_group DEPTH-3``) and reads its slot, copies trip t + DEPTH - 1
+    (where it exists) through the same induction pointer into trip t - 1's slot, and adds one
+    value, in trip order; the loop waits for every copy after it. The ring replaces the L1
+    prefetch. The default build unrolls instead; a kernel of several waves gets neither."""
     import re
 
     from ptxgen.pipeline import DEPTH
@@ -320,7 +320,14 @@ def test_single_wave_runtime_loops_copy_ahead(tmp_path) -> None:
     assert [(bool(p), int(d), int(s)) for p, d, s in fills] == \
         [(j > 0, j * 512, j * 512) for j in range(DEPTH - 1)]
     assert head.count("cp.async.commit_group") == DEPTH - 1
-    assert loop.index(f"cp.async.wait_group {DEPTH - 2};") < loop.index("ld.shared.f32")
+    first = re.search(rf"cp\.async\.wait_group {DEPTH - 2};\n\tld\.shared\.f32 (%f\d+), "
+                      r"\[%r\d+\];", head)
+    assert first, head[-600:]
+    ahead = first.group(1)
+    # the trip's value is the one read ahead; then trip t + 1's slot is read into its place
+    value = re.search(rf"mov\.f32 (%f\d+), {re.escape(ahead)};", loop).group(1)
+    assert loop.index(f"mov.f32 {value}") < loop.index(f"cp.async.wait_group {DEPTH - 3};") < \
+        loop.index(f"ld.shared.f32 {ahead}, ")
     refill = re.search(r"@(%p\d+) cp\.async\.ca\.shared\.global \[%r\d+\+0\], "
                        r"\[(%rd\d+)\+(\d+)\], 4;", loop)
     step = re.search(r"add\.s64 (%rd\d+), %rd\d+, 512;", loop)
@@ -329,7 +336,6 @@ def test_single_wave_runtime_loops_copy_ahead(tmp_path) -> None:
     assert guard and re.search(rf"add\.u32 {re.escape(guard.group(1))}, %r\d+, "
                                rf"{(DEPTH - 1) * 128};", loop)
     assert loop.count("cp.async.commit_group") == 1 and loop.count("add.rn.f32") == 1
-    value = re.search(r"ld\.shared\.f32 (%f\d+), \[%r\d+\];", loop).group(1)
     assert re.search(rf"add\.rn\.f32 (%f\d+), \1, {re.escape(value)};", loop)
     after = rolled[rolled.index("@%p1 bra $L_loop_1;"):rolled.index("$L_loop_end")]
     assert "cp.async.wait_all" in after
