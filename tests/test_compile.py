@@ -364,12 +364,15 @@ def gemm_plan(spec: problems.ProblemSpec):
                                    (128, 1024, 65536, 32), (640, 768, 4096, 2)])
 def test_gemm_segments_cover_every_k_block_once(shape) -> None:
     """The template's work table: every K block of every output tile exactly once; a plain GEMM
-    keeps the IR's tile order; a split-K GEMM goes split-major over the IR's tiles, with splits of
-    at least MIN_SEGMENT K blocks that differ by at most one, in as few waves of SM_COUNT CTAs as
-    its split count needs."""
+    takes its tiles in the template's grouped raster (groups of isqrt(CTAs at once) tile rows,
+    rows fastest); a split-K GEMM goes split-major over the IR's tiles, with splits of at least
+    MIN_SEGMENT K blocks that differ by at most one, in as few waves of SM_COUNT CTAs as its
+    split count needs."""
     from collections import Counter
 
-    from ptxgen.templates.matmul import BK, MIN_SEGMENT, SM_COUNT
+    import math
+
+    from ptxgen.templates.matmul import BK, MIN_SEGMENT, SM_COUNT, raster
 
     m, n, k, split = shape
     kw = {"split_k": split, "raster_group": None} if split > 1 else {}
@@ -386,8 +389,9 @@ def test_gemm_segments_cover_every_k_block_once(shape) -> None:
     assert set(seen.values()) == {1}
     order = list(dict.fromkeys((mt // rows, nt) for mt, nt, _ in p.schedule))
     if split == 1:
-        assert [(mt, nt) for mt, nt, _, _ in table] == order
-        assert ctas == len(table) * rows
+        want = raster(m // (128 * rows), n // p.bn, math.isqrt(SM_COUNT // rows))
+        assert [(mt, nt) for mt, nt, _, _ in table] == want == p.order()
+        assert sorted(want) == sorted(order) and ctas == len(table) * rows
         return
     splits = len(table) // len(order)
     assert [(mt, nt) for mt, nt, _, _ in table] == order * splits
