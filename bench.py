@@ -503,7 +503,11 @@ def measure_kernel(plan: Any, steps: int, warmup: int, world: int, l2: str = "cl
         peer.check()
     out = {"mean_ms": max_over_ranks(mean_ms, world),
            "median_ms": max_over_ranks(statistics.median(times), world),
-           "min_ms": max_over_ranks(min(times), world), "launches": steps,
+           "min_ms": max_over_ranks(min(times), world),
+           # this backend's kernels per step: the workload's own, and a zero kernel of its
+           # module for each zero_outputs buffer it clears in place of a memset
+           "launches": steps * (1 + sum(n in prob.module.zeroers
+                                        for n in prob.launch_entry.get("zero_outputs", []))),
            "clocks": sampler.summary(),
            "tensors": {**tensors, **{f"{n}@rows": t for n, t in rows_out.items()}},
            "prob": prob, "peer": peer, "slots": slots}

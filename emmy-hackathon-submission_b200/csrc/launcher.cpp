@@ -60,6 +60,7 @@ struct Driver {
                                    CUtensorMapSwizzle, CUtensorMapL2promotion,
                                    CUtensorMapFloatOOBfill);
   CUresult (*OccupancyMaxActiveClusters)(int *, CUfunction, const CUlaunchConfig *);
+  CUresult (*LaunchKernelEx)(const CUlaunchConfig *, CUfunction, void **, void **);
   CUresult (*EventCreate)(CUevent *, unsigned);
   CUresult (*EventRecord)(CUevent, CUstream);
   CUresult (*EventSynchronize)(CUevent);
@@ -110,6 +111,7 @@ int load_driver() {
   PG_SYM(CtxSynchronize, "cuCtxSynchronize")
   PG_SYM(TensorMapEncodeTiled, "cuTensorMapEncodeTiled")
   PG_SYM(OccupancyMaxActiveClusters, "cuOccupancyMaxActiveClusters")
+  PG_SYM(LaunchKernelEx, "cuLaunchKernelEx")
   PG_SYM(EventCreate, "cuEventCreate")
   PG_SYM(EventRecord, "cuEventRecord")
   PG_SYM(EventSynchronize, "cuEventSynchronize")
@@ -243,10 +245,17 @@ int pg_kernel_get(pg_module *module, const char *entry, pg_kernel **out) {
 
 int pg_kernel_launch(pg_kernel *kernel, uint32_t grid, uint32_t block, uint32_t smem_bytes,
                      uint64_t stream, const uint64_t *ptrs, int nptrs) {
+  return pg_kernel_launch_ex(kernel, grid, block, smem_bytes, stream, ptrs, nptrs, 0);
+}
+
+int pg_kernel_launch_ex(pg_kernel *kernel, uint32_t grid, uint32_t block, uint32_t smem_bytes,
+                        uint64_t stream, const uint64_t *ptrs, int nptrs, uint32_t flags) {
   if (!kernel || (nptrs > 0 && !ptrs) || nptrs < 0 || nptrs > 256)
     return fail(PG_ERR_ARGUMENT, "pg_kernel_launch: bad kernel or arguments");
   if (grid == 0 || block == 0 || block > 1024)
     return fail(PG_ERR_ARGUMENT, "pg_kernel_launch: grid %u block %u", grid, block);
+  if (flags & ~static_cast<uint32_t>(PG_LAUNCH_EARLY))
+    return fail(PG_ERR_ARGUMENT, "pg_kernel_launch_ex: unknown flags 0x%x", flags);
   int rc = ensure_current();
   if (rc) return rc;
   if (static_cast<int>(smem_bytes) > kernel->smem_optin) {
@@ -258,9 +267,29 @@ int pg_kernel_launch(pg_kernel *kernel, uint32_t grid, uint32_t block, uint32_t 
   std::vector<uint64_t> vals(ptrs, ptrs + nptrs);
   std::vector<void *> args(nptrs);
   for (int i = 0; i < nptrs; ++i) args[i] = &vals[i];
-  PG_CU(g_drv.LaunchKernel(kernel->fn, grid, 1, 1, block, 1, 1, smem_bytes,
-                           reinterpret_cast<CUstream>(stream), args.data(), nullptr),
-        "cuLaunchKernel");
+  if (!(flags & PG_LAUNCH_EARLY)) {
+    PG_CU(g_drv.LaunchKernel(kernel->fn, grid, 1, 1, block, 1, 1, smem_bytes,
+                             reinterpret_cast<CUstream>(stream), args.data(), nullptr),
+          "cuLaunchKernel");
+    return PG_OK;
+  }
+  // programmatic stream serialization: the kernel may start once the previous kernel on the
+  // stream has triggered (griddepcontrol.launch_dependents) or ended
+  CUlaunchAttribute attr;
+  std::memset(&attr, 0, sizeof attr);
+  attr.id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+  attr.value.programmaticStreamSerializationAllowed = 1;
+  CUlaunchConfig cfg;
+  std::memset(&cfg, 0, sizeof cfg);
+  cfg.gridDimX = grid;
+  cfg.gridDimY = cfg.gridDimZ = 1;
+  cfg.blockDimX = block;
+  cfg.blockDimY = cfg.blockDimZ = 1;
+  cfg.sharedMemBytes = smem_bytes;
+  cfg.hStream = reinterpret_cast<CUstream>(stream);
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  PG_CU(g_drv.LaunchKernelEx(&cfg, kernel->fn, args.data(), nullptr), "cuLaunchKernelEx");
   return PG_OK;
 }
 

@@ -63,6 +63,7 @@ def library() -> ctypes.CDLL:
                 "pg_module_unload": [vp],
                 "pg_kernel_get": [vp, cp, ctypes.POINTER(vp)],
                 "pg_kernel_launch": [vp, u32, u32, u32, u64, pu64, i32],
+                "pg_kernel_launch_ex": [vp, u32, u32, u32, u64, pu64, i32, u32],
                 "pg_kernel_max_clusters": [vp, u32, u32, u32, ctypes.POINTER(i32)],
                 "pg_kernel_time": [vp, u32, u32, u32, u64, pu64, i32, i32, i32,
                                    ctypes.POINTER(ctypes.c_float)],
@@ -154,6 +155,12 @@ class Module:
         self.cluster = int(launch.get("cluster", "1"))
         dyn = self.notes.get("dynamic_smem")
         self.dynamic_smem = int(dyn[0]) if dyn else 0
+        # output buffer -> (entry, grid, block) of a kernel in the module that zeroes it, to run
+        # in place of a memset right before the main entry (``// @ptxgen zero``)
+        self.zeroers = {}
+        for z in self.notes.get("zero", []):
+            kv = _kv(z)
+            self.zeroers[kv["buffer"]] = (kv["entry"], int(kv["grid"]), int(kv["block"]))
 
     def kernel(self, entry: str) -> Kernel:
         handle = ctypes.c_void_p()
@@ -208,7 +215,10 @@ class Kernel:
     entry: str
 
     def launch(self, grid: int, block: int, smem: int, pointers: list[int],
-               stream: int = 0) -> None:
+               stream: int = 0, early: bool = False) -> None:
+        """Launch the module's main entry. ``early``: programmatic stream serialization
+        (``PG_LAUNCH_EARLY``), for a kernel that waits (``griddepcontrol.wait``) before it
+        touches what the kernel ahead of it writes."""
         m = self.module
         if m.persistent:
             if block != m.block:
@@ -221,7 +231,15 @@ class Kernel:
                               f"size {m.cluster}")
         smem = max(smem, m.dynamic_smem)
         ptrs = (ctypes.c_uint64 * len(pointers))(*pointers)
-        _check(library().pg_kernel_launch(self.handle, grid, block, smem, stream, ptrs,
+        _check(library().pg_kernel_launch_ex(self.handle, grid, block, smem, stream, ptrs,
+                                             len(pointers), 1 if early else 0),
+               f"pg_kernel_launch({self.entry})")
+
+    def launch_plain(self, grid: int, block: int, pointers: list[int], stream: int = 0) -> None:
+        """Launch this entry as it is, with no dynamic shared memory and none of the main
+        entry's launch notes (a helper kernel of the module, such as its zero kernel)."""
+        ptrs = (ctypes.c_uint64 * len(pointers))(*pointers)
+        _check(library().pg_kernel_launch(self.handle, grid, block, 0, stream, ptrs,
                                           len(pointers)), f"pg_kernel_launch({self.entry})")
 
     def time(self, grid: int, block: int, smem: int, pointers: list[int], warmup: int = 3,
@@ -281,6 +299,7 @@ class Problem:
     _kernel: Kernel | None = None
     _launch: dict[str, Any] | None = None
     _max_clusters: int | None = None
+    _helpers: dict[str, Kernel] = field(default_factory=dict)  # other entries of the module
 
     @classmethod
     def from_dir(cls, path: str | Path, **flags: bool) -> Problem:
@@ -330,6 +349,12 @@ class Problem:
         assert self._module is not None
         return self._module
 
+    def _helper(self, entry: str) -> Kernel:
+        """Another entry of this problem's module (looked up once)."""
+        if entry not in self._helpers:
+            self._helpers[entry] = self.module.kernel(entry)
+        return self._helpers[entry]
+
     def grid(self) -> int:
         """meta.json's grid, or for a persistent kernel one CTA per SM (at most one per tile),
         in whole clusters that can all be resident at once."""
@@ -368,15 +393,24 @@ class Problem:
             stream = torch.cuda.current_stream(self._dev()).cuda_stream
         ptrs = {name: t.data_ptr() for name, t in tensors.items()}
         self.module.fill_tensormaps(ptrs)
+        early = False
         if zero:
             shapes = {a["name"]: a["shape"] for a in launch["args"]}
             for name in launch.get("zero_outputs", []):
                 t = tensors[name]
+                zeroer = self.module.zeroers.get(name)
+                if zeroer is not None:
+                    # the module's own kernel clears the buffer and lets the main kernel start
+                    # at once; the main kernel waits for it before it adds into the buffer
+                    entry, grid, block = zeroer
+                    self._helper(entry).launch_plain(grid, block, [t.data_ptr()], stream)
+                    early = True
+                    continue
                 n = int(np.prod(shapes[name])) if shapes[name] else 1
                 _check(library().pg_memset_async(t.data_ptr(), n * t.element_size(), stream),
                        "pg_memset_async")
         kernel.launch(self.grid(), launch["block"][0], int(launch.get("smem_bytes", 0)),
-                      [ptrs[n] for n in launch["arg_order"]], stream)
+                      [ptrs[n] for n in launch["arg_order"]], stream, early=early)
         if check_status:
             torch.cuda.synchronize(self._dev())
             status = self.module.status()

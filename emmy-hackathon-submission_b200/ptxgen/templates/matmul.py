@@ -79,6 +79,7 @@ MIXED_GAIN = 0.05  # ... used only when the cost model finishes that much sooner
 # B200 with one tile per pair (K = 8192): the loads of A and B and the pipeline around the MMAs,
 # not the MMAs, set the pace of a narrow tile, so a narrower tile is barely faster
 K_BLOCK_TIME = {256: 1.0, 192: 0.98, 128: 0.95, 64: 0.90}
+ZERO_GRID, ZERO_BLOCK = SM_COUNT, 256  # launch of a split-K module's kernel that zeroes C
 SMEM_LIMIT = 232448  # dynamic shared memory one CTA may opt into on sm_100 (227 KiB)
 STAGE_BLOCK = 32  # rows and columns of the f32 block an epilogue warp stages per TMA op
 STAGE_BUF = STAGE_BLOCK * STAGE_BLOCK * 4  # 4 KiB: 32 rows of 128 bytes, 128-byte swizzled
@@ -889,6 +890,11 @@ def emit(p: MatmulPlan) -> str:
         x("@%plane0 cp.async.bulk.commit_group;")
 
     x(f"{epi}:")
+    if p.atomic:
+        # C is zeroed by the module's zero kernel, which may still run when this kernel was
+        # launched early (PG_LAUNCH_EARLY): nothing adds into C before that kernel has ended and
+        # its stores are visible. Without an early launch there is nothing to wait for.
+        x("griddepcontrol.wait;")
     x(f"sub.u32 {r('quad')}, %warp, {EPILOGUE_WARPS[0]};")
     x(f"shl.b32 {r('lanebase')}, %quad, 21;")  # TMEM lane (quad*32) in bits 16..31
     if p.staged:
@@ -1014,6 +1020,8 @@ def emit(p: MatmulPlan) -> str:
         f"dims={p.n},{p.k} strides={p.n * esz} box=64,{BK} swizzle=128",
         *([f"// @ptxgen tensormap symbol={e}_tmap_c buffer={p.c} dtype=f32 dims={p.n},{p.m} "
            f"strides={p.n * 4} box={STAGE_BLOCK},{STAGE_BLOCK} swizzle=128"] if p.staged else []),
+        *([f"// @ptxgen zero entry={e}_zero buffer={p.c} grid={ZERO_GRID} block={ZERO_BLOCK}"]
+          if p.atomic else []),
         f"// @ptxgen matmul m={p.m} n={p.n} k={p.k} bn={p.bn} splits={p.splits} "
         f"stages={stages} tiles={p.tiles} segments={entries} cta_group={g}"
         + (" widths=mixed" if mixed else ""),
@@ -1031,4 +1039,37 @@ def emit(p: MatmulPlan) -> str:
         + (".reqnctapercluster 2, 1, 1\n" if pair else "") + "{",
         decls,
     ]
-    return "\n".join(head + x.finish() + ["}", ""])
+    tail = [zero_kernel_ptx(f"{e}_zero", p.m * p.n * 4)] if p.atomic else []
+    return "\n".join(head + x.finish() + ["}", ""] + tail)
+
+
+def zero_kernel_ptx(entry: str, nbytes: int) -> str:
+    """The entry that zeroes a split-K GEMM's C (``nbytes``, a multiple of 16) ahead of it:
+    ``ZERO_GRID`` x ``ZERO_BLOCK`` threads store 16 zero bytes at a time in a grid-stride
+    loop. Its first instruction lets the launch that follows it on the stream start at once
+    (``griddepcontrol.launch_dependents``), so that launch's set-up and MMAs overlap this one;
+    the GEMM's epilogue waits for this kernel (``griddepcontrol.wait``) before adding into C."""
+    chunks = nbytes // 16
+    threads = ZERO_GRID * ZERO_BLOCK
+    return "\n".join([
+        f".visible .entry {entry}(\n\t.param .u64 {entry}_param_c\n)\n"
+        f".maxntid {ZERO_BLOCK}, 1, 1\n{{",
+        "\t.reg .pred %z_p;", "\t.reg .b32 %z_i, %z_t;", "\t.reg .b64 %z_c, %z_a;",
+        "\tgriddepcontrol.launch_dependents;",
+        f"\tld.param.u64 %z_c, [{entry}_param_c];",
+        "\tcvta.to.global.u64 %z_c, %z_c;",
+        "\tmov.u32 %z_i, %ctaid.x;",
+        "\tmov.u32 %z_t, %tid.x;",
+        f"\tmad.lo.u32 %z_i, %z_i, {ZERO_BLOCK}, %z_t;",
+        f"\tsetp.ge.u32 %z_p, %z_i, {chunks};",
+        "\t@%z_p bra $Z_done;",
+        "$Z_loop:",
+        "\tmul.wide.u32 %z_a, %z_i, 16;",
+        "\tadd.s64 %z_a, %z_c, %z_a;",
+        "\tst.global.v4.b32 [%z_a], {0, 0, 0, 0};",
+        f"\tadd.u32 %z_i, %z_i, {threads};",
+        f"\tsetp.lt.u32 %z_p, %z_i, {chunks};",
+        "\t@%z_p bra $Z_loop;",
+        "$Z_done:",
+        "\tret;",
+        "}", ""])

@@ -87,6 +87,20 @@ int pg_kernel_get(pg_module *module, const char *entry, pg_kernel **out);
 int pg_kernel_launch(pg_kernel *kernel, uint32_t grid, uint32_t block, uint32_t smem_bytes,
                      uint64_t stream, const uint64_t *ptrs, int nptrs);
 
+/* pg_kernel_launch_ex flag: launch with programmatic stream serialization
+ * (CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION). The kernel may then start while the
+ * kernel before it on the stream still runs, once that kernel has executed
+ * griddepcontrol.launch_dependents (or ended); it must execute griddepcontrol.wait before it
+ * touches anything that kernel writes. ptxgen uses it for the split-K GEMM after the module's
+ * own kernel that zeroes C (which the launcher launches plainly, so it follows all earlier
+ * work): the GEMM's set-up and MMAs overlap the zeroing, and its epilogue waits before adding
+ * into C. No counterpart in the reference, whose evaluator zeroes with a memset. */
+#define PG_LAUNCH_EARLY 1u
+
+/* pg_kernel_launch with `flags` (0 or PG_LAUNCH_EARLY; anything else is PG_ERR_ARGUMENT). */
+int pg_kernel_launch_ex(pg_kernel *kernel, uint32_t grid, uint32_t block, uint32_t smem_bytes,
+                        uint64_t stream, const uint64_t *ptrs, int nptrs, uint32_t flags);
+
 /* Launch like pg_kernel_launch `warmup` times untimed, then `reps` times, each bracketed by
  * CUDA events on `stream`; waits for the last and writes launch i's device time in
  * milliseconds to ms_out[i]. Launches run back to back (no cache flush between them). */

@@ -220,6 +220,36 @@ def test_gemm_uses_the_tcgen05_template() -> None:
     assert "tcgen05" not in generic and "cp.async.cg.shared.global" in generic
 
 
+def test_splitk_module_zeroes_c_itself(tmp_path) -> None:
+    """A split-K GEMM's module carries the kernel that zeroes C (named in a ``zero`` note the
+    launcher reads), whose first instruction lets the next launch start, and whose stores
+    cover exactly C's bytes; the GEMM waits (``griddepcontrol.wait``) at the top of its
+    epilogue, before any reduce-add into C. A plain GEMM has neither. Both assemble."""
+    import re
+
+    from ptxgen.runtime import header_notes
+    from ptxgen.templates.matmul import ZERO_BLOCK, ZERO_GRID
+
+    spec = problems.CONFIGS["c5b_matmul_splitk"]()
+    ptx = compile_spec(spec)
+    note = header_notes(ptx)["zero"]
+    entry = f"{spec.kernel['entry']}_zero"
+    assert note == [f"entry={entry} buffer=matmul grid={ZERO_GRID} block={ZERO_BLOCK}"]
+    zero = ptx[ptx.index(f".visible .entry {entry}("):]
+    body = [ln.strip() for ln in zero.splitlines() if ln.startswith("\t")]
+    first = next(ln for ln in body if not ln.startswith((".reg", ".param")))
+    assert first == "griddepcontrol.launch_dependents;"
+    assert re.search(rf"setp\.lt\.u32 %z_p, %z_i, {1024 * 1024 * 4 // 16};", zero)
+    assert "st.global.v4.b32 [%z_a], {0, 0, 0, 0};" in zero
+    main = ptx[:ptx.index(f".visible .entry {entry}(")]
+    epi = main[main.index("$M_epilogue:"):]
+    assert epi.index("griddepcontrol.wait;") < epi.index("cp.reduce.async.bulk.tensor")
+    assert main.count("griddepcontrol") == 1
+    plain = compile_spec(problems.CONFIGS["c5_matmul"]())
+    assert "griddepcontrol" not in plain and "zero" not in header_notes(plain)
+    ptxas(ptx, tmp_path)
+
+
 def test_gemm_epilogue_wait_is_warp_uniform(tmp_path) -> None:
     """The epilogue's warps go from their accumulator wait to warp-collective ``tcgen05.ld``:
     that wait leaves only through warp votes (all lanes saw the phase, or no lane has time

@@ -245,6 +245,38 @@ def test_launcher_times_launches(cuda) -> None:
     assert theirs / 1.5 < ours < theirs * 1.5, (ours, theirs)
 
 
+def test_splitk_zero_kernel_and_early_launch(cuda) -> None:
+    """A split-K GEMM runs as its module's zero kernel followed by the GEMM launched early
+    (programmatic stream serialization), eagerly and captured in a CUDA graph. C is filled with
+    NaN before each run, so a GEMM that added into it before the zero kernel's stores landed, or
+    a graph without the zeroing, leaves NaN behind; both runs must meet the GEMM bar against
+    the f64 product (the reduce-add order may differ between runs, so not bit for bit)."""
+    import numpy as np
+    import torch
+
+    from ptxgen.runtime import Problem
+
+    spec = problems.matmul(512, 512, 16384, split_k=8, raster_group=None)
+    ins = reference_inputs(spec.meta)
+    prob = Problem(spec.graph, spec.meta)
+    assert "matmul" in prob.module.zeroers
+    tensors = prob.allocate()
+    for name, arr in ins.items():
+        tensors[name].copy_(torch.from_numpy(arr.reshape(-1).view(np.int16)).view(torch.bfloat16))
+    a, b = operands(spec, ins)
+    want = a @ b
+    tensors["matmul"].fill_(float("nan"))
+    prob.launch(tensors, check_status=True)
+    torch.cuda.synchronize()
+    assert_gemm_close(tensors["matmul"].cpu().numpy().reshape(512, 512), want)
+    graph = prob.capture(tensors)
+    tensors["matmul"].fill_(float("nan"))
+    graph.replay()
+    torch.cuda.synchronize()
+    assert_gemm_close(tensors["matmul"].cpu().numpy().reshape(512, 512), want)
+    assert prob.module.status() == 0
+
+
 def test_gemm_graph_replay(cuda) -> None:
     """The tcgen05 template (tensor maps in module globals, a paired persistent grid) captured
     as a CUDA graph replays to the eager launch's result bit for bit."""
