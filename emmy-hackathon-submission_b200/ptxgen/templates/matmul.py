@@ -42,7 +42,13 @@ split plus ``SEGMENT_COST`` per segment for its epilogue (for 32 tiles of 1024 K
 uneven splits, 288 segments in two full waves, where the IR's 4 splits fill 128 of 148 SMs
 once). Segments go split-major, so the CTAs running at one time read the same few K windows of A
 and B and share them in L2. The sum is the IR's (every K block of every tile is added once into
-zeroed C); only the f32 association differs, as it does between atomic orders. Tensor maps live in module ``.global`` symbols that the launcher fills
+zeroed C); only the f32 association differs, as it does between atomic orders. The split-K
+module carries its own kernel that zeroes C (``zero_kernel_ptx``, named in a ``// @ptxgen
+zero`` line): the launcher runs it in place of a memset and starts the GEMM right after it with
+programmatic stream serialization, and the GEMM's epilogue waits for it
+(``griddepcontrol.wait``) before its first reduce-add. A plain GEMM with fewer tiles than SM
+pairs may cut its tiles narrower (``MatmulPlan.columns``). Tensor maps live in module
+``.global`` symbols that the launcher fills
 (``pg_tensormap_fill``), named in ``// @ptxgen tensormap`` header lines, so the kernel's
 parameters stay the plain device pointers of meta.json's arg_order. Every mbarrier wait is
 bounded by ``%globaltimer``; a wait that runs out sets a bit of the module's ``ptxgen_status``
