@@ -97,6 +97,21 @@ def test_full_size_configs_assemble(tmp_path) -> None:
         ptxas(compile_spec(problems.CONFIGS[key]()), tmp_path)
 
 
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_gemm_rank_shares_assemble(world: int, tmp_path) -> None:
+    """The GEMM kernel one rank of ``world`` compiles for configs 5 and 5b (rows of A and C on
+    SM pairs down to the 1/8 share's 128 rows on single SMs; 5b also along K), through the
+    template, with plain TMA only; each module assembles."""
+    from ptxgen import shard
+
+    for name, ksplit in (("c5_matmul", False), ("c5b_matmul_splitk", False),
+                         ("c5b_matmul_splitk", True)):
+        ptx = compile_spec(shard.local_problem(name, world, ksplit=ksplit).spec)
+        assert "tcgen05.mma" in ptx, (name, world)
+        assert_plain_tma(ptx)
+        ptxas(ptx, tmp_path)
+
+
 def test_pointwise_is_vectorised() -> None:
     ptx = compile_spec(problems.pointwise_add(1 << 20))
     assert ptx.count("ld.global.nc.v4.f32") == 2
