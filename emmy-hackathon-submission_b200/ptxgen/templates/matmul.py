@@ -85,6 +85,12 @@ MIXED_GAIN = 0.05  # ... used only when the cost model finishes that much sooner
 # B200 with one tile per pair (K = 8192): the loads of A and B and the pipeline around the MMAs,
 # not the MMAs, set the pace of a narrow tile, so a narrower tile is barely faster
 K_BLOCK_TIME = {256: 1.0, 192: 0.98, 128: 0.95, 64: 0.90}
+# what cutting a tail tile costs per piece beyond the first, in K blocks of MMA time: the
+# partials written and summed. Set from config 5's shares on a B200: the 1/4 share's tail in two
+# pieces took 174.3 us against 184.0 for whole tiles; the 1/8 share's in four took 104.7 against
+# 96.0, so four pieces must not pay
+TAIL_FIXUP = 16
+ROLE_WHOLE, ROLE_PIECE = 0, 1  # a work-table entry: a whole tile, or a piece of a tail tile
 ZERO_GRID, ZERO_BLOCK = SM_COUNT, 256  # launch of a split-K module's kernel that zeroes C
 SMEM_LIMIT = 232448  # dynamic shared memory one CTA may opt into on sm_100 (227 KiB)
 STAGE_BLOCK = 32  # rows and columns of the f32 block an epilogue warp stages per TMA op
@@ -115,6 +121,9 @@ class MatmulPlan:
     # a plain pair GEMM may cut some tiles narrower to even out the pairs' work (``columns``);
     # False keeps whole tiles
     mixed: bool = True
+    # a plain GEMM whose last wave of tiles is part full may cut those tiles along K (``tail``);
+    # False keeps whole tiles
+    stream_k: bool = True
 
     @property
     def kc(self) -> int:
@@ -134,6 +143,9 @@ class MatmulPlan:
         kbs = self.k // BK
         rows = 2 if self.pair else 1  # IR tiles (128 rows) per table tile
         if not self.atomic:  # one whole-K segment per tile (a plain GEMM has no split)
+            if self.tail() is not None:
+                table = tuple(e[:4] for e in self.tail_table())
+                return table, min(SM_COUNT // rows, len(table)) * rows
             table = tuple((mt, nt, 0, kbs) for mt, nt in self.order())
             return table, len(table) * rows
         tiles = list(dict.fromkeys((mt // rows, nt) for mt, nt, _ in self.schedule))
@@ -147,6 +159,45 @@ class MatmulPlan:
         table = tuple((mt, nt, cut[j], cut[j + 1] - cut[j])
                       for j in range(splits) for mt, nt in tiles)
         return table, min(slots, len(table)) * rows
+
+    def tail(self) -> tuple[int, int] | None:
+        """(whole-tile entries, pieces per tail tile) for a plain GEMM whose tiles leave the last
+        wave of CTAs (pairs) part full, or None. The whole waves keep whole tiles; each of the
+        ``rest`` tiles after them is cut along K into ``q`` pieces, so that the pieces spread
+        over every CTA. A piece costs its K blocks plus ``SEGMENT_COST``, and the last piece of a
+        tail tile adds the others' partials, ``TAIL_FIXUP`` a partial; the cut is taken when it
+        finishes ``MIXED_GAIN`` sooner than a last wave of whole tiles (config 5's 1/4 share:
+        three waves and 34 tiles in two pieces; its 1/8 share keeps whole tiles)."""
+        if not self.stream_k or self.atomic or self.columns() is not None:
+            return None
+        kbs = self.k // BK
+        slots = SM_COUNT // (2 if self.pair else 1)
+        waves, rest = divmod(len(self.order()), slots)
+        if not waves or not rest:
+            return None
+        best: tuple[float, int | None] = (
+            (1 - MIXED_GAIN) * (waves + 1) * (kbs + SEGMENT_COST), None)
+        for q in range(2, kbs // MIN_SEGMENT + 1):
+            rounds = -(-rest * q // slots)
+            cost = (waves * (kbs + SEGMENT_COST) + rounds * (-(-kbs // q) + SEGMENT_COST)
+                    + TAIL_FIXUP * (q - 1))
+            if cost < best[0]:
+                best = (cost, q)
+        return None if best[1] is None else (waves * slots, best[1])
+
+    def tail_table(self) -> tuple[tuple[int, ...], ...]:
+        """The work table of a plan with a ``tail``: (m tile, n tile, first K block, K blocks,
+        role, piece, pieces, tail tile) per entry. The whole tiles come first, in raster order;
+        then the pieces, split-major (piece j of every tail tile, then piece j + 1), so the
+        pieces running at once read the same K window of A and B."""
+        whole, q = self.tail()
+        kbs = self.k // BK
+        order = self.order()
+        table = [(mt, nt, 0, kbs, ROLE_WHOLE, 0, 0, 0) for mt, nt in order[:whole]]
+        cut = [j * kbs // q for j in range(q + 1)]
+        table += [(mt, nt, cut[j], cut[j + 1] - cut[j], ROLE_PIECE, j, q, u)
+                  for j in range(q) for u, (mt, nt) in enumerate(order[whole:])]
+        return tuple(table)
 
     def order(self) -> list[tuple[int, int]]:
         """A plain GEMM's table tiles (m tile, n tile) in the order the CTAs take them."""
@@ -545,7 +596,13 @@ def emit(p: MatmulPlan) -> str:
     x = _Text()
     cols = p.columns()
     mixed = cols is not None  # per-entry width and first column (pair GEMMs only)
-    table, ctas = cols if mixed else p.segments()
+    tail = None if mixed else p.tail()  # whole-tile entries and pieces per tail tile
+    if mixed:
+        table, ctas = cols
+    elif tail:
+        table, ctas = p.tail_table(), p.segments()[1]
+    else:
+        table, ctas = p.segments()
     entries = len(table)
     pair = p.pair
     g = 2 if pair else 1  # the tcgen05 cta_group
@@ -589,9 +646,15 @@ def emit(p: MatmulPlan) -> str:
     def sched_lookup(skip: str) -> None:
         """Entry %t of the table into %mt, %nt, %kb0, %cnt (mixed widths: %mt, %col, %wid,
         %cnt, with %kb0 0); an empty entry branches to skip."""
-        x(f"mul.wide.u32 {r('s_off', u64)}, %t, 8;")
+        x(f"mul.wide.u32 {r('s_off', u64)}, %t, {16 if tail else 8};")
         x(f"add.s64 %s_off, {r('sched', u64)}, %s_off;")
-        x(f"ld.global.nc.v2.u32 {{{r('code')}, {r('code2')}}}, [%s_off];")
+        if tail:  # (..., role | piece << 8 | pieces << 16, tail tile)
+            x(f"ld.global.nc.v4.u32 {{{r('code')}, {r('code2')}, {r('code3')}, {r('tu')}}}, "
+              "[%s_off];")
+            x(f"and.b32 {r('role')}, %code3, 255;")
+            x(f"bfe.u32 {r('pj')}, %code3, 8, 8;")
+        else:
+            x(f"ld.global.nc.v2.u32 {{{r('code')}, {r('code2')}}}, [%s_off];")
         x(f"and.b32 {r('mt')}, %code, 65535;")
         if mixed:
             x(f"shr.u32 {r('col')}, %code, 16;")
@@ -895,6 +958,76 @@ def emit(p: MatmulPlan) -> str:
         x(f"@%plane0 {tma_out} [%tmap_c, {{%sx, %srow}}], [{buf}];")
         x("@%plane0 cp.async.bulk.commit_group;")
 
+    wpt = len(EPILOGUE_WARPS) * g  # epilogue warps a table tile's rows are spread over
+    warp_bytes = 32 * p.bn * 4  # one warp's 32 rows of a tile, f32
+
+    def tail_piece(q: int) -> None:
+        """A piece of a tail tile. Every piece's warp stores its 32 rows of the partial sum into
+        its own slot of the module's workspace (``_ws``: [tail tile][piece][warp][chunk][16-byte
+        word][lane], so each store instruction covers 512 contiguous bytes), then lane 0 adds
+        one to the tile's counter for this warp (``_cnt``, release and acquire at GPU scope,
+        after a fence in every lane). The warp whose add completes the count -- the last of
+        the tile's ``q`` pieces to get there -- sums the ``q`` partials in piece order (its own
+        read again from TMEM, the others from the workspace through L2), stores the sum into C
+        as a whole tile's epilogue does, and clears the counter for the next launch. Nothing
+        waits on another CTA, and the sum's order does not depend on which piece ends last."""
+        x(f"mov.u64 {r('wsb', u64)}, {e}_ws;")
+        x(f"mov.u64 {r('cnb', u64)}, {e}_cnt;")
+        if pair:
+            x(f"mad.lo.u32 {r('wslot')}, %rank, {len(EPILOGUE_WARPS)}, %quad;")
+        else:
+            x(f"mov.u32 {r('wslot')}, %quad;")
+        # this lane's word in piece 0's slot of its warp, and in its own piece's slot
+        x(f"mul.lo.u32 {r('wsi')}, %tu, {q * wpt};")
+        x("add.u32 %wsi, %wsi, %wslot;")
+        x(f"mul.wide.u32 {r('wsu', u64)}, %wsi, {warp_bytes};")
+        x(f"mul.wide.u32 {r('wln', u64)}, %lane, 16;")
+        x("add.s64 %wsu, %wsu, %wln;")
+        x("add.s64 %wsu, %wsu, %wsb;")
+        x(f"mul.wide.u32 {r('wso', u64)}, %pj, {wpt * warp_bytes};")
+        x(f"add.s64 {r('wsl', u64)}, %wsu, %wso;")
+        for chunk in range(p.bn // 32):
+            x(f"add.u32 {r('tcol')}, %taddr, {chunk * 32};")
+            x(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(vals)}}}, [%tcol];")
+            x("tcgen05.wait::ld.sync.aligned;")
+            for j in range(8):
+                x(f"st.global.v4.b32 [%wsl+{(chunk * 8 + j) * 512}], "
+                  f"{{{', '.join(vals[4 * j:4 * j + 4])}}};")
+        done = x.label("piece_done")
+        x("fence.acq_rel.gpu;")
+        x("bar.warp.sync -1;")
+        x(f"mad.lo.u32 {r('cni')}, %tu, {wpt}, %wslot;")
+        x(f"mul.wide.u32 {r('cno', u64)}, %cni, 4;")
+        x("add.s64 %cnb, %cnb, %cno;")
+        x(f"setp.eq.u32 {r('pl0', pred)}, %lane, 0;")
+        x(f"@%pl0 atom.acq_rel.gpu.global.add.u32 {r('old')}, [%cnb], 1;")
+        x("shfl.sync.idx.b32 %old, %old, 0, 31, -1;")
+        x(f"setp.ne.u32 %p, %old, {q - 1};")
+        x(f"@%p bra.uni {done};")  # not the last piece: its partial is in the workspace
+        x("fence.acq_rel.gpu;")
+        ws = [r(f"w{i}", "b32") for i in range(32)]
+        for chunk in range(p.bn // 32):
+            for v in vals:
+                x(f"mov.b32 {v}, 0x80000000;")  # -0.0: adding it changes no value
+            for jj in range(q):
+                own, add = x.label("own"), x.label("add")
+                x(f"setp.eq.u32 %p, %pj, {jj};")
+                x(f"@%p bra.uni {own};")
+                for j in range(8):
+                    x(f"ld.global.cg.v4.f32 {{{', '.join(ws[4 * j:4 * j + 4])}}}, "
+                      f"[%wsu+{jj * wpt * warp_bytes + (chunk * 8 + j) * 512}];")
+                x(f"bra.uni {add};")
+                x(f"{own}:")
+                x(f"add.u32 {r('tcol')}, %taddr, {chunk * 32};")
+                x(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ws)}}}, [%tcol];")
+                x("tcgen05.wait::ld.sync.aligned;")
+                x(f"{add}:")
+                for v, w in zip(vals, ws):
+                    x(f"add.rn.f32 {v}, {v}, {w};")
+            store_chunk(chunk)
+        x("@%pl0 st.relaxed.gpu.global.u32 [%cnb], 0;")
+        x(f"{done}:")
+
     x(f"{epi}:")
     if p.atomic:
         # C is zeroed by the module's zero kernel, which may still run when this kernel was
@@ -953,6 +1086,23 @@ def emit(p: MatmulPlan) -> str:
         x(f"cvt.u64.u32 {r('ncol64', u64)}, %n0;")
         x("add.s64 %crow, %crow, %ncol64;")
         x("add.s64 %crow, %crow, %c_ptr;")
+    def store_chunk(chunk: int) -> None:
+        """%v0..%v31 (this lane's row, columns 32*chunk..) into C."""
+        if p.staged:
+            stage_block(chunk)
+            return
+        for j in range(8):
+            quad = ", ".join(vals[4 * j:4 * j + 4])
+            off = chunk * 128 + j * 16
+            if p.atomic:
+                x(f"red.global.add.v4.f32 [%crow+{off}], {{{quad}}};")
+            else:
+                x(f"st.global.v4.b32 [%crow+{off}], {{{quad}}};")
+
+    if tail:
+        piece, released = x.label("piece"), x.label("released")
+        x("setp.ne.u32 %p, %role, 0;")
+        x(f"@%p bra.uni {piece};")  # the role is the same in every lane
     chunks_done = x.label("chunks_done")
     for chunk in range(p.bn // 32):
         if mixed and chunk >= 2:  # a tile of width wid has wid/32 blocks (64 at the least)
@@ -961,18 +1111,14 @@ def emit(p: MatmulPlan) -> str:
         x(f"add.u32 {r('tcol')}, %taddr, {chunk * 32};")
         x(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(vals)}}}, [%tcol];")
         x("tcgen05.wait::ld.sync.aligned;")
-        if p.staged:
-            stage_block(chunk)
-            continue
-        for j in range(8):
-            quad = ", ".join(vals[4 * j:4 * j + 4])
-            off = chunk * 128 + j * 16
-            if p.atomic:
-                x(f"red.global.add.v4.f32 [%crow+{off}], {{{quad}}};")
-            else:
-                x(f"st.global.v4.b32 [%crow+{off}], {{{quad}}};")
+        store_chunk(chunk)
     if mixed:
         x(f"{chunks_done}:")
+    if tail:
+        x(f"bra.uni {released};")
+        x(f"{piece}:")
+        tail_piece(tail[1])
+        x(f"{released}:")
     x("tcgen05.fence::before_thread_sync;")
     x("mad.lo.u32 %tebar, %ab, 8, %bars;")
     x(f"add.u32 %tebar, %tebar, {tempty};")
@@ -1006,11 +1152,15 @@ def emit(p: MatmulPlan) -> str:
     # mixed widths: (band | first column / 32 << 16, width | K blocks << 16); else
     # (m tile | n tile << 16, first K block | K blocks << 16)
     words = ([(mt, col // 32, w, kbs if w else 0) for mt, col, w in table] if mixed
-             else table)
-    for w0, w1, w2, w3 in words:
+             else [e[:4] for e in table])
+    for i, (w0, w1, w2, w3) in enumerate(words):
         if max(w0, w1, w2, w3) >= 1 << 16:
             raise NotImplementedError("matmul template: more tiles than the schedule encodes")
         sched_words += [str(w0 | w1 << 16), str(w2 | w3 << 16)]
+        if tail:
+            _, _, _, _, role, piece_j, pieces, tu = table[i]
+            sched_words += [str(role | piece_j << 8 | pieces << 16), str(tu)]
+    n_tail = len(p.order()) - tail[0] if tail else 0
     rows = [", ".join(sched_words[i:i + 16]) for i in range(0, len(sched_words), 16)]
     params = ",\n".join(f"\t.param .u64 {e}_param_{q}" for q in p.params)
     decls = "\n".join(f"\t.reg .{t} %m_{n};" for n, t in x.regs.items())
@@ -1030,7 +1180,8 @@ def emit(p: MatmulPlan) -> str:
           if p.atomic else []),
         f"// @ptxgen matmul m={p.m} n={p.n} k={p.k} bn={p.bn} splits={p.splits} "
         f"stages={stages} tiles={p.tiles} segments={entries} cta_group={g}"
-        + (" widths=mixed" if mixed else ""),
+        + (" widths=mixed" if mixed else "")
+        + (f" tail={tail[0]},{tail[1]}" if tail else ""),
         "",
         f".version {PTX_VERSION}\n.target {TARGET}\n.address_size 64\n",
         ".extern .shared .align 1024 .b8 smem_pool[];",
@@ -1038,7 +1189,9 @@ def emit(p: MatmulPlan) -> str:
         f".global .align 64 .b8 {e}_tmap_b[128];",
         *([f".global .align 64 .b8 {e}_tmap_c[128];"] if p.staged else []),
         ".global .align 4 .u32 ptxgen_status;",
-        f".global .align 8 .u32 {e}_sched[{len(sched_words)}] = {{\n\t"
+        *([f".global .align 16 .b8 {e}_ws[{n_tail * tail[1] * wpt * warp_bytes}];",
+           f".global .align 4 .u32 {e}_cnt[{n_tail * wpt}];"] if tail else []),
+        f".global .align {16 if tail else 8} .u32 {e}_sched[{len(sched_words)}] = {{\n\t"
         + ",\n\t".join(rows) + "\n};",
         "",
         f".visible .entry {e}(\n{params}\n)\n.maxntid {p.block}, 1, 1\n.minnctapersm 1\n"

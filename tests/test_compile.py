@@ -235,6 +235,49 @@ def test_gemm_uses_the_tcgen05_template() -> None:
     assert "tcgen05" not in generic and "cp.async.cg.shared.global" in generic
 
 
+def test_stream_k_tail_plan_and_table(tmp_path) -> None:
+    """Config 5's 1/4 share (256 pair tiles: three waves of 74 and 34 more) cuts its 34 tail
+    tiles along K into two pieces each; the full kernel, the 1/2 share and the 1/8 share keep
+    whole tiles. The table covers every K block of every tile once: the whole tiles first in
+    raster order, then the pieces split-major. The module carries the partials' workspace and
+    one counter per tail tile and epilogue warp, adds to a counter with acquire-release order,
+    reads partials through L2, and clears the counter; nothing in it waits on another CTA."""
+    from collections import Counter
+
+    from ptxgen import shard
+    from ptxgen.templates import matmul
+    from ptxgen.templates.matmul import BK, ROLE_PIECE, ROLE_WHOLE
+
+    plans = {n: gemm_plan(shard.local_problem("c5_matmul", n).spec) for n in (1, 2, 4, 8)}
+    assert [plans[n].tail() for n in (1, 2, 4, 8)] == [None, None, (222, 2), None]
+    p = plans[4]
+    table = p.tail_table()
+    kbs = p.k // BK
+    cover = Counter()
+    for mt, nt, kb0, cnt, *_ in table:
+        cover.update((mt, nt, kb) for kb in range(kb0, kb0 + cnt))
+    assert set(cover.values()) == {1} and len(cover) == len(p.order()) * kbs
+    whole = [e for e in table if e[4] == ROLE_WHOLE]
+    pieces = [e for e in table if e[4] == ROLE_PIECE]
+    assert [e[:4] for e in whole] == [(mt, nt, 0, kbs) for mt, nt in p.order()[:222]]
+    tails = p.order()[222:]
+    assert [(e[0], e[1], e[5], e[6], e[7]) for e in pieces] == \
+        [(mt, nt, j, 2, u) for j in range(2) for u, (mt, nt) in enumerate(tails)]
+    ptx = matmul.emit(p)
+    name = p.entry
+    assert "tail=222,2" in ptx
+    assert f".global .align 16 .b8 {name}_ws[{34 * 2 * 8 * 32 * 256 * 4}];" in ptx
+    assert f".global .align 4 .u32 {name}_cnt[{34 * 8}];" in ptx
+    assert ptx.count("atom.acq_rel.gpu.global.add.u32") == 1
+    assert "ld.global.cg.v4.f32" in ptx and "st.relaxed.gpu.global.u32" in ptx
+    assert "ld.acquire" not in ptx and "griddepcontrol" not in ptx
+    assert_plain_tma(ptx)
+    ptxas(ptx, tmp_path)
+    import dataclasses
+
+    assert dataclasses.replace(p, stream_k=False).tail() is None
+
+
 def test_splitk_module_zeroes_c_itself(tmp_path) -> None:
     """A split-K GEMM's module carries the kernel that zeroes C (named in a ``zero`` note the
     launcher reads), whose first instruction lets the next launch start, and whose stores

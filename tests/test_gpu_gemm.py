@@ -245,6 +245,58 @@ def test_launcher_times_launches(cuda) -> None:
     assert theirs / 1.5 < ours < theirs * 1.5, (ours, theirs)
 
 
+@pytest.mark.parametrize("staged", [True, False], ids=["staged", "per_thread"])
+def test_stream_k_tail(cuda, staged: bool) -> None:
+    """A 4096^3 GEMM (256 pair tiles: three waves of 74 and 34 more) with its 34 tail tiles in
+    two K pieces each: the last piece of each tile to finish sums both partials. C is filled
+    with NaN before each of two launches of one module; they must agree bit for bit (the sum's
+    order does not depend on which piece ends last, and the counters clear themselves), meet
+    the GEMM bar against the f64 product on sampled rows, and stay within it of the whole-tile
+    build."""
+    import dataclasses
+
+    import torch
+
+    from ptxgen.compiler import kernel_for_meta
+    from ptxgen.lower import Buffer
+    from ptxgen.runtime import Problem
+    from ptxgen.templates import matmul
+
+    spec = problems.matmul(4096, 4096, 4096)
+    op, launch = kernel_for_meta(Graph.from_dict(spec.graph), spec.meta)
+    bufs = {a["name"]: Buffer(tuple(a["shape"]), a["dtype"],
+                              bool(a.get("output")) or a["name"] in op.outputs)
+            for a in launch["args"]}
+    plan = matmul.match(op, bufs, launch["arg_order"], launch["block"][0],
+                        int(launch.get("smem_bytes", 0)))
+    plan = dataclasses.replace(plan, staged=staged)
+    assert plan.tail() == (222, 2)
+    ins = reference_inputs(spec.meta)
+    outs = {}
+    for name, p in (("tail", plan), ("whole", dataclasses.replace(plan, stream_k=False))):
+        ptx = matmul.emit(p)
+        assert ("tail=" in ptx) == (name == "tail")
+        prob = Problem(spec.graph, spec.meta, ptx=ptx)
+        t = prob.allocate()
+        for k, arr in ins.items():
+            host = np.ascontiguousarray(arr).reshape(-1)
+            t[k].copy_(torch.from_numpy(host.view(np.int16)).view(t[k].dtype))
+        runs = []
+        for _ in range(2):
+            t["matmul"].fill_(float("nan"))
+            prob.launch(t, check_status=True)
+            torch.cuda.synchronize()
+            runs.append(t["matmul"].clone())
+        assert torch.equal(runs[0].view(torch.int32), runs[1].view(torch.int32)), name
+        outs[name] = runs[0].cpu().numpy().reshape(4096, 4096)
+    rows = np.array(sorted({0, 4095, *range(7, 4096, 131)}))
+    a, b = operands(spec, {"x0": ins["x0"].reshape(4096, 4096)[rows], "x1": ins["x1"]})
+    worst = assert_gemm_close(outs["tail"][rows], a @ b)
+    assert_gemm_close(outs["tail"], outs["whole"].astype(np.float64))
+    print(f"stream-K tail ({'staged' if staged else 'per thread'}): max |err| / max |C| = "
+          f"{worst:.3e}")
+
+
 def test_splitk_zero_kernel_and_early_launch(cuda) -> None:
     """A split-K GEMM runs as its module's zero kernel followed by the GEMM launched early
     (programmatic stream serialization), eagerly and captured in a CUDA graph. C is filled with
