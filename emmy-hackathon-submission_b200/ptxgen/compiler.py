@@ -32,12 +32,17 @@ def compile_module(op: KernelOp, buffers: Mapping[str, Buffer], arg_order: Seque
         if ptx is not None:
             return ptx
     # sibling loops over one axis, trip by trip (``jam``); with unrolling off the jammed loop is
-    # still a runtime loop with one body per trip
+    # still a runtime loop with one body per trip. Then accumulators that hold equal values on
+    # every trip become one (``congruence``), with common subexpression elimination.
     from dataclasses import replace
 
+    from .congruence import merge_equal
     from .jam import jam
 
-    op = replace(op, body=replace(op.body, body=jam(op.body.body)))
+    stmts = jam(op.body.body)
+    if not no_cse:
+        stmts = merge_equal(stmts)
+    op = replace(op, body=replace(op.body, body=stmts))
     k = Lowering(op, buffers, arg_order, block_threads, no_unroll=no_unroll,
                  no_fusion=no_fusion, no_cse=no_cse, exchange=exchange).run()
     return k.render()
