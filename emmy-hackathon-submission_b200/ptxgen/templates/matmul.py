@@ -297,8 +297,30 @@ def _names_in(e: object) -> set[str]:
     return out
 
 
-def match(op: KernelOp, buffers: Mapping[str, Buffer], arg_order: Sequence[str], block: int,
-          smem_bytes: int) -> MatmulPlan | None:
+@dataclass(frozen=True)
+class Nest:
+    """A block-tiled matmul nest as Emmy writes it, whatever the operands' type: C [M, N] (+)=
+    A [M, K] @ B [K, N] through two shared tiles fed by cp.async copies, one K loop with one
+    inner loop of loads, products and Accum adds into Init'ed f32 accumulators, and Writes of the
+    accumulators into C (atomic for split-K)."""
+
+    tile: Tile
+    kloop: Loop | StridedLoop
+    copies: tuple[CpAsyncCopy, ...]
+    accs: int  # accumulators per thread
+    a: str
+    b: str
+    c: str
+    m: int
+    n: int
+    k: int
+    atomic: bool
+    mi: int  # the Tile's block axis over M
+    ni: int  # the Tile's block axis over N
+
+
+def nest(op: KernelOp, buffers: Mapping[str, Buffer]) -> Nest | None:
+    """The facts of the nest ``op`` holds, or None when it is not one (see ``Nest``)."""
     t = op.body
     if not isinstance(t, Tile) or not t.is_static_grid or t.aux_threads:
         return None
@@ -357,7 +379,7 @@ def match(op: KernelOp, buffers: Mapping[str, Buffer], arg_order: Sequence[str],
     if a_name is None or b_name is None:
         return None
     abuf, bbuf = buffers[a_name], buffers[b_name]
-    if abuf.dtype != bbuf.dtype or abuf.dtype not in ("bf16", "f16"):
+    if abuf.dtype != bbuf.dtype:
         return None
     k = abuf.shape[1]
     if abuf.shape[0] != m or bbuf.shape != (k, n):
@@ -376,11 +398,23 @@ def match(op: KernelOp, buffers: Mapping[str, Buffer], arg_order: Sequence[str],
           i not in mb]
     if len(mb) != 1 or len(nb) != 1:
         return None
-    mi, ni = mb[0], nb[0]
+    return Nest(t, kloop, tuple(copies), len(accs), a_name, b_name, c, m, n, k, atomic,
+                mb[0], nb[0])
+
+
+def match(op: KernelOp, buffers: Mapping[str, Buffer], arg_order: Sequence[str], block: int,
+          smem_bytes: int) -> MatmulPlan | None:
+    g = nest(op, buffers)
+    if g is None or buffers[g.a].dtype not in ("bf16", "f16"):
+        return None
+    t, kloop, copies, atomic = g.tile, g.kloop, g.copies, g.atomic
+    a_name, b_name, c, m, n, k, mi, ni = g.a, g.b, g.c, g.m, g.n, g.k, g.mi, g.ni
+    abuf = buffers[a_name]
+    axes = list(t.axes)
     if m // axes[mi].extent.as_static() != BM:
         return None
     bn = n // axes[ni].extent.as_static()
-    if bn not in (64, 128, 256) or len(accs) * block != BM * bn:
+    if bn not in (64, 128, 256) or g.accs * block != BM * bn:
         return None
     copy_names = set().union(*(_names_in(cp.src_index) for cp in copies))
     extents = [ax.extent.as_static() for ax in axes]

@@ -627,10 +627,11 @@ def test_shared_loads_merge_unless_a_shared_store_sits_between() -> None:
 
 
 def test_simt_matmul_reads_shared_memory_in_vectors() -> None:
-    """The shipped m01 nest: A's four consecutive k of one row in one v4 load, B's two columns
-    of one thread in one v2 load; no scalar shared loads remain."""
+    """The shipped m01 nest on the generic lowering (the default build takes the register-blocked
+    template): A's four consecutive k of one row in one v4 load, B's two columns of one thread
+    in one v2 load; no scalar shared loads remain."""
     graph, meta = shipped("m01_matmul_512")
-    ptx = to_ptx(Graph.from_dict(graph), meta)
+    ptx = to_ptx(Graph.from_dict(graph), meta, templates=False)
     assert ptx.count("ld.shared.v4.f32") == 64 and ptx.count("ld.shared.v2.f32") == 128
     assert "ld.shared.f32" not in ptx
 

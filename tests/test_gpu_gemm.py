@@ -130,6 +130,42 @@ def test_mixed_widths_match_whole_tiles(cuda, key: str, monkeypatch) -> None:
     print(f"{key}: bit-equal to whole tiles; max |err| / max |C| = {worst:.3e}")
 
 
+def simt_cases() -> dict[str, tuple[dict, dict]]:
+    """(graph, meta) of each f32 nest the register-blocked template takes: the shipped m01 and
+    the generated ones of ``test_simt.CASES``."""
+    import json
+    from pathlib import Path
+
+    from test_simt import CASES, case
+
+    d = Path(__file__).parent / "golden" / "shipped" / "m01_matmul_512"
+    out = {"m01_shipped": (json.loads(next(d.glob("*.ir.json")).read_text()),
+                           json.loads((d / "meta.json").read_text()))}
+    for key in CASES:
+        spec = case(key)
+        out[key] = (spec.graph, spec.meta)
+    return out
+
+
+@pytest.mark.parametrize("key", ["m01_shipped", "one_k_step", "rect", "tile_32x32",
+                                 "tile_64x64"])
+def test_simt_gemm_bit_equal(cuda, key: str) -> None:
+    """The register-blocked f32 template against the generic lowering of the same nest and
+    against the oracle, bit for bit: every element of C is the same fma chain over k in order.
+    The canaries past C must survive."""
+    graph, meta = simt_cases()[key]
+    g = Graph.from_dict(graph)
+    ptx = to_ptx(g, meta)
+    assert "@ptxgen simt" in ptx
+    ins = reference_inputs(meta)
+    out = meta["graph_outputs"][0]
+    got = gpu_run(graph, meta, ins, guard=64, ptx=ptx)[out]
+    generic = gpu_run(graph, meta, ins, guard=64, ptx=to_ptx(g, meta, templates=False))[out]
+    want = oracle_run(graph, meta, ins)[out]
+    assert np.array_equal(got.view(np.uint32), generic.view(np.uint32))
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
 def test_tcgen05_matches_oracle_small(cuda) -> None:
     """The template against the oracle's run of the very SIMT nest it replaces."""
     spec = problems.matmul(256, 256, 128)
