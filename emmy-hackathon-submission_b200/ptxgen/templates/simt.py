@@ -16,13 +16,15 @@ and the same threads per CTA), so a launcher that runs the IR's geometry runs it
   a ring of ``STAGES`` shared-memory stages with ``cp.async.cg`` (16 bytes a copy), one commit
   group per stage;
 * the first ``BM * BN / 16`` threads (whole warps) each own a 4 x 4 block of the CTA's tile.
-  Per 4 k they read their 4 rows of A and 4 k-rows of B as 8 ``ld.shared.v4`` (8 lanes of a
-  quarter warp read the same A row, a broadcast, and 128 contiguous bytes of B) and issue 64
-  ``fma.rn.f32``; the other warps only copy and meet the barriers;
+  Per 4 k they read their 4 rows of A and 4 k-rows of B as 8 16-byte shared loads (8 lanes of a
+  quarter warp read the same A row, a broadcast, and 128 contiguous bytes of B) and issue their
+  64 FMAs as 32 ``fma.rn.f32x2``, two columns of a row each, with each A value duplicated into
+  a register pair; the other warps only copy and meet the barriers;
 * each owner stores its block with 4 ``st.global.v4``.
 
-Each element of C is still one ``fma.rn.f32`` chain over k = 0 .. K-1 in order, starting from
-+0.0, the chain the nest's Accum computes: the result is the same bit for bit as the generic
+Each element of C is still one fused multiply-add chain over k = 0 .. K-1 in order, starting
+from +0.0 (each lane of an ``fma.rn.f32x2`` is an ``fma.rn.f32``), the chain the nest's Accum
+computes: the result is the same bit for bit as the generic
 lowering's and the oracle's. The template applies only where it reduces the bytes per FMA: the
 nest must give each thread fewer than 16 accumulators.
 """
@@ -65,6 +67,10 @@ class SimtPlan:
     # owners a warp spans across a row of 4 x 4 blocks (the rest of it spans down): as many as
     # the row holds, up to 32. The shipped m01 (16 a row) took 11.7 us so and 13.3 with 8 across
     lanes_x: int
+    # accumulate in fma.rn.f32x2 (two columns of a row per instruction; each lane is the same
+    # fma.rn.f32), with each A value duplicated into a register pair. The shipped m01 took
+    # 9.7-9.9 us so and 10.7-10.9 in scalar fma.rn.f32
+    pairs: bool = True
 
     @property
     def grid(self) -> int:
@@ -203,7 +209,10 @@ def emit(p: SimtPlan) -> str:
     emit_(f"mul.lo.u32 %boff, %tx, {TILE * 4};")
     emit_(f"add.u32 %boff, %boff, {a_part};")
     for r in range(TILE * TILE):
-        emit_(f"mov.f32 %acc{r}, 0f00000000;")
+        if p.pairs and r < 8:
+            emit_(f"mov.b64 %acp{r}, 0;")
+        elif not p.pairs:
+            emit_(f"mov.f32 %acc{r}, 0f00000000;")
     emit_("mov.u32 %kt, 0;")
     emit_("mov.u32 %cur, 0;")
     emit_(f"mov.u32 %nxt, {(p.stages - 1) * p.stage_bytes};")
@@ -225,6 +234,18 @@ def emit(p: SimtPlan) -> str:
         for i in range(TILE):
             regs = ", ".join(f"%a{i * 4 + j}" for j in range(4))
             emit_(f"ld.shared.v4.f32 {{{regs}}}, [%sa+{(i * p.bk + kk) * 4}];")
+        if p.pairs:
+            for j in range(4):
+                emit_(f"ld.shared.v2.b64 {{%bq{j * 2}, %bq{j * 2 + 1}}}, "
+                      f"[%sb+{(kk + j) * p.bn * 4}];")
+            for r in range(16):
+                emit_(f"mov.b64 %ad{r}, {{%a{r}, %a{r}}};")
+            for j in range(4):
+                for i in range(TILE):
+                    for h in range(2):
+                        q = i * 2 + h
+                        emit_(f"fma.rn.f32x2 %acp{q}, %ad{i * 4 + j}, %bq{j * 2 + h}, %acp{q};")
+            continue
         for j in range(4):
             regs = ", ".join(f"%b{j * 4 + c}" for c in range(TILE))
             emit_(f"ld.shared.v4.f32 {{{regs}}}, [%sb+{(kk + j) * p.bn * 4}];")
@@ -251,6 +272,9 @@ def emit(p: SimtPlan) -> str:
     emit_("mul.wide.u32 %gt, %x, 4;")
     emit_("add.s64 %gt, %gc, %gt;")
     for i in range(TILE):
+        if p.pairs:
+            emit_(f"st.global.v2.b64 [%gt+{i * p.n * 4}], {{%acp{i * 2}, %acp{i * 2 + 1}}};")
+            continue
         regs = ", ".join(f"%acc{i * TILE + c}" for c in range(TILE))
         emit_(f"st.global.v4.f32 [%gt+{i * p.n * 4}], {{{regs}}};")
     lines.append("$L_done:")
@@ -265,6 +289,7 @@ def emit(p: SimtPlan) -> str:
         "\t.reg .b64 %gp, %ga, %gb, %gc, %gt, %ga0, %gb0" + "".join(f", %p{t}" for t in tags)
         + ";",
         "\t.reg .f32 %acc<16>, %a<16>, %b<16>;",
+        "\t.reg .b64 %acp<8>, %ad<16>, %bq<8>;",
     ]
     smem = p.stages * p.stage_bytes
     head = [

@@ -67,8 +67,9 @@ def test_shipped_m01_takes_the_template(tmp_path: Path) -> None:
     assert (int(launch["grid"]), int(launch["block"])) == (k["grid"][0], k["block"][0])
     assert note(ptx, "simt") == {"m": "512", "n": "512", "k": "512", "bm": "32", "bn": "64",
                                  "bk": "64", "stages": "2", "owners": "128"}
-    assert ptx.count("fma.rn.f32") == 16 * 64  # 16 accumulators, 64 k per stage
-    assert ptx.count("ld.shared.v4.f32") == 8 * 16  # 8 per 4 k
+    # 16 accumulators in 8 pairs, 64 k per stage; per 4 k, 4 loads of A and 4 of B
+    assert ptx.count("fma.rn.f32x2") == 8 * 64 and ptx.count("fma.rn.f32 ") == 0
+    assert ptx.count("ld.shared.v4.f32") == ptx.count("ld.shared.v2.b64") == 4 * 16
     info = ptxas_info(ptx, tmp_path)
     assert "0 bytes spill stores" in info
     for flag in ("no_unroll", "no_fusion", "no_cse"):
