@@ -183,3 +183,92 @@ def test_name_written_twice_is_not_merged() -> None:
             Loop(A, (load("v"), acc("s1", "v"), acc("s2", "v"))),
             Loop(A, (load("v"), acc("s2", "v"))), out("s1", "s2"))
     assert accums(merge_equal(body)) == ["s1", "s2", "s2"]
+
+
+# --- random loops ----------------------------------------------------------------------------
+
+FUZZ_THREADS, FUZZ_TRIPS = 64, 6
+
+
+def random_nest(seed: int):
+    """A Tile of 64 threads, each running a seeded loop of 6 trips: three loads, then a random
+    mix of assignments, accumulations (add, maximum, minimum, multiply; some with a base) and
+    repeats of earlier ones under new names, reading loaded values, temporaries and accumulator
+    states before and after their updates. After the loop every accumulator is written out (a
+    loop body's temporaries are not visible after it)."""
+    import random
+
+    from ptxgen.ir import Tile
+    from ptxgen.problems import _arg, _spec, add, mul
+
+    rng = random.Random(seed)
+    a0, k = Var("a0"), Var("k")
+    loop: list = [Load(("xv",), "x", (add(mul(a0, Literal(FUZZ_TRIPS)), k),), F32),
+                  Load(("yv",), "y", (add(mul(a0, Literal(FUZZ_TRIPS)), k),), F32),
+                  Load(("wv",), "w", (k,), F32)]
+    values, accs, temps = ["xv", "yv", "wv"], [], []
+    for n in range(rng.randint(8, 18)):
+        roll = rng.random()
+        if roll < 0.3 and (temps or accs):
+            old = rng.choice([s for s in loop if isinstance(s, Assign | Accum)])
+            if isinstance(old, Assign):  # a repeat of an earlier assignment
+                loop.append(replace(old, name=f"t{n}"))
+                temps.append(f"t{n}")
+            else:  # a twin of an earlier accumulator
+                loop.append(replace(old, name=f"s{n}"))
+                accs.append(f"s{n}")
+        elif roll < 0.65:
+            op = rng.choice(["add", "multiply", "maximum", "subtract", "minimum"])
+            args = (rng.choice(values + temps + accs), rng.choice(values + temps + accs))
+            loop.append(Assign(f"t{n}", ElementwiseImpl(op), args, F32))
+            temps.append(f"t{n}")
+        else:
+            op = rng.choice(["add", "add", "maximum", "minimum", "multiply"])
+            base = rng.choice(values + temps) if op == "add" and rng.random() < 0.3 else None
+            loop.append(Accum(f"s{n}", rng.choice(values + temps), ElementwiseImpl(op), F32,
+                              ("k",), base))
+            accs.append(f"s{n}")
+    if not accs:
+        loop.append(Accum("s_end", "xv", ElementwiseImpl("add"), F32, ("k",), None))
+        accs.append("s_end")
+    outs = accs
+    body = (Loop(Axis("k", Dim(FUZZ_TRIPS)), tuple(loop)),
+            *(Write("out", (add(mul(a0, Literal(len(outs))), Literal(i)),), (name,), F32)
+              for i, name in enumerate(outs)))
+    tile = Tile((Axis("a0", Dim(FUZZ_THREADS)),), body, None)
+    dist = ["uniform", -1.0, 1.0]
+    n = FUZZ_THREADS * FUZZ_TRIPS
+    args = [_arg("x", "f32", [n], seed=0, dist=dist), _arg("y", "f32", [n], seed=1, dist=dist),
+            _arg("w", "f32", [FUZZ_TRIPS], seed=2, dist=dist),
+            _arg("out", "f32", [FUZZ_THREADS * len(outs)], output=True)]
+    return _spec(f"fuzz{seed}", "random loop", 0, 0, f"k_fuzz{seed}", tile, args,
+                 ["x", "y", "w"], ["out"], {}, FUZZ_THREADS)
+
+
+def test_random_loops_merge_bit_equal() -> None:
+    """On 80 random loops the oracle's output is the same bit for bit after the pass, and the
+    pass merges something in most of them."""
+    merged_any = 0
+    for seed in range(80):
+        spec = random_nest(seed)
+        want, got, body, merged = oracle_both(spec.graph, spec.meta)
+        assert np.array_equal(want["out"].view(np.uint8), got["out"].view(np.uint8)), seed
+        merged_any += merged != tuple(body)
+    assert merged_any >= 40, merged_any
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("flag", ["default", "no_unroll"])
+def test_random_loops_on_the_gpu(cuda, flag: str) -> None:
+    """24 random loops through the whole compiler (merge, lowering, ptxas) on the GPU, each
+    against the oracle's run of the original IR, bit for bit: the arithmetic is IEEE-rn adds,
+    multiplies (fused into fmas as the oracle models), maxima and minima."""
+    from conftest import gpu_run, oracle_run
+
+    for seed in range(24):
+        spec = random_nest(seed)
+        ins = reference_inputs(spec.meta)
+        flags = {} if flag == "default" else {flag: True}
+        got = gpu_run(spec.graph, spec.meta, ins, guard=16, **flags)["out"]
+        want = oracle_run(spec.graph, spec.meta, ins)["out"]
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), seed
