@@ -68,9 +68,20 @@ def test_shipped_attention_merges_bit_equal(name: str) -> None:
     assert [n for n in after if n.startswith("acc5__")] == outs
 
 
+# the two largest attention cases take tens of seconds in the oracle; they are the same nest as
+# the shipped a01 at other sizes, so for them only the merge itself is checked here (the GPU
+# suite checks their results against the oracle under every flag set)
+LARGE = ("a01_256", "a06_long_kv")
+
+
 @pytest.mark.parametrize("name", sorted(n for n in SUITE if n.startswith("a0")))
 def test_suite_attention_merges_bit_equal(name: str) -> None:
     case = SUITE[name]()
+    if name in LARGE:
+        for op in Graph.from_dict(case.spec.graph).kernel_ops():
+            body = jam(op.body.body)
+            assert len(accums(merge_equal(body))) < len(accums(body))
+        return
     want, got, body, merged = oracle_both(case.spec.graph, case.spec.meta)
     assert len(accums(merged)) < len(accums(body))
     for k in want:
