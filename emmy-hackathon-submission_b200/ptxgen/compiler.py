@@ -33,16 +33,22 @@ def compile_module(op: KernelOp, buffers: Mapping[str, Buffer], arg_order: Seque
             return ptx
     # sibling loops over one axis, trip by trip (``jam``); with unrolling off the jammed loop is
     # still a runtime loop with one body per trip. Then accumulators that hold equal values on
-    # every trip become one (``congruence``), with common subexpression elimination.
+    # every trip become one (``congruence``), with common subexpression elimination. In the
+    # default build, work a loop repeats across one thread axis is done once and shared
+    # (``hoist``).
     from dataclasses import replace
 
     from .congruence import merge_equal
+    from .hoist import share_invariant
     from .jam import jam
 
     stmts = jam(op.body.body)
     if not no_cse:
         stmts = merge_equal(stmts)
-    op = replace(op, body=replace(op.body, body=stmts))
+    tile = replace(op.body, body=stmts)
+    if templates and exchange is None:
+        tile = share_invariant(tile, block_threads)
+    op = replace(op, body=tile)
     k = Lowering(op, buffers, arg_order, block_threads, no_unroll=no_unroll,
                  no_fusion=no_fusion, no_cse=no_cse, exchange=exchange).run()
     return k.render()

@@ -313,11 +313,16 @@ class Interpreter:
     """Runs one KernelOp over given input arrays; ``run`` returns the output buffers."""
 
     def __init__(self, graph: Graph | dict[str, Any], meta: dict[str, Any],
-                 inputs: dict[str, np.ndarray], options: Options | None = None):
+                 inputs: dict[str, np.ndarray], options: Options | None = None,
+                 op: Any = None):
+        """``op``: run this KernelOp in place of the graph's (a rewritten body of the same
+        kernel, as a compiler pass produces it), with its own shared buffers."""
         from ptxgen.compiler import kernel_for_meta
 
         graph = graph if isinstance(graph, Graph) else Graph.from_dict(graph)
         self.op, self.launch = kernel_for_meta(graph, meta)
+        if op is not None:
+            self.op = op
         self.opts = options or Options()
         self.block = int(self.launch["block"][0])
         self.grid = int(self.launch["grid"][0])
