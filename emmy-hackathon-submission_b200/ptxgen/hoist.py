@@ -26,8 +26,9 @@ its operands and its order.
 
 On the shipped a01 each thread then computes 4 rows x 4 keys of scores in place of 4 rows x 64
 keys. The rewrite applies to whole blocks only (the barrier needs every thread), to f32 values,
-and where the shared array fits ``MAX_BYTES``. It is a template-level change, so a compiler flag
-turns it off.
+and where the kernel's shared buffers, the new array included, stay under the static limit
+(``lower.STATIC_SMEM_CAP``), so no launch needs dynamic shared memory for it. It is a
+template-level change, so a compiler flag turns it off.
 """
 
 from __future__ import annotations
@@ -38,8 +39,8 @@ from dataclasses import replace
 
 from .ir import (Accum, Assign, BinaryExpr, Literal, Load, Loop, Smem, Stmt, StridedLoop, Sync,
                  Tile, Var, Write, dt, walk)
+from .lower import STATIC_SMEM_CAP, pack_shared
 
-MAX_BYTES = 64 << 10  # shared memory one rewrite may take
 F32 = dt("f32")
 _PLAIN = (Load, Assign, Accum)
 
@@ -53,14 +54,15 @@ def share_invariant(tile: Tile, block: int) -> Tile:
     if not threads:
         return tile
     body = list(tile.body)
-    used = sum(math.prod(int(e) for e in s.extents) * 4 for s in walk(body)
-               if isinstance(s, Smem))
+    # the kernel's shared buffers stay static arrays, so a launcher that passes only meta.json's
+    # dynamic shared memory still runs it
+    _, used = pack_shared(list({s.name: s for s in walk(body) if isinstance(s, Smem)}.values()))
     out: list[Stmt] = []
     changed = False
     for j, st in enumerate(body):
         split = None
         if isinstance(st, Loop) and st.axis.extent.is_static:
-            split = _split(st, threads, body[:j], f"_shared{j}", MAX_BYTES - used)
+            split = _split(st, threads, body[:j], f"_shared{j}", STATIC_SMEM_CAP - used - 16)
         if split is None:
             out.append(st)
             continue
