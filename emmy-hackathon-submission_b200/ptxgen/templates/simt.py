@@ -46,7 +46,7 @@ TILE = 4  # rows and columns of C a compute thread owns
 # 256 with 2 17.7-17.9; the generic nest 15.5-15.7
 BK_CHOICES = (64, 32, 16, 8, 4)
 STAGES = 2
-SMEM_LIMIT = 232448
+STATIC_LIMIT = 48 << 10  # a ring this size or smaller is a static array: no launch setting needed
 
 
 @dataclass(frozen=True)
@@ -85,6 +85,11 @@ class SimtPlan:
     def stage_bytes(self) -> int:
         return (self.bm + self.bn) * self.bk * 4
 
+    @property
+    def static(self) -> bool:
+        """The ring fits a static shared array (else it is meta.json's dynamic shared memory)."""
+        return self.stages * self.stage_bytes <= STATIC_LIMIT
+
 
 def match(op: KernelOp, buffers: Mapping[str, Buffer], arg_order: Sequence[str], block: int,
           smem_bytes: int) -> SimtPlan | None:
@@ -105,8 +110,11 @@ def match(op: KernelOp, buffers: Mapping[str, Buffer], arg_order: Sequence[str],
         return None
     if g.k % 4 or g.n % 4:
         return None
+    # the ring is a static array, or the dynamic shared memory meta.json already gives the
+    # nest, so a launcher that runs the IR's launch as it stands runs this kernel too
+    room = max(STATIC_LIMIT, smem_bytes)
     for bk in BK_CHOICES:
-        if g.k % bk == 0 and STAGES * (bm + bn) * bk * 4 <= SMEM_LIMIT:
+        if g.k % bk == 0 and STAGES * (bm + bn) * bk * 4 <= room:
             break
     else:
         return None
@@ -139,7 +147,7 @@ def emit(p: SimtPlan) -> str:
     emit_("mov.u32 %cta, %ctaid.x;")
     emit_(f"div.u32 %mt, %cta, {p.n // p.bn};")
     emit_(f"rem.u32 %nt, %cta, {p.n // p.bn};")
-    emit_("mov.u32 %sbase, smem_pool;")
+    emit_(f"mov.u32 %sbase, {'smem_ring' if p.static else 'smem_pool'};")
     # this thread's copies: chunk c = tid + j * threads, row c / (row chunks), 16 bytes at
     # column (c % row chunks) * 4; global pointers at stage 0, shared offsets within a stage
     copies = []
@@ -295,12 +303,13 @@ def emit(p: SimtPlan) -> str:
     head = [
         "//\n// Generated by ptxgen (B200 backend): register-blocked f32 GEMM template\n//",
         f"// @ptxgen launch grid={p.grid} block={p.block}",
-        f"// @ptxgen dynamic_smem={smem}",
+        *([] if p.static else [f"// @ptxgen dynamic_smem={smem}"]),
         f"// @ptxgen simt m={p.m} n={p.n} k={p.k} bm={p.bm} bn={p.bn} bk={p.bk} "
         f"stages={p.stages} owners={p.owners}",
         "",
         f".version {PTX_VERSION}\n.target {TARGET}\n.address_size 64\n",
-        ".extern .shared .align 16 .b8 smem_pool[];",
+        (f".shared .align 16 .b8 smem_ring[{smem}];" if p.static else
+         ".extern .shared .align 16 .b8 smem_pool[];"),
         "",
         f".visible .entry {e}(\n{params}\n)\n.maxntid {p.block}, 1, 1\n.minnctapersm 1\n{{",
         *decls,

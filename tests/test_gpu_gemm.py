@@ -148,7 +148,7 @@ def simt_cases() -> dict[str, tuple[dict, dict]]:
 
 
 @pytest.mark.parametrize("key", ["m01_shipped", "one_k_step", "rect", "tile_32x32",
-                                 "tile_64x64"])
+                                 "tile_64x64", "tile_64x128"])
 def test_simt_gemm_bit_equal(cuda, key: str) -> None:
     """The register-blocked f32 template against the generic lowering of the same nest and
     against the oracle, bit for bit: every element of C is the same fma chain over k in order.

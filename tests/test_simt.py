@@ -19,13 +19,16 @@ from ptxgen.suite import SUITE
 
 SHIPPED = Path(__file__).parent / "golden" / "shipped" / "m01_matmul_512"
 
-# nests in the shipped m01's form (each thread 2 x 2 or 4 x 2 of C) at other shapes: ragged
-# tile counts, one K step (fewer steps than the ring has stages), 64 x 64 and 32 x 32 tiles
+# nests in the shipped m01's form (each thread 2 x 2, 4 x 2 or 2 x 4 of C) at other shapes:
+# ragged tile counts, one K step (fewer steps than the ring has stages), 64 x 64, 32 x 32 and
+# 64 x 128 tiles
 CASES = {
     "rect": dict(m=96, n=192, k=192, bm=32, bn=64, bk=64, stages=3, block=512),
     "one_k_step": dict(m=64, n=64, k=32, bm=32, bn=32, bk=32, stages=3, block=256),
     "tile_64x64": dict(m=128, n=128, k=256, bm=64, bn=64, bk=32, stages=3, block=512),
     "tile_32x32": dict(m=64, n=64, k=96, bm=32, bn=32, bk=32, stages=3, block=256),
+    # 1024 threads, 512 owners, a 96 KiB ring in the nest's own dynamic shared memory
+    "tile_64x128": dict(m=128, n=256, k=256, bm=64, bn=128, bk=64, stages=3, block=1024),
 }
 
 
@@ -99,3 +102,22 @@ def test_threads_that_own_16_outputs_keep_the_generic_nest() -> None:
         if spec.meta["kernels"][0]["args"][0]["dtype"] != "f32":
             continue
         assert "@ptxgen simt" not in to_ptx(Graph.from_dict(spec.graph), spec.meta), name
+
+
+@pytest.mark.parametrize("key", ["shipped", *sorted(CASES)])
+def test_ring_needs_nothing_meta_does_not_give(key: str) -> None:
+    """The copy ring is a static array when it fits 48 KiB, else no larger than the dynamic
+    shared memory meta.json gives the nest: a launcher that runs the IR's launch as it stands
+    (grid, block, smem_bytes) runs the template too."""
+    if key == "shipped":
+        graph, meta = shipped()
+    else:
+        spec = case(key)
+        graph, meta = spec.graph, spec.meta
+    ptx = to_ptx(Graph.from_dict(graph), meta)
+    assert "@ptxgen simt" in ptx
+    dyn = re.search(r"^// @ptxgen dynamic_smem=(\d+)$", ptx, re.M)
+    if dyn is None:
+        assert ".shared .align 16 .b8 smem_ring[" in ptx
+    else:
+        assert int(dyn.group(1)) <= int(meta["kernels"][0]["smem_bytes"])
