@@ -452,12 +452,23 @@ def measure_kernel(plan: Any, steps: int, warmup: int, world: int, l2: str = "cl
                                                 .view(-1, out.shape[1]))
 
     align = torch.zeros(1, dtype=torch.float32, device="cuda")
+    # where the path's collective is over peer memory, the ranks realign over peer memory too:
+    # a one-warp exchange kernel releases every rank within NVLink latency of the last one to
+    # arrive, where ranks leave a one-element NCCL all-reduce microseconds apart, and a rank that
+    # starts its step early is charged the others' lag by the step's own exchange
+    aligner = None
+    if collective and via in ("fused", "peer") and plan.allreduce:
+        from ptxgen.peer import PeerSum
+
+        aligner = PeerSum()
 
     def realign() -> None:
         """Ranks leave one step's collective together; the L2 flush before the next (not part
-        of the workload) takes each rank a different time, so a one-element all-reduce after it,
+        of the workload) takes each rank a different time, so a one-element exchange after it,
         outside the step's events, lines them up again as the previous collective would."""
-        if collective:
+        if aligner is not None:
+            aligner(align.data_ptr(), stream=stream.cuda_stream)
+        elif collective:
             import torch.distributed as tdist
 
             tdist.all_reduce(align)
@@ -501,6 +512,8 @@ def measure_kernel(plan: Any, steps: int, warmup: int, world: int, l2: str = "cl
         raise RuntimeError(f"kernel status word 0x{status:08x}")
     if peer is not None:
         peer.check()
+    if aligner is not None:
+        aligner.check()
     out = {"mean_ms": max_over_ranks(mean_ms, world),
            "median_ms": max_over_ranks(statistics.median(times), world),
            "min_ms": max_over_ranks(min(times), world),
@@ -510,7 +523,7 @@ def measure_kernel(plan: Any, steps: int, warmup: int, world: int, l2: str = "cl
                                         for n in prob.launch_entry.get("zero_outputs", []))),
            "clocks": sampler.summary(),
            "tensors": {**tensors, **{f"{n}@rows": t for n, t in rows_out.items()}},
-           "prob": prob, "peer": peer, "slots": slots}
+           "prob": prob, "peer": peer, "slots": slots, "aligner": aligner}
     return out
 
 
@@ -865,6 +878,8 @@ def run_ours(args: argparse.Namespace) -> None:
                 m["peer"].check()
             tdist.barrier()
             (m["peer"] or m["slots"]).close()
+            if m["aligner"] is not None:
+                m["aligner"].close()
         del m
         torch.cuda.empty_cache()
         return res
