@@ -20,8 +20,8 @@ from oracle.interp import Interpreter
 from ptxgen.compiler import kernel_for_meta, to_ptx
 from ptxgen.congruence import merge_equal
 from ptxgen.hoist import share_invariant
-from ptxgen.ir import (Accum, Assign, Axis, BinaryExpr, Dim, ElementwiseImpl, Graph, Let, Literal,
-                       Load, Loop, Smem, StridedLoop, Sync, Tile, Var, Write, dt)
+from ptxgen.ir import (Accum, Assign, Axis, BinaryExpr, Dim, ElementwiseImpl, Graph, Let, Load,
+                       Loop, Smem, StridedLoop, Sync, Tile, Var, Write, dt)
 from ptxgen.jam import jam
 from ptxgen.suite import SUITE
 
