@@ -36,6 +36,7 @@ from .ir import (Accum, Assign, BinaryExpr, CastExpr, Cond, CpAsyncCommit, CpAsy
                  WarpShuffle, Write, walk)
 from .ops import Val
 from .pipeline import Pipe
+from .stage import Stage
 from .ptx import BUFFER_ALIGN, SM_COUNT, Ins, Kernel, pow2_part
 
 UNROLL_BUDGET = 6144  # instructions a loop may fully unroll to
@@ -111,6 +112,7 @@ class Lowering:
         self.env: dict[str, Value] = {}
         self.mem: dict[str, Memory] = {}
         self.loop_depth = 0
+        self._converged = False  # every thread of the block is running this code together
         self._order = {id(st): i for i, st in enumerate(walk([op.body]))}
         self._stmts = list(walk([op.body]))
 
@@ -256,7 +258,11 @@ class Lowering:
             raise NotImplementedError("Tile: a partial last block around a barrier")
         with (k.skip_if(beyond) if guarded else nullcontext()), self._block():
             self.env.update(self._decode(t, cell, _raster_pair(t)))
+            # every thread of a block runs the Tile body together (no tail guard), until a
+            # condition splits them; the staging pass needs whole warps
+            self._converged = not guarded
             self.body(t.body)
+            self._converged = False
         if self.exchange is not None:  # every thread reaches it, past the tail guard
             from .templates.exchange import emit_epilogue
 
@@ -704,11 +710,14 @@ class Lowering:
         if isinstance(p, bool):
             with self._block():
                 self.body(s.body if p else s.else_body)
-        elif not s.else_body:
+            return
+        converged, self._converged = self._converged, False
+        if not s.else_body:
             with self._where(p), self._block():
                 self.body(s.body)
         else:
             self._if_else(p, s.body, s.else_body)
+        self._converged = converged
 
     def _if_else(self, p: str, then: Sequence[Stmt], otherwise: Sequence[Stmt]) -> None:
         k = self.k
@@ -875,6 +884,7 @@ class Lowering:
             k.emit("bra", src=(done,), pred=f"!{enters}", barrier=True)
         with k.loop(entered=enters is True, counter=self._iv_counter(s, i), step=n * f) as mark:
             k.place(top)
+            top_label = k.body[-1]
             for reg in written:
                 k.forget(reg)
             for j in range(f):
@@ -888,7 +898,28 @@ class Lowering:
         k.emit("add.u32", (i,), (i, str(n * f)))
         k.emit("setp.lt.s32", (again,), (i, bound_op))
         k.emit("bra", src=(top,), pred=again, barrier=True)
+        rows = self._warp_rows(start, enters, mark)
+        if rows:
+            pre = Ins(text="")  # where the preheader ends, for the staging pass
+            k.body.insert(mark.at, pre)
+            k.markers.append(pre)
+            k.stages.append(Stage(pre, top_label, k.body[-1], rows))
         k.place(done)
+
+    def _warp_rows(self, start: Aff, enters: Any, mark: Any) -> dict[str, int]:
+        """The induction pointers of a counted loop through which each warp reads one contiguous
+        row of 4-byte elements per load, with their per-trip steps; empty unless every thread of
+        the block runs every trip together. A pointer qualifies when the loop starts at ``tid``
+        plus block-uniform terms that keep a warp's first element 32-element aligned, and the
+        pointer steps the counter with coefficient 1 over 4-byte elements and nothing else."""
+        k = self.k
+        if not self._converged or enters is not True or k._loops or self.block % 32:
+            return {}
+        if start.terms.get(self.tid) != 1 or start.const % 32:
+            return {}
+        if any(r != self.tid and (r != self.ctaid or c % 32) for r, c in start.terms.items()):
+            return {}
+        return {p: d for p, d in mark.incs if k.iv_meta.get(p) == (1, 4, ())}
 
     def _runtime_loop(self, s: Loop | StridedLoop, start: Aff, step: Aff, end: Aff,
                       written: list[str]) -> None:

@@ -131,6 +131,9 @@ class Kernel:
         self.reqntid: int | None = None
         self.min_ctas: int | None = None
         self.pipes: list = []  # runtime loops whose loads the pipeline pass issues ahead
+        self.stages: list = []  # counted loops whose warp rows the staging pass fetches wide
+        # induction pointer -> (counter coefficient, element bytes, other index terms)
+        self.iv_meta: dict[str, tuple[int, int, tuple]] = {}
         self.markers: list[Ins] = []  # placeholder lines the render drops
         self._counts: dict[str, int] = {}
         self._labels = 0
@@ -328,6 +331,7 @@ class Kernel:
         self.align[p] = align
         loop.ivs[key] = p
         loop.incs.append((p, coef * loop.step * esz))
+        self.iv_meta[p] = (coef, esz, tuple(sorted(rest.items())))
         return p
 
     @contextmanager
@@ -364,11 +368,13 @@ class Kernel:
         from .slp import SLP
 
         from .pipeline import pipeline_loads
+        from .stage import stage_loads
 
         self.drop_dead()
         self.vectorize()
         self.drop_dead()
         pipeline_loads(self, self.pipes)
+        stage_loads(self, self.stages)
         drop = {id(m) for m in self.markers}
         self.body = [ins for ins in self.body if id(ins) not in drop]
         if not self.no_cse:  # pairing reuses values across copies, as CSE does

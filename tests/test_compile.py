@@ -168,8 +168,14 @@ def test_no_unroll_makes_runtime_loops() -> None:
 
 
 def test_sum_unrolls_grid_stride_loop() -> None:
+    """Config 4's counted loop runs 16 copies of its body a trip. The trip's 16 rows of 128
+    bytes a warp come in as 8 8-byte loads a lane, go through a warp-private shared area, and
+    each lane adds its own 16 elements in their order (``stage.py``)."""
     ptx = compile_spec(problems.CONFIGS["c4_full_sum"]())
-    assert ptx.count("ld.global.nc.f32") >= 16
+    loop = ptx[ptx.index("$L_loop_1:"):ptx.index("$L_loop_end_2:")]
+    assert loop.count("ld.global.nc.v2.f32") == 8 and loop.count("st.shared.v2.f32") == 8
+    assert loop.count("ld.shared.f32") == 16 and loop.count("bar.warp.sync") == 2
+    assert "ld.global.nc.f32" not in loop
     assert "red.global.add.f32" in ptx
     # no immediate offset beyond 2^30 bytes
     offs = [int(m) for m in re.findall(r"\[%rd\d+\+(\d+)\]", ptx)]

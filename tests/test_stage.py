@@ -1,0 +1,77 @@
+"""Warp rows fetched 8 bytes a lane through shared memory (``ptxgen.stage``).
+
+A per-thread grid-stride sum (each thread writes its own sum, so the result does not depend on
+any atomic order) takes the rewrite with whole blocks and keeps its scalar loads with a partial
+last block. On the GPU the staged sums must equal the oracle's bit for bit.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+from conftest import reference_inputs
+
+from ptxgen import problems
+from ptxgen.compiler import to_ptx
+from ptxgen.ir import (Accum, Axis, Dim, ElementwiseImpl, Graph, Load, StridedLoop, Tile, Var,
+                       Write, dt)
+
+F32 = dt("f32")
+
+
+def per_thread_sum(threads: int, n: int, block: int) -> problems.ProblemSpec:
+    """out[t] = x[t] + x[t + threads] + ... over n elements, in that order, one thread per t."""
+    from ptxgen.problems import _arg, _spec
+
+    t = Var("a0")
+    loop = StridedLoop(Axis("i", Dim(n)), t, threads,
+                       (Load(("xv",), "x", (Var("i"),), F32),
+                        Accum("acc", "xv", ElementwiseImpl("add"), F32, ("i",), None)),
+                       False, None, True)
+    tile = Tile((Axis("a0", Dim(threads)),), (loop, Write("out", (t,), ("acc",), F32)), None)
+    args = [_arg("x", "f32", [n], seed=0, dist=["uniform", 0.0, 1.0]),
+            _arg("out", "f32", [threads], output=True)]
+    return _spec("stage_sum", "per-thread grid-stride sums", 0, 0, "k_stage_sum", tile, args,
+                 ["x"], ["out"], {}, block)
+
+
+def loop_of(ptx: str) -> str:
+    return ptx[ptx.index("$L_loop_1:"):ptx.index("$L_loop_end_2:")]
+
+
+def test_whole_blocks_are_staged() -> None:
+    spec = per_thread_sum(1024, 1024 * 4096, 256)
+    loop = loop_of(to_ptx(Graph.from_dict(spec.graph), spec.meta))
+    assert loop.count("bar.warp.sync") == 2 and "ld.global.nc.v2.f32" in loop
+    assert "ld.global.nc.f32" not in loop
+
+
+def test_partial_last_block_keeps_scalar_loads() -> None:
+    """1000 threads in blocks of 256: the last block's threads past 1000 skip the body, so a
+    warp sync there would wait on lanes that never come."""
+    spec = per_thread_sum(1000, 1000 * 4096, 256)
+    ptx = to_ptx(Graph.from_dict(spec.graph), spec.meta)
+    assert "bar.warp.sync" not in ptx and "ld.global.nc.f32" in ptx
+
+
+def test_flags_keep_it_where_they_keep_the_loop() -> None:
+    """The rewrite changes no value, so, like the copy ring, it stays under the flags that keep
+    the counted loop (with CSE off every address is recomputed and there is no pointer)."""
+    spec = per_thread_sum(1024, 1024 * 4096, 256)
+    g = Graph.from_dict(spec.graph)
+    assert "bar.warp.sync" in to_ptx(g, spec.meta, no_fusion=True)
+    assert "bar.warp.sync" not in to_ptx(g, spec.meta, no_cse=True)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("threads,block", [(1024, 256), (2048, 512), (256, 256)])
+def test_staged_sums_equal_the_oracle(cuda, threads: int, block: int) -> None:
+    from conftest import gpu_run, oracle_run
+
+    spec = per_thread_sum(threads, threads * 4096, block)
+    ptx = to_ptx(Graph.from_dict(spec.graph), spec.meta)
+    assert "bar.warp.sync" in ptx
+    ins = reference_inputs(spec.meta)
+    got = gpu_run(spec.graph, spec.meta, ins, guard=16, ptx=ptx)["out"]
+    want = oracle_run(spec.graph, spec.meta, ins)["out"]
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
