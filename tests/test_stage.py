@@ -1,8 +1,9 @@
 """Warp rows fetched 8 bytes a lane through shared memory (``ptxgen.stage``).
 
 A per-thread grid-stride sum (each thread writes its own sum, so the result does not depend on
-any atomic order) takes the rewrite with whole blocks and keeps its scalar loads with a partial
-last block. On the GPU the staged sums must equal the oracle's bit for bit.
+any atomic order) over a grid of several waves takes the rewrite with whole blocks, and keeps its
+scalar loads with a partial last block or in a grid of one wave. On the GPU the staged sums must
+equal the oracle's bit for bit.
 """
 
 from __future__ import annotations
@@ -39,36 +40,48 @@ def loop_of(ptx: str) -> str:
     return ptx[ptx.index("$L_loop_1:"):ptx.index("$L_loop_end_2:")]
 
 
+WAVES = 160 * 256  # 160 blocks of 256 threads: more blocks than the B200's 148 SMs
+
+
 def test_whole_blocks_are_staged() -> None:
-    spec = per_thread_sum(1024, 1024 * 4096, 256)
+    spec = per_thread_sum(WAVES, WAVES * 64, 256)
     loop = loop_of(to_ptx(Graph.from_dict(spec.graph), spec.meta))
     assert loop.count("bar.warp.sync") == 2 and "ld.global.nc.v2.f32" in loop
     assert "ld.global.nc.f32" not in loop
 
 
 def test_partial_last_block_keeps_scalar_loads() -> None:
-    """1000 threads in blocks of 256: the last block's threads past 1000 skip the body, so a
-    warp sync there would wait on lanes that never come."""
-    spec = per_thread_sum(1000, 1000 * 4096, 256)
+    """A grid 100 threads short of whole blocks of 256: the last block's threads past the end
+    skip the body, so a warp sync there would wait on lanes that never come."""
+    spec = per_thread_sum(WAVES - 100, (WAVES - 100) * 64, 256)
     ptx = to_ptx(Graph.from_dict(spec.graph), spec.meta)
     assert "bar.warp.sync" not in ptx and "ld.global.nc.f32" in ptx
+
+
+def test_one_wave_keeps_its_unroll() -> None:
+    """4 blocks: an SM holds too few warps to cover a staged trip's round of loads, stores and
+    syncs (the shipped r02, one block, took 26.7 us staged against 14.3 unrolled)."""
+    spec = per_thread_sum(1024, 1024 * 4096, 256)
+    ptx = to_ptx(Graph.from_dict(spec.graph), spec.meta)
+    assert "bar.warp.sync" not in ptx
 
 
 def test_flags_keep_it_where_they_keep_the_loop() -> None:
     """The rewrite changes no value, so, like the copy ring, it stays under the flags that keep
     the counted loop (with CSE off every address is recomputed and there is no pointer)."""
-    spec = per_thread_sum(1024, 1024 * 4096, 256)
+    spec = per_thread_sum(WAVES, WAVES * 64, 256)
     g = Graph.from_dict(spec.graph)
     assert "bar.warp.sync" in to_ptx(g, spec.meta, no_fusion=True)
     assert "bar.warp.sync" not in to_ptx(g, spec.meta, no_cse=True)
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("threads,block", [(1024, 256), (2048, 512), (256, 256)])
-def test_staged_sums_equal_the_oracle(cuda, threads: int, block: int) -> None:
+@pytest.mark.parametrize("threads,block,trips", [(WAVES, 256, 64), (150 * 512, 512, 40),
+                                                (WAVES, 256, 4096 // 32)])
+def test_staged_sums_equal_the_oracle(cuda, threads: int, block: int, trips: int) -> None:
     from conftest import gpu_run, oracle_run
 
-    spec = per_thread_sum(threads, threads * 4096, block)
+    spec = per_thread_sum(threads, threads * trips, block)
     ptx = to_ptx(Graph.from_dict(spec.graph), spec.meta)
     assert "bar.warp.sync" in ptx
     ins = reference_inputs(spec.meta)
