@@ -88,3 +88,23 @@ def test_staged_sums_equal_the_oracle(cuda, threads: int, block: int, trips: int
     got = gpu_run(spec.graph, spec.meta, ins, guard=16, ptx=ptx)["out"]
     want = oracle_run(spec.graph, spec.meta, ins)["out"]
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_strided_rows_keep_scalar_loads() -> None:
+    """A loop over every other element: a warp's lanes read 4 bytes out of each 8, not one
+    contiguous row, so nothing is staged."""
+    from ptxgen.ir import BinaryExpr, Literal
+    from ptxgen.problems import _arg, _spec
+
+    t, threads = Var("a0"), WAVES
+    n = threads * 64
+    loop = StridedLoop(Axis("i", Dim(n)), t, threads,
+                       (Load(("xv",), "x", (BinaryExpr("*", Var("i"), Literal(2)),), F32),
+                        Accum("acc", "xv", ElementwiseImpl("add"), F32, ("i",), None)),
+                       False, None, True)
+    tile = Tile((Axis("a0", Dim(threads)),), (loop, Write("out", (t,), ("acc",), F32)), None)
+    args = [_arg("x", "f32", [2 * n], seed=0, dist=["uniform", 0.0, 1.0]),
+            _arg("out", "f32", [threads], output=True)]
+    spec = _spec("stage_strided", "every other element", 0, 0, "k_stage_strided", tile, args,
+                 ["x"], ["out"], {}, 256)
+    assert "bar.warp.sync" not in to_ptx(Graph.from_dict(spec.graph), spec.meta)
